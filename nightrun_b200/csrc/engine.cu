@@ -1,0 +1,980 @@
+// nrcuda engine: .nrm parsing and upload, synthetic models, the inference
+// context (crates/nr-model/src/infer.rs InferCtx) and the C ABI of
+// include/nrcuda.h.
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "nrcuda.h"
+#include "ops.cuh"
+#include "synth.cuh"
+
+using namespace nrc;
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_err;
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+#define CU(call)                                                                          \
+  do {                                                                                    \
+    cudaError_t e_ = (call);                                                              \
+    if (e_ != cudaSuccess) return fail(NRC_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+int nrc_fail_api(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+extern "C" const char* nrc_last_error(void) { return g_err.c_str(); }
+extern "C" int nrc_version(void) { return 100; }
+
+// ---------------------------------------------------- CRC-32 (crc32.rs:6-79)
+namespace {
+struct Crc {
+  uint32_t t[8][256];
+  Crc() {
+    for (uint32_t i = 0; i < 256; i++) {
+      uint32_t c = i;
+      for (int k = 0; k < 8; k++) c = (c & 1) ? (0xEDB88320u ^ (c >> 1)) : (c >> 1);
+      t[0][i] = c;
+    }
+    for (int s = 1; s < 8; s++)
+      for (int i = 0; i < 256; i++) t[s][i] = t[0][t[s - 1][i] & 0xff] ^ (t[s - 1][i] >> 8);
+  }
+  uint32_t update(uint32_t c, const uint8_t* w, size_t n) const {
+    size_t i = 0;
+    for (; i + 8 <= n; i += 8) {
+      const uint32_t lo = ((uint32_t)w[i] | ((uint32_t)w[i + 1] << 8) | ((uint32_t)w[i + 2] << 16) |
+                           ((uint32_t)w[i + 3] << 24)) ^ c;
+      c = t[7][lo & 0xff] ^ t[6][(lo >> 8) & 0xff] ^ t[5][(lo >> 16) & 0xff] ^ t[4][lo >> 24] ^ t[3][w[i + 4]] ^
+          t[2][w[i + 5]] ^ t[1][w[i + 6]] ^ t[0][w[i + 7]];
+    }
+    for (; i < n; i++) c = t[0][(c ^ w[i]) & 0xff] ^ (c >> 8);
+    return c;
+  }
+};
+const Crc& crc_tables() {
+  static Crc c;
+  return c;
+}
+uint32_t crc32_host(const uint8_t* d, size_t n) { return crc_tables().update(0xffffffffu, d, n) ^ 0xffffffffu; }
+
+// ------------------------------------------------------ .nrm format (format.rs)
+constexpr size_t HEADER_SIZE = 192, NAME_LEN = 48, ENTRY_SIZE = 32, DATA_ALIGN = 64;
+constexpr uint32_t FLAG_TIED = 1;
+enum { TK_TOK_EMBED = 1, TK_OUTPUT_NORM = 2, TK_OUTPUT = 3, TK_ROPE_FREQS = 4, TK_ATTN_NORM = 10, TK_ATTN_Q = 11,
+       TK_ATTN_K = 12, TK_ATTN_V = 13, TK_ATTN_O = 14, TK_FFN_NORM = 15, TK_FFN_GATE = 16, TK_FFN_UP = 17,
+       TK_FFN_DOWN = 18, TK_ATTN_Q_NORM = 19, TK_ATTN_K_NORM = 20 };
+enum { DT_F32 = 0, DT_Q8_0 = 1, DT_Q4K = 2, DT_Q6K = 3 };
+
+struct Entry {
+  uint16_t kind, layer, dtype;
+  uint64_t offset, size;
+  uint32_t rows, cols;
+};
+
+// TensorDtype::byte_size (format.rs:104-124), checked.
+bool byte_size(int dtype, uint64_t n, uint64_t* out) {
+  uint64_t b, per;
+  switch (dtype) {
+    case DT_F32: return !__builtin_mul_overflow(n, (uint64_t)4, out);
+    case DT_Q8_0: if (n % 32) return false; b = n / 32; per = 34; break;
+    case DT_Q4K: if (n % 256) return false; b = n / 256; per = 144; break;
+    case DT_Q6K: if (n % 256) return false; b = n / 256; per = 210; break;
+    default: return false;
+  }
+  return !__builtin_mul_overflow(b, per, out);
+}
+
+template <typename T>
+T rd(const uint8_t* p) {
+  T v;
+  memcpy(&v, p, sizeof(T));
+  return v;
+}
+template <typename T>
+void wr(uint8_t* p, T v) {
+  memcpy(p, &v, sizeof(T));
+}
+
+int dtype_fmt(int dt) { return dt == DT_Q8_0 ? FMT_Q8_0 : (dt == DT_Q4K ? FMT_Q4K : FMT_Q6K); }
+}  // namespace
+
+struct nrc_model {
+  int device = 0;
+  nrc_meta meta{};
+  std::vector<Entry> entries;
+  std::vector<uint8_t> prefix;  // header | tokenizer | table | padding  (bytes [0, data_off))
+  uint8_t* d_data = nullptr;
+  uint64_t data_size = 0;
+  bool crc_known = false;
+  uint32_t data_crc = 0;
+
+  const Entry* find(int kind, int layer) const {
+    for (const auto& e : entries)
+      if (e.kind == kind && e.layer == layer) return &e;
+    return nullptr;
+  }
+  bool has(int kind) const {
+    for (const auto& e : entries)
+      if (e.kind == kind) return true;
+    return false;
+  }
+};
+
+// Model::parse (format.rs:260-406).
+static int parse_nrm(const uint8_t* blob, size_t len, nrc_model* m, uint64_t* data_off_out) {
+  if (len < HEADER_SIZE) return fail(NRC_ERR_TOO_SHORT, "blob shorter than the 192-byte header");
+  if (memcmp(blob, "NRUN", 4) != 0) return fail(NRC_ERR_BAD_MAGIC, "bad magic");
+  const uint32_t version = rd<uint32_t>(blob + 4);
+  if (version != 3) return fail(NRC_ERR_BAD_VERSION, "unsupported version %u", version);
+  nrc_meta& mt = m->meta;
+  mt.arch = (int32_t)rd<uint32_t>(blob + 8);
+  if (mt.arch < 1 || mt.arch > 3) return fail(NRC_ERR_BAD_TABLE, "unknown arch %d", mt.arch);
+  uint32_t* dims[8] = {&mt.dim, &mt.n_layers, &mt.n_heads, &mt.n_kv_heads, &mt.head_dim, &mt.ffn_dim, &mt.vocab,
+                       &mt.ctx_train};
+  for (int i = 0; i < 8; i++) *dims[i] = rd<uint32_t>(blob + 12 + 4 * i);
+  float* rp[6] = {&mt.rope_theta, &mt.norm_eps, &mt.rope_factor, &mt.rope_low, &mt.rope_high, &mt.rope_orig_ctx};
+  for (int i = 0; i < 6; i++) *rp[i] = rd<float>(blob + 44 + 4 * i);
+  mt.flags = rd<uint32_t>(blob + 68);
+  mt.embed_scale = rd<float>(blob + 72);
+  mt.attn_scale = rd<float>(blob + 76);
+  mt.residual_scale = rd<float>(blob + 80);
+  mt.logit_scale = rd<float>(blob + 84);
+  memcpy(mt.name, blob + 88, NAME_LEN);
+  const uint64_t tok_off = rd<uint64_t>(blob + 136), tok_size = rd<uint64_t>(blob + 144);
+  const uint64_t table_off = rd<uint64_t>(blob + 152);
+  const uint64_t count = rd<uint32_t>(blob + 160);
+  const uint64_t data_off = rd<uint64_t>(blob + 168), data_size = rd<uint64_t>(blob + 176);
+  const uint32_t data_crc = rd<uint32_t>(blob + 184), meta_crc = rd<uint32_t>(blob + 188);
+  if (!isfinite(mt.embed_scale) || !isfinite(mt.attn_scale) || mt.attn_scale < 0.0f ||
+      !isfinite(mt.residual_scale) || mt.residual_scale <= 0.0f || !isfinite(mt.logit_scale) ||
+      mt.logit_scale <= 0.0f)
+    return fail(NRC_ERR_BAD_TABLE, "nonsensical muP scalars");
+  uint64_t table_len, table_end, data_end, tok_end;
+  if (__builtin_mul_overflow(count, (uint64_t)ENTRY_SIZE, &table_len)) return fail(NRC_ERR_BAD_TABLE, "table size overflow");
+  if (__builtin_add_overflow(table_off, table_len, &table_end) || __builtin_add_overflow(data_off, data_size, &data_end) ||
+      __builtin_add_overflow(tok_off, tok_size, &tok_end))
+    return fail(NRC_ERR_TOO_SHORT, "region bounds overflow");
+  if (len < table_end || len < data_end || len < tok_end) return fail(NRC_ERR_TOO_SHORT, "region past end of blob");
+  const Crc& C = crc_tables();
+  uint32_t c = 0xffffffffu;
+  c = C.update(c, blob, HEADER_SIZE - 8);
+  const uint8_t zeros[8] = {0};
+  c = C.update(c, zeros, 8);
+  c = C.update(c, blob + tok_off, tok_size);
+  c = C.update(c, blob + table_off, table_len);
+  if ((c ^ 0xffffffffu) != meta_crc) return fail(NRC_ERR_META_CRC, "meta crc mismatch");
+  m->entries.clear();
+  for (uint64_t i = 0; i < count; i++) {
+    const uint8_t* e = blob + table_off + i * ENTRY_SIZE;
+    Entry t;
+    t.kind = rd<uint16_t>(e);
+    t.layer = rd<uint16_t>(e + 2);
+    t.dtype = rd<uint16_t>(e + 4);
+    if (t.dtype > 3) return fail(NRC_ERR_BAD_TABLE, "bad dtype");
+    t.offset = rd<uint64_t>(e + 8);
+    t.size = rd<uint64_t>(e + 16);
+    t.rows = rd<uint32_t>(e + 24);
+    t.cols = rd<uint32_t>(e + 28);
+    uint64_t end, bs;
+    if (__builtin_add_overflow(t.offset, t.size, &end) || end > data_size)
+      return fail(NRC_ERR_BAD_TABLE, "tensor outside the data section");
+    if (t.offset % DATA_ALIGN) return fail(NRC_ERR_BAD_TABLE, "misaligned tensor offset");
+    const uint64_t n = (uint64_t)t.rows * (uint64_t)t.cols;
+    if (!byte_size(t.dtype, n, &bs) || bs != t.size) return fail(NRC_ERR_BAD_TABLE, "size/dtype mismatch");
+    m->entries.push_back(t);
+  }
+  m->data_size = data_size;
+  m->data_crc = data_crc;
+  m->crc_known = true;
+  *data_off_out = data_off;
+  return NRC_OK;
+}
+
+extern "C" int nrc_model_load(const uint8_t* blob, size_t len, int device, int verify_crc, nrc_model** out) {
+  if (!blob || !out) return fail(NRC_ERR_INVALID, "null argument");
+  *out = nullptr;
+  nrc_model* m = new nrc_model();
+  uint64_t data_off = 0;
+  int rc = parse_nrm(blob, len, m, &data_off);
+  if (rc) {
+    delete m;
+    return rc;
+  }
+  if (verify_crc && crc32_host(blob + data_off, m->data_size) != m->data_crc) {
+    delete m;
+    return fail(NRC_ERR_DATA_CRC, "data crc mismatch");
+  }
+  m->device = device;
+  m->prefix.assign(blob, blob + data_off);
+  if (cudaSetDevice(device) != cudaSuccess) {
+    delete m;
+    return fail(NRC_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  }
+  // +256: slack so no kernel ever needs to read past the allocation.
+  if (cudaMalloc(&m->d_data, m->data_size + 256) != cudaSuccess) {
+    delete m;
+    return fail(NRC_ERR_ALLOC, "cannot allocate %llu bytes of weights", (unsigned long long)m->data_size);
+  }
+  if (cudaMemcpy(m->d_data, blob + data_off, m->data_size, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(m->d_data);
+    delete m;
+    return fail(NRC_ERR_CUDA, "weight upload failed");
+  }
+  *out = m;
+  return NRC_OK;
+}
+
+// Tensor list of a synthetic model, in the order tools/nrconvert writes them
+// (tools/nrconvert/src/main.rs:231-277), 64-byte aligned.
+static void synth_entries(const nrc_synth_cfg& c, std::vector<Entry>& out) {
+  out.clear();
+  const uint32_t att = c.n_heads * c.head_dim, kv = c.n_kv_heads * c.head_dim;
+  const bool mix = c.quant == 1;
+  auto lin = [&](uint16_t kind, uint16_t layer, uint32_t rows, uint32_t cols, bool q6) {
+    out.push_back({kind, layer, (uint16_t)(mix ? (q6 ? DT_Q6K : DT_Q4K) : DT_Q8_0), 0, 0, rows, cols});
+  };
+  auto f32 = [&](uint16_t kind, uint16_t layer, uint32_t n) { out.push_back({kind, layer, DT_F32, 0, 0, 1, n}); };
+  lin(TK_TOK_EMBED, 0, c.vocab, c.dim, true);
+  if (c.rope_freqs_tensor) f32(TK_ROPE_FREQS, 0, c.head_dim / 2);
+  for (uint32_t l = 0; l < c.n_layers; l++) {
+    const bool even = (l % 2) == 0;
+    const uint16_t L = (uint16_t)l;
+    f32(TK_ATTN_NORM, L, c.dim);
+    if (c.arch == 2) {
+      f32(TK_ATTN_Q_NORM, L, c.head_dim);
+      f32(TK_ATTN_K_NORM, L, c.head_dim);
+    }
+    lin(TK_ATTN_Q, L, att, c.dim, false);
+    lin(TK_ATTN_K, L, kv, c.dim, false);
+    lin(TK_ATTN_V, L, kv, c.dim, even);
+    lin(TK_ATTN_O, L, c.dim, att, false);
+    f32(TK_FFN_NORM, L, c.dim);
+    lin(TK_FFN_GATE, L, c.ffn_dim, c.dim, false);
+    lin(TK_FFN_UP, L, c.ffn_dim, c.dim, false);
+    lin(TK_FFN_DOWN, L, c.dim, c.ffn_dim, even);
+  }
+  f32(TK_OUTPUT_NORM, 0, c.dim);
+  if (!c.tied) lin(TK_OUTPUT, 0, c.vocab, c.dim, true);
+  uint64_t cur = 0;
+  for (auto& e : out) {
+    cur = (cur + DATA_ALIGN - 1) / DATA_ALIGN * DATA_ALIGN;
+    e.offset = cur;
+    uint64_t bs = 0;
+    byte_size(e.dtype, (uint64_t)e.rows * e.cols, &bs);
+    e.size = bs;
+    cur += bs;
+  }
+}
+
+extern "C" int nrc_model_synth(const nrc_synth_cfg* cfg, uint64_t seed, int device, nrc_model** out) {
+  if (!cfg || !out) return fail(NRC_ERR_INVALID, "null argument");
+  *out = nullptr;
+  const nrc_synth_cfg& c = *cfg;
+  if (c.arch < 1 || c.arch > 3 || !c.dim || !c.n_layers || !c.n_heads || !c.n_kv_heads || !c.head_dim ||
+      c.n_heads % c.n_kv_heads)
+    return fail(NRC_ERR_INVALID, "bad synthetic config");
+  nrc_model* m = new nrc_model();
+  m->device = device;
+  synth_entries(c, m->entries);
+  m->data_size = m->entries.empty() ? 0 : m->entries.back().offset + m->entries.back().size;
+  const uint64_t table_off = HEADER_SIZE, table_len = m->entries.size() * ENTRY_SIZE;
+  const uint64_t data_off = (table_off + table_len + DATA_ALIGN - 1) / DATA_ALIGN * DATA_ALIGN;
+  std::vector<uint8_t>& p = m->prefix;
+  p.assign(data_off, 0);
+  memcpy(p.data(), "NRUN", 4);
+  wr<uint32_t>(&p[4], 3);
+  wr<uint32_t>(&p[8], c.arch);
+  const uint32_t dims[8] = {c.dim, c.n_layers, c.n_heads, c.n_kv_heads, c.head_dim, c.ffn_dim, c.vocab, c.ctx_train};
+  for (int i = 0; i < 8; i++) wr<uint32_t>(&p[12 + 4 * i], dims[i]);
+  const float rp[6] = {c.rope_theta, c.norm_eps, c.rope_factor, c.rope_low, c.rope_high, c.rope_orig_ctx};
+  for (int i = 0; i < 6; i++) wr<float>(&p[44 + 4 * i], rp[i]);
+  wr<uint32_t>(&p[68], c.tied ? FLAG_TIED : 0);
+  wr<float>(&p[72], c.embed_scale);
+  wr<float>(&p[76], c.attn_scale);
+  wr<float>(&p[80], c.residual_scale);
+  wr<float>(&p[84], c.logit_scale);
+  memcpy(&p[88], c.name, NAME_LEN);
+  wr<uint64_t>(&p[136], HEADER_SIZE);
+  wr<uint64_t>(&p[144], 0);
+  wr<uint64_t>(&p[152], table_off);
+  wr<uint32_t>(&p[160], (uint32_t)m->entries.size());
+  wr<uint64_t>(&p[168], data_off);
+  wr<uint64_t>(&p[176], m->data_size);
+  for (size_t i = 0; i < m->entries.size(); i++) {
+    uint8_t* e = &p[table_off + i * ENTRY_SIZE];
+    const Entry& t = m->entries[i];
+    wr<uint16_t>(e, t.kind);
+    wr<uint16_t>(e + 2, t.layer);
+    wr<uint16_t>(e + 4, t.dtype);
+    wr<uint64_t>(e + 8, t.offset);
+    wr<uint64_t>(e + 16, t.size);
+    wr<uint32_t>(e + 24, t.rows);
+    wr<uint32_t>(e + 28, t.cols);
+  }
+  const Crc& C = crc_tables();
+  uint32_t mc = 0xffffffffu;
+  mc = C.update(mc, p.data(), HEADER_SIZE - 8);
+  const uint8_t zeros[8] = {0};
+  mc = C.update(mc, zeros, 8);
+  mc = C.update(mc, p.data() + table_off, table_len);
+  wr<uint32_t>(&p[188], mc ^ 0xffffffffu);
+  m->meta.arch = (int32_t)c.arch;
+  m->meta.dim = c.dim;
+  m->meta.n_layers = c.n_layers;
+  m->meta.n_heads = c.n_heads;
+  m->meta.n_kv_heads = c.n_kv_heads;
+  m->meta.head_dim = c.head_dim;
+  m->meta.ffn_dim = c.ffn_dim;
+  m->meta.vocab = c.vocab;
+  m->meta.ctx_train = c.ctx_train;
+  m->meta.rope_theta = c.rope_theta;
+  m->meta.norm_eps = c.norm_eps;
+  m->meta.rope_factor = c.rope_factor;
+  m->meta.rope_low = c.rope_low;
+  m->meta.rope_high = c.rope_high;
+  m->meta.rope_orig_ctx = c.rope_orig_ctx;
+  m->meta.flags = c.tied ? FLAG_TIED : 0;
+  m->meta.embed_scale = c.embed_scale;
+  m->meta.attn_scale = c.attn_scale;
+  m->meta.residual_scale = c.residual_scale;
+  m->meta.logit_scale = c.logit_scale;
+  memcpy(m->meta.name, c.name, NAME_LEN);
+  if (cudaSetDevice(device) != cudaSuccess) {
+    delete m;
+    return fail(NRC_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+  }
+  if (cudaMalloc(&m->d_data, m->data_size + 256) != cudaSuccess) {
+    delete m;
+    return fail(NRC_ERR_ALLOC, "cannot allocate %llu bytes of weights", (unsigned long long)m->data_size);
+  }
+  cudaMemset(m->d_data, 0, m->data_size + 256);
+  for (const auto& e : m->entries) {
+    cudaError_t err = synth_fill(m->d_data + e.offset, e.dtype, e.kind, e.rows, e.cols,
+                                 synth_tensor_key(seed, e.kind, e.layer), 0);
+    if (err != cudaSuccess) {
+      cudaFree(m->d_data);
+      delete m;
+      return fail(NRC_ERR_CUDA, "synthetic fill failed: %s", cudaGetErrorString(err));
+    }
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(m->d_data);
+    delete m;
+    return fail(NRC_ERR_CUDA, "synthetic fill failed");
+  }
+  *out = m;
+  return NRC_OK;
+}
+
+extern "C" int nrc_model_meta(const nrc_model* m, nrc_meta* out) {
+  if (!m || !out) return fail(NRC_ERR_INVALID, "null argument");
+  *out = m->meta;
+  return NRC_OK;
+}
+
+extern "C" size_t nrc_model_nrm_size(const nrc_model* m) { return m ? m->prefix.size() + m->data_size : 0; }
+
+static int ensure_crc(nrc_model* m, const uint8_t* host_data) {
+  if (m->crc_known) return NRC_OK;
+  std::vector<uint8_t> tmp;
+  if (!host_data) {
+    tmp.resize(m->data_size);
+    CU(cudaSetDevice(m->device));
+    CU(cudaMemcpy(tmp.data(), m->d_data, m->data_size, cudaMemcpyDeviceToHost));
+    host_data = tmp.data();
+  }
+  m->data_crc = crc32_host(host_data, m->data_size);
+  m->crc_known = true;
+  wr<uint32_t>(&m->prefix[184], m->data_crc);
+  return NRC_OK;
+}
+
+extern "C" int nrc_model_export(const nrc_model* mc, uint8_t* out, size_t cap) {
+  nrc_model* m = const_cast<nrc_model*>(mc);
+  if (!m || !out) return fail(NRC_ERR_INVALID, "null argument");
+  if (cap < m->prefix.size() + m->data_size) return fail(NRC_ERR_INVALID, "export buffer too small");
+  CU(cudaSetDevice(m->device));
+  CU(cudaMemcpy(out + m->prefix.size(), m->d_data, m->data_size, cudaMemcpyDeviceToHost));
+  int rc = ensure_crc(m, out + m->prefix.size());
+  if (rc) return rc;
+  memcpy(out, m->prefix.data(), m->prefix.size());
+  return NRC_OK;
+}
+
+extern "C" int nrc_model_data_crc(const nrc_model* mc, uint32_t* out) {
+  nrc_model* m = const_cast<nrc_model*>(mc);
+  if (!m || !out) return fail(NRC_ERR_INVALID, "null argument");
+  // Recomputed from the device copy (checks what the kernels will read).
+  std::vector<uint8_t> tmp(m->data_size);
+  CU(cudaSetDevice(m->device));
+  CU(cudaMemcpy(tmp.data(), m->d_data, m->data_size, cudaMemcpyDeviceToHost));
+  *out = crc32_host(tmp.data(), m->data_size);
+  return NRC_OK;
+}
+
+extern "C" int nrc_model_free(nrc_model* m) {
+  if (!m) return NRC_OK;
+  cudaSetDevice(m->device);
+  if (m->d_data) cudaFree(m->d_data);
+  delete m;
+  return NRC_OK;
+}
+
+// ------------------------------------------------------------ inference context
+namespace {
+struct LayerW {
+  const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+  int fq, fk, fv, fo, fg, fu, fd;
+  const float *attn_norm, *ffn_norm, *q_norm, *k_norm;
+};
+
+// Device-resident step state (positions and tokens are read by the kernels
+// so one captured graph serves every decode step).
+struct Status {
+  uint32_t pos;
+  uint32_t next;
+  uint32_t err;
+  uint32_t pad;
+  unsigned long long key;
+  uint32_t tok[NRC_MAX_BATCH];
+};
+
+struct Layout {
+  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, partial, counters, status, hist, total;
+};
+
+size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
+
+Layout layout_for(const nrc_meta& mt, size_t ctx) {
+  Layout L{};
+  const size_t dim = mt.dim, att = (size_t)mt.n_heads * mt.head_dim, kv = (size_t)mt.n_kv_heads * mt.head_dim;
+  const size_t B = NRC_MAX_BATCH;
+  const size_t splits = (ctx + ATTN_SPLIT - 1) / ATTN_SPLIT;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t r = o;
+    o = al(o + bytes);
+    return r;
+  };
+  L.kc = take((size_t)mt.n_layers * ctx * kv * 2);
+  L.vc = take((size_t)mt.n_layers * ctx * kv * 2);
+  L.x = take(B * dim * 4);
+  L.q = take(B * att * 4);
+  L.k = take(B * kv * 4);
+  L.v = take(B * kv * 4);
+  L.att = take(B * att * 4);
+  L.g = take(B * mt.ffn_dim * 4);
+  L.u = take(B * mt.ffn_dim * 4);
+  L.logits = take((size_t)mt.vocab * 4);
+  L.cos_t = take(ctx * (mt.head_dim / 2) * 4);
+  L.sin_t = take(ctx * (mt.head_dim / 2) * 4);
+  L.partial = take(B * mt.n_heads * splits * (mt.head_dim + 2) * 4);
+  L.counters = take(B * mt.n_kv_heads * 4);
+  L.status = take(sizeof(Status));
+  L.hist = take((ctx + 1) * 4);
+  L.total = o;
+  return L;
+}
+
+// rope::rope_freqs (crates/nr-tensor/src/rope.rs:14-34) with glibc powf.
+void host_rope_freqs(float* out, size_t head_dim, float theta, bool scaled, float factor, float low, float high,
+                     float orig) {
+  const size_t half = head_dim / 2;
+  const float PI = 3.14159265358979323846f;
+  for (size_t i = 0; i < half; i++) {
+    volatile float exponent = -2.0f * (float)i / (float)head_dim;
+    float freq = powf(theta, exponent);
+    if (scaled) {
+      const float wavelen = 2.0f * PI / freq;
+      const float low_wavelen = orig / low;
+      const float high_wavelen = orig / high;
+      if (wavelen > low_wavelen) {
+        freq /= factor;
+      } else if (wavelen > high_wavelen) {
+        volatile float smooth = (orig / wavelen - low) / (high - low);
+        volatile float a = (1.0f - smooth) * freq;
+        volatile float b = a / factor;
+        volatile float c2 = smooth * freq;
+        freq = b + c2;
+      }
+    }
+    out[i] = freq;
+  }
+}
+}  // namespace
+
+struct nrc_ctx {
+  const nrc_model* m = nullptr;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  size_t ctx = 0;
+  int dim, att_dim, n_layers, n_heads, n_kv, hd, kv_dim, ffn, vocab;
+  int style;
+  float eps, embed_scale, att_scale, rs, logit_recip;
+  std::vector<LayerW> L;
+  const uint8_t* embed;
+  int f_embed;
+  const uint8_t* out_w;
+  int f_out;
+  const float* out_norm;
+  uint8_t* arena = nullptr;
+  Layout lay;
+  uint16_t *kc, *vc;
+  float *x, *q, *k, *v, *att, *g, *u, *logits, *cos_t, *sin_t, *partial;
+  unsigned* counters;
+  Status* st;
+  uint32_t* hist;
+  uint32_t* h_stage = nullptr;  // pinned host staging: tokens in, status out
+  size_t pos = 0;
+  size_t pending = 0;  // decode steps enqueued by nrc_ctx_decode_async, not yet synced
+  cudaGraphExec_t gexec = nullptr;
+  bool pdl = true;
+};
+
+extern "C" int nrc_ctx_required_bytes(const nrc_model* m, size_t ctx, size_t* out) {
+  if (!m || !out) return fail(NRC_ERR_INVALID, "null argument");
+  *out = layout_for(m->meta, ctx).total;
+  return NRC_OK;
+}
+
+// InferCtx::new (infer.rs:352-492): shape-checked binding of every tensor.
+extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
+  if (!m || !out) return fail(NRC_ERR_INVALID, "null argument");
+  if (ctx == 0) return fail(NRC_ERR_INVALID, "ctx must be > 0");
+  *out = nullptr;
+  const nrc_meta& mt = m->meta;
+  if (mt.head_dim % 32 || mt.head_dim > 128 || mt.n_kv_heads == 0 || mt.n_heads % mt.n_kv_heads ||
+      mt.n_heads / mt.n_kv_heads > 8)
+    return fail(NRC_ERR_INVALID, "unsupported attention shape (head_dim %u, heads %u/%u)", mt.head_dim, mt.n_heads,
+                mt.n_kv_heads);
+  nrc_ctx* c = new nrc_ctx();
+  c->m = m;
+  c->device = m->device;
+  c->ctx = ctx;
+  c->dim = mt.dim;
+  c->att_dim = mt.n_heads * mt.head_dim;
+  c->n_layers = mt.n_layers;
+  c->n_heads = mt.n_heads;
+  c->n_kv = mt.n_kv_heads;
+  c->hd = mt.head_dim;
+  c->kv_dim = mt.n_kv_heads * mt.head_dim;
+  c->ffn = mt.ffn_dim;
+  c->vocab = mt.vocab;
+  std::unique_ptr<nrc_ctx> guard(c);
+  const uint8_t* base = m->d_data;
+  auto mat = [&](int kind, int layer, uint32_t rows, uint32_t cols, const uint8_t** p, int* fmt) -> int {
+    const Entry* e = m->find(kind, layer);
+    if (!e) return fail(NRC_ERR_MISSING, "missing tensor kind %d layer %d", kind, layer);
+    if (e->rows != rows || e->cols != cols) return fail(NRC_ERR_MISSING, "bad matrix shape (kind %d layer %d)", kind, layer);
+    if (e->dtype == DT_F32) return fail(NRC_ERR_BAD_TABLE, "f32 matrix (kind %d)", kind);
+    *p = base + e->offset;
+    *fmt = dtype_fmt(e->dtype);
+    return NRC_OK;
+  };
+  auto f32t = [&](int kind, int layer, uint32_t n, const float** p) -> int {
+    const Entry* e = m->find(kind, layer);
+    if (!e) return fail(NRC_ERR_MISSING, "missing tensor kind %d layer %d", kind, layer);
+    if (e->dtype != DT_F32 || (uint64_t)e->rows * e->cols != n) return fail(NRC_ERR_MISSING, "bad f32 tensor shape");
+    *p = reinterpret_cast<const float*>(base + e->offset);
+    return NRC_OK;
+  };
+  int rc;
+  if ((rc = mat(TK_TOK_EMBED, 0, mt.vocab, mt.dim, &c->embed, &c->f_embed))) return rc;
+  const bool qwen = mt.arch == 2;
+  if (!qwen && m->has(TK_ATTN_Q_NORM)) return fail(NRC_ERR_MISSING, "unexpected attn_q_norm for this arch");
+  c->L.resize(mt.n_layers);
+  for (uint32_t l = 0; l < mt.n_layers; l++) {
+    LayerW& w = c->L[l];
+    if ((rc = f32t(TK_ATTN_NORM, l, mt.dim, &w.attn_norm))) return rc;
+    w.q_norm = w.k_norm = nullptr;
+    if (qwen) {
+      if ((rc = f32t(TK_ATTN_Q_NORM, l, mt.head_dim, &w.q_norm))) return rc;
+      if ((rc = f32t(TK_ATTN_K_NORM, l, mt.head_dim, &w.k_norm))) return rc;
+    }
+    if ((rc = mat(TK_ATTN_Q, l, c->att_dim, mt.dim, &w.wq, &w.fq))) return rc;
+    if ((rc = mat(TK_ATTN_K, l, c->kv_dim, mt.dim, &w.wk, &w.fk))) return rc;
+    if ((rc = mat(TK_ATTN_V, l, c->kv_dim, mt.dim, &w.wv, &w.fv))) return rc;
+    if ((rc = mat(TK_ATTN_O, l, mt.dim, c->att_dim, &w.wo, &w.fo))) return rc;
+    if ((rc = f32t(TK_FFN_NORM, l, mt.dim, &w.ffn_norm))) return rc;
+    if ((rc = mat(TK_FFN_GATE, l, mt.ffn_dim, mt.dim, &w.wg, &w.fg))) return rc;
+    if ((rc = mat(TK_FFN_UP, l, mt.ffn_dim, mt.dim, &w.wu, &w.fu))) return rc;
+    if ((rc = mat(TK_FFN_DOWN, l, mt.dim, mt.ffn_dim, &w.wd, &w.fd))) return rc;
+  }
+  if ((rc = f32t(TK_OUTPUT_NORM, 0, mt.dim, &c->out_norm))) return rc;
+  if (mt.flags & FLAG_TIED) {
+    c->out_w = c->embed;
+    c->f_out = c->f_embed;
+  } else if ((rc = mat(TK_OUTPUT, 0, mt.vocab, mt.dim, &c->out_w, &c->f_out))) {
+    return rc;
+  }
+  c->style = qwen ? 1 : 0;
+  c->eps = mt.norm_eps;
+  c->embed_scale = mt.embed_scale;
+  c->att_scale = mt.attn_scale != 0.0f ? mt.attn_scale : 1.0f / sqrtf((float)mt.head_dim);
+  c->rs = mt.residual_scale;
+  c->logit_recip = 1.0f / mt.logit_scale;
+
+  CU(cudaSetDevice(c->device));
+  c->lay = layout_for(mt, ctx);
+  if (cudaMalloc(&c->arena, c->lay.total) != cudaSuccess)
+    return fail(NRC_ERR_ALLOC, "inference arena exhausted (%llu bytes)", (unsigned long long)c->lay.total);
+  CU(cudaMemset(c->arena, 0, c->lay.total));
+  uint8_t* A = c->arena;
+  c->kc = reinterpret_cast<uint16_t*>(A + c->lay.kc);
+  c->vc = reinterpret_cast<uint16_t*>(A + c->lay.vc);
+  c->x = reinterpret_cast<float*>(A + c->lay.x);
+  c->q = reinterpret_cast<float*>(A + c->lay.q);
+  c->k = reinterpret_cast<float*>(A + c->lay.k);
+  c->v = reinterpret_cast<float*>(A + c->lay.v);
+  c->att = reinterpret_cast<float*>(A + c->lay.att);
+  c->g = reinterpret_cast<float*>(A + c->lay.g);
+  c->u = reinterpret_cast<float*>(A + c->lay.u);
+  c->logits = reinterpret_cast<float*>(A + c->lay.logits);
+  c->cos_t = reinterpret_cast<float*>(A + c->lay.cos_t);
+  c->sin_t = reinterpret_cast<float*>(A + c->lay.sin_t);
+  c->partial = reinterpret_cast<float*>(A + c->lay.partial);
+  c->counters = reinterpret_cast<unsigned*>(A + c->lay.counters);
+  c->st = reinterpret_cast<Status*>(A + c->lay.status);
+  c->hist = reinterpret_cast<uint32_t*>(A + c->lay.hist);
+
+  // RoPE tables (infer.rs:427-445; rope.rs:49-65): cos/sin of pos * freq.
+  const size_t half = mt.head_dim / 2;
+  std::vector<float> freqs(half);
+  if (m->has(TK_ROPE_FREQS)) {
+    host_rope_freqs(freqs.data(), mt.head_dim, mt.rope_theta, false, 0, 0, 0, 0);
+    const Entry* e = m->find(TK_ROPE_FREQS, 0);
+    std::vector<float> fac((size_t)e->rows * e->cols);
+    CU(cudaMemcpy(fac.data(), base + e->offset, fac.size() * 4, cudaMemcpyDeviceToHost));
+    for (size_t i = 0; i < half && i < fac.size(); i++) freqs[i] /= fac[i];
+  } else {
+    host_rope_freqs(freqs.data(), mt.head_dim, mt.rope_theta, mt.rope_factor > 0.0f, mt.rope_factor, mt.rope_low,
+                    mt.rope_high, mt.rope_orig_ctx);
+  }
+  std::vector<float> ct(ctx * half), stab(ctx * half);
+  for (size_t p = 0; p < ctx; p++)
+    for (size_t i = 0; i < half; i++) {
+      volatile float angle = (float)p * freqs[i];
+      float s, co;
+      sincosf(angle, &s, &co);
+      ct[p * half + i] = co;
+      stab[p * half + i] = s;
+    }
+  CU(cudaMemcpy(c->cos_t, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice));
+  CU(cudaMemcpy(c->sin_t, stab.data(), stab.size() * 4, cudaMemcpyHostToDevice));
+  CU(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  CU(cudaMallocHost(&c->h_stage, 4096));
+  *out = guard.release();
+  return NRC_OK;
+}
+
+extern "C" int nrc_ctx_free(nrc_ctx* c) {
+  if (!c) return NRC_OK;
+  cudaSetDevice(c->device);
+  if (c->stream) cudaStreamSynchronize(c->stream);
+  if (c->gexec) cudaGraphExecDestroy(c->gexec);
+  if (c->stream) cudaStreamDestroy(c->stream);
+  if (c->h_stage) cudaFreeHost(c->h_stage);
+  if (c->arena) cudaFree(c->arena);
+  delete c;
+  return NRC_OK;
+}
+
+namespace {
+// One GEMV over up to 64 tokens (groups of 8 per launch).
+cudaError_t gemv_tokens(GemvArgs a, int nt, int x_ld_f, cudaStream_t s, bool pdl) {
+  for (int t0 = 0; t0 < nt; t0 += 8) {
+    GemvArgs b = a;
+    b.nt = nt - t0 < 8 ? nt - t0 : 8;
+    if (b.xf) b.xf = a.xf + (size_t)t0 * x_ld_f;
+    for (int i = 0; i < b.nseg; i++)
+      if (b.seg[i].y) b.seg[i].y = a.seg[i].y + (size_t)t0 * a.seg[i].ld;
+    if (b.resid) b.resid = a.resid + (size_t)t0 * a.resid_ld;
+    cudaError_t e = gemv_run(b, s, pdl);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+GemvArgs gemv_base(nrc_ctx* c, int fmt, int K) {
+  GemvArgs a{};
+  a.fmt = fmt;
+  a.K = K;
+  a.scale = 1.0f;
+  a.err = &c->st->err;
+  a.eps = c->eps;
+  return a;
+}
+
+// Enqueue one forward step over nt tokens at positions st->pos .. +nt-1
+// (infer.rs:510-595 for nt == 1, infer.rs:601-750 otherwise).
+cudaError_t enqueue_step(nrc_ctx* c, int nt) {
+  cudaStream_t s = c->stream;
+  const bool pdl = c->pdl;
+  cudaError_t e;
+  EmbedArgs ea{c->embed, c->f_embed, c->dim, c->embed_scale, c->st->tok, nt, c->x, &c->st->key};
+  if ((e = embed_run(ea, s, pdl))) return e;
+  for (int l = 0; l < c->n_layers; l++) {
+    const LayerW& w = c->L[l];
+    // QKV: one launch per weight format (rmsnorm + quantize in the prologue).
+    {
+      const uint8_t* ws[3] = {w.wq, w.wk, w.wv};
+      const int fs[3] = {w.fq, w.fk, w.fv};
+      float* ys[3] = {c->q, c->k, c->v};
+      const int rows[3] = {c->att_dim, c->kv_dim, c->kv_dim};
+      bool done[3] = {false, false, false};
+      for (int i = 0; i < 3; i++) {
+        if (done[i]) continue;
+        GemvArgs a = gemv_base(c, fs[i], c->dim);
+        a.xf = c->x;
+        a.xf_ld = c->dim;
+        a.norm_w = w.attn_norm;
+        a.epi = EPI_STORE;
+        for (int j = i; j < 3; j++)
+          if (!done[j] && fs[j] == fs[i]) {
+            a.seg[a.nseg++] = GemvSegArg{ws[j], ys[j], rows[j], rows[j]};
+            done[j] = true;
+          }
+        if ((e = gemv_tokens(a, nt, c->dim, s, pdl))) return e;
+      }
+    }
+    RopeArgs ra{c->q, c->k, c->v, w.q_norm, w.k_norm, c->eps, c->cos_t, c->sin_t, c->style,
+                c->kc + (size_t)l * c->ctx * c->kv_dim, c->vc + (size_t)l * c->ctx * c->kv_dim,
+                nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
+    if ((e = rope_append_run(ra, s, pdl))) return e;
+    AttnArgs aa{c->q, c->att, c->kc + (size_t)l * c->ctx * c->kv_dim, c->vc + (size_t)l * c->ctx * c->kv_dim,
+                c->partial, c->counters, c->att_scale, nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
+    if ((e = attention_run(aa, s, pdl))) return e;
+    {
+      GemvArgs a = gemv_base(c, w.fo, c->att_dim);
+      a.xf = c->att;
+      a.xf_ld = c->att_dim;
+      a.seg[0] = GemvSegArg{w.wo, nullptr, c->dim, c->dim};
+      a.nseg = 1;
+      a.epi = EPI_RESID;
+      a.resid = c->x;
+      a.resid_ld = c->dim;
+      a.rs = c->rs;
+      if ((e = gemv_tokens(a, nt, c->att_dim, s, pdl))) return e;
+    }
+    if (w.fg == w.fu) {
+      GemvArgs a = gemv_base(c, w.fg, c->dim);
+      a.xf = c->x;
+      a.xf_ld = c->dim;
+      a.norm_w = w.ffn_norm;
+      a.seg[0] = GemvSegArg{w.wg, c->g, c->ffn, c->ffn};
+      a.seg[1] = GemvSegArg{w.wu, nullptr, c->ffn, c->ffn};
+      a.nseg = 2;
+      a.pair = 1;
+      a.epi = EPI_SWIGLU;
+      if ((e = gemv_tokens(a, nt, c->dim, s, pdl))) return e;
+    } else {
+      GemvArgs a = gemv_base(c, w.fg, c->dim);
+      a.xf = c->x;
+      a.xf_ld = c->dim;
+      a.norm_w = w.ffn_norm;
+      a.seg[0] = GemvSegArg{w.wg, c->g, c->ffn, c->ffn};
+      a.nseg = 1;
+      a.epi = EPI_STORE;
+      if ((e = gemv_tokens(a, nt, c->dim, s, pdl))) return e;
+      a.fmt = w.fu;
+      a.seg[0] = GemvSegArg{w.wu, c->u, c->ffn, c->ffn};
+      if ((e = gemv_tokens(a, nt, c->dim, s, pdl))) return e;
+      if ((e = op_swiglu(c->g, c->u, (size_t)nt * c->ffn, s))) return e;
+    }
+    {
+      GemvArgs a = gemv_base(c, w.fd, c->ffn);
+      a.xf = c->g;
+      a.xf_ld = c->ffn;
+      a.seg[0] = GemvSegArg{w.wd, nullptr, c->dim, c->dim};
+      a.nseg = 1;
+      a.epi = EPI_RESID;
+      a.resid = c->x;
+      a.resid_ld = c->dim;
+      a.rs = c->rs;
+      if ((e = gemv_tokens(a, nt, c->ffn, s, pdl))) return e;
+    }
+  }
+  // Final norm + classifier on the last token, fused greedy argmax (infer.rs:586-591, 740-746).
+  {
+    GemvArgs a = gemv_base(c, c->f_out, c->dim);
+    a.xf = c->x + (size_t)(nt - 1) * c->dim;
+    a.xf_ld = c->dim;
+    a.norm_w = c->out_norm;
+    a.seg[0] = GemvSegArg{c->out_w, c->logits, c->vocab, c->vocab};
+    a.nseg = 1;
+    a.epi = EPI_ARGMAX;
+    a.scale = c->logit_recip;
+    a.argmax_key = &c->st->key;
+    a.nt = 1;
+    if ((e = gemv_run(a, s, pdl))) return e;
+  }
+  return step_finish_run(&c->st->pos, (uint32_t)nt, &c->st->key, &c->st->next, c->st->tok, c->hist, s, pdl);
+}
+
+int finish_sync(nrc_ctx* c, float* logits_host, uint32_t* next_host, size_t advance) {
+  if (logits_host)
+    CU(cudaMemcpyAsync(logits_host, c->logits, (size_t)c->vocab * 4, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaMemcpyAsync(c->h_stage, &c->st->next, 8, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  const uint32_t next = c->h_stage[0], err = c->h_stage[1];
+  c->pos += advance;
+  if (err) return fail(NRC_ERR_DEVICE, "kernel wait expired (error bits 0x%x)", err);
+  if (next_host) *next_host = next;
+  return NRC_OK;
+}
+
+int ensure_graph(nrc_ctx* c) {
+  if (c->gexec) return NRC_OK;
+  cudaGraph_t g = nullptr;
+  CU(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e = enqueue_step(c, 1);
+  cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    return fail(NRC_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(e != cudaSuccess ? e : e2));
+  }
+  e = cudaGraphInstantiate(&c->gexec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    c->gexec = nullptr;
+    return fail(NRC_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
+  }
+  return NRC_OK;
+}
+}  // namespace
+
+extern "C" int nrc_ctx_forward(nrc_ctx* c, uint32_t token, float* logits_host, uint32_t* next_host) {
+  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  if (c->pos >= c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  if (token >= (uint32_t)c->vocab) return fail(NRC_ERR_BAD_TOKEN, "token %u >= vocab %d", token, c->vocab);
+  CU(cudaSetDevice(c->device));
+  if (!c->gexec) {
+    // First step runs eagerly (warms per-kernel caches), later ones replay the graph.
+    c->h_stage[16] = token;
+    CU(cudaMemcpyAsync(c->st->tok, &c->h_stage[16], 4, cudaMemcpyHostToDevice, c->stream));
+    CU(enqueue_step(c, 1));
+    int rc = finish_sync(c, logits_host, next_host, 1);
+    if (rc) return rc;
+    return ensure_graph(c);
+  }
+  c->h_stage[16] = token;
+  CU(cudaMemcpyAsync(c->st->tok, &c->h_stage[16], 4, cudaMemcpyHostToDevice, c->stream));
+  CU(cudaGraphLaunch(c->gexec, c->stream));
+  return finish_sync(c, logits_host, next_host, 1);
+}
+
+extern "C" int nrc_ctx_prefill_chunk(nrc_ctx* c, const uint32_t* tokens, size_t n, float* logits_host,
+                                     uint32_t* next_host) {
+  if (!c || !tokens) return fail(NRC_ERR_INVALID, "null argument");
+  if (n < 1 || n > NRC_MAX_BATCH) return fail(NRC_ERR_BAD_BATCH, "prefill chunk of %zu tokens", n);
+  if (c->pos + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  for (size_t i = 0; i < n; i++)
+    if (tokens[i] >= (uint32_t)c->vocab) return fail(NRC_ERR_BAD_TOKEN, "token %u >= vocab %d", tokens[i], c->vocab);
+  CU(cudaSetDevice(c->device));
+  memcpy(&c->h_stage[16], tokens, n * 4);
+  CU(cudaMemcpyAsync(c->st->tok, &c->h_stage[16], n * 4, cudaMemcpyHostToDevice, c->stream));
+  CU(enqueue_step(c, (int)n));
+  int rc = finish_sync(c, logits_host, next_host, n);
+  if (rc) return rc;
+  return ensure_graph(c);
+}
+
+extern "C" int nrc_ctx_prefill(nrc_ctx* c, const uint32_t* tokens, size_t n, float* logits_host, uint32_t* next_host) {
+  if (!c || !tokens) return fail(NRC_ERR_INVALID, "null argument");
+  if (n == 0) return fail(NRC_ERR_BAD_BATCH, "empty prompt");
+  if (c->pos + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  for (size_t i = 0; i < n; i += NRC_MAX_BATCH) {
+    const size_t b = n - i < (size_t)NRC_MAX_BATCH ? n - i : (size_t)NRC_MAX_BATCH;
+    const bool last = i + b == n;
+    int rc = nrc_ctx_prefill_chunk(c, tokens + i, b, last ? logits_host : nullptr, last ? next_host : nullptr);
+    if (rc) return rc;
+  }
+  return NRC_OK;
+}
+
+extern "C" int nrc_ctx_generate(nrc_ctx* c, uint32_t first, size_t n, uint32_t* out_host) {
+  if (!c || (!out_host && n)) return fail(NRC_ERR_INVALID, "null argument");
+  if (n == 0) return NRC_OK;
+  if (c->pos + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  if (first >= (uint32_t)c->vocab) return fail(NRC_ERR_BAD_TOKEN, "token %u >= vocab %d", first, c->vocab);
+  CU(cudaSetDevice(c->device));
+  const size_t p0 = c->pos;
+  uint32_t next = 0;
+  int rc = nrc_ctx_forward(c, first, nullptr, &next);  // eager first step + graph capture
+  if (rc) return rc;
+  for (size_t i = 1; i < n; i++) CU(cudaGraphLaunch(c->gexec, c->stream));
+  CU(cudaMemcpyAsync(out_host, c->hist + p0, n * 4, cudaMemcpyDeviceToHost, c->stream));
+  rc = finish_sync(c, nullptr, nullptr, n - 1);
+  return rc;
+}
+
+extern "C" int nrc_ctx_decode_async(nrc_ctx* c, size_t n) {
+  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  if (c->pos + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  if (!c->gexec) return fail(NRC_ERR_INVALID, "no decode step yet: call nrc_ctx_forward or nrc_ctx_prefill first");
+  CU(cudaSetDevice(c->device));
+  for (size_t i = 0; i < n; i++) CU(cudaGraphLaunch(c->gexec, c->stream));
+  c->pending += n;
+  return NRC_OK;
+}
+
+extern "C" int nrc_ctx_sync(nrc_ctx* c, uint32_t* next_host) {
+  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  CU(cudaSetDevice(c->device));
+  const size_t adv = c->pending;
+  c->pending = 0;
+  return finish_sync(c, nullptr, next_host, adv);
+}
+
+extern "C" int nrc_ctx_reset(nrc_ctx* c) {
+  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  CU(cudaSetDevice(c->device));
+  CU(cudaStreamSynchronize(c->stream));
+  c->pos = 0;
+  c->pending = 0;
+  CU(cudaMemsetAsync(&c->st->pos, 0, 4, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  return NRC_OK;
+}
+extern "C" size_t nrc_ctx_pos(const nrc_ctx* c) { return c ? c->pos : 0; }
+extern "C" size_t nrc_ctx_remaining(const nrc_ctx* c) { return c ? c->ctx - c->pos : 0; }
+extern "C" int nrc_ctx_logits_device(const nrc_ctx* c, const float** out) {
+  if (!c || !out) return fail(NRC_ERR_INVALID, "null argument");
+  *out = c->logits;
+  return NRC_OK;
+}
+extern "C" void* nrc_ctx_stream(const nrc_ctx* c) { return c ? (void*)c->stream : nullptr; }
+extern "C" int nrc_ctx_kv(nrc_ctx* c, size_t layer, size_t pos, uint16_t* k_host, uint16_t* v_host) {
+  if (!c || !k_host || !v_host) return fail(NRC_ERR_INVALID, "null argument");
+  if (layer >= (size_t)c->n_layers || pos >= c->ctx) return fail(NRC_ERR_INVALID, "kv index out of range");
+  CU(cudaSetDevice(c->device));
+  const size_t off = (layer * c->ctx + pos) * c->kv_dim;
+  CU(cudaMemcpyAsync(k_host, c->kc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaMemcpyAsync(v_host, c->vc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  return NRC_OK;
+}

@@ -1,0 +1,73 @@
+// Host launchers of the element kernels (ops.cu) and the attention kernels (attn.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace nrc {
+
+cudaError_t op_quantize_q8_0(const float* x, void* out, size_t n, cudaStream_t s);
+cudaError_t op_dequantize_q8_0(const void* b, float* out, size_t n, cudaStream_t s);
+cudaError_t op_quantize_q8k(const float* x, void* out, size_t n, cudaStream_t s);
+cudaError_t op_dequant_q4k(const void* b, float* out, size_t nblocks, cudaStream_t s);
+cudaError_t op_dequant_q6k(const void* b, float* out, size_t nblocks, cudaStream_t s);
+cudaError_t op_f32_to_f16(const float* x, uint16_t* o, size_t n, cudaStream_t s);
+cudaError_t op_f16_to_f32(const uint16_t* x, float* o, size_t n, cudaStream_t s);
+cudaError_t op_rmsnorm(float* out, const float* x, const float* w, size_t n, size_t rows, float eps,
+                       cudaStream_t s);
+cudaError_t op_softmax(float* x, size_t n, size_t rows, cudaStream_t s);
+cudaError_t op_swiglu(float* g, const float* u, size_t n, cudaStream_t s);
+cudaError_t op_argmax(const float* x, size_t n, unsigned long long* key_scratch, uint32_t* out, cudaStream_t s);
+
+// Position-dependent kernels of the forward pass. Positions are read from
+// device memory (pos_dev[0] + token index) so a captured CUDA graph replays
+// unchanged for every decode step.
+struct RopeArgs {
+  float* q;        // [nt][att_dim], rotated in place
+  const float* k;  // [nt][kv_dim]
+  const float* v;  // [nt][kv_dim]
+  const float* q_norm;  // per-head RMSNorm weights (Qwen3) or null
+  const float* k_norm;
+  float eps;
+  const float* cos_tab;  // [ctx][head_dim/2]
+  const float* sin_tab;
+  int style;  // 0 Adjacent, 1 Neox
+  uint16_t* kcache;  // this layer's [ctx][kv_dim]
+  uint16_t* vcache;
+  int nt, n_heads, n_kv_heads, head_dim, ctx;
+  const uint32_t* pos_dev;
+};
+cudaError_t rope_append_run(const RopeArgs& a, cudaStream_t s, bool pdl);
+
+struct AttnArgs {
+  const float* q;  // [nt][att_dim] (rotated)
+  float* out;      // [nt][att_dim]
+  const uint16_t* kcache;
+  const uint16_t* vcache;
+  float* partial;      // scratch [nt][n_heads][max_splits][head_dim + 2]
+  unsigned* counters;  // [nt][n_kv_heads], zero between launches
+  float scale;
+  int nt, n_heads, n_kv_heads, head_dim, ctx;
+  const uint32_t* pos_dev;
+};
+constexpr int ATTN_SPLIT = 128;
+cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl);
+
+// Embedding rows (QMat::dequant_row, infer.rs:37-56) times embed_scale for nt
+// tokens read from tok_dev; also clears the greedy-argmax key.
+struct EmbedArgs {
+  const uint8_t* embed;
+  int fmt, dim;
+  float embed_scale;
+  const uint32_t* tok_dev;
+  int nt;
+  float* x;  // [nt][dim]
+  unsigned long long* argmax_key;
+};
+cudaError_t embed_run(const EmbedArgs& a, cudaStream_t s, bool pdl);
+
+// Decode the argmax key into next_tok (and tok_in[0], the next step's input),
+// record it in hist[pos], then advance the device position by n.
+cudaError_t step_finish_run(uint32_t* pos_dev, uint32_t n, const unsigned long long* key, uint32_t* next_tok,
+                            uint32_t* tok_in, uint32_t* hist, cudaStream_t s, bool pdl);
+
+}  // namespace nrc

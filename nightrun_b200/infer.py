@@ -1,0 +1,167 @@
+"""Model and inference context (crates/nr-model): `.nrm` models on the GPU and
+the InferCtx surface (new / forward / prefill_chunk / prefill / reset /
+logits / remaining / pos) over the nrcuda C ABI.
+"""
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import check, lib
+
+
+class Model:
+    """A `.nrm` model resident in device memory (Model::parse + upload, format.rs:260-406)."""
+
+    def __init__(self, handle, device):
+        self.h = handle
+        self.device = device
+        self.meta = _lib.Meta()
+        check(lib().nrc_model_meta(self.h, C.byref(self.meta)))
+
+    @classmethod
+    def load(cls, blob, device=0, verify_crc=True):
+        buf = np.ascontiguousarray(np.frombuffer(bytes(blob), np.uint8) if not isinstance(blob, np.ndarray) else blob,
+                                   dtype=np.uint8)
+        h = C.c_void_p()
+        check(lib().nrc_model_load(buf.ctypes.data_as(C.c_void_p), buf.size, device, int(verify_crc), C.byref(h)))
+        return cls(h, device)
+
+    @classmethod
+    def synth(cls, cfg, seed, device=0):
+        """Seeded synthetic model of a nightrun_b200.configs preset, built on the device."""
+        s = _lib.synth_cfg(cfg)
+        h = C.c_void_p()
+        check(lib().nrc_model_synth(C.byref(s), seed, device, C.byref(h)))
+        return cls(h, device)
+
+    def export(self):
+        """The model as a complete `.nrm` blob (numpy uint8)."""
+        n = lib().nrc_model_nrm_size(self.h)
+        out = np.empty(n, np.uint8)
+        check(lib().nrc_model_export(self.h, out.ctypes.data_as(C.c_void_p), n))
+        return out
+
+    def data_crc(self):
+        v = C.c_uint32()
+        check(lib().nrc_model_data_crc(self.h, C.byref(v)))
+        return v.value
+
+    def required_bytes(self, ctx):
+        v = C.c_size_t()
+        check(lib().nrc_ctx_required_bytes(self.h, ctx, C.byref(v)))
+        return v.value
+
+    def ctx(self, ctx_len):
+        return InferCtx(self, ctx_len)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().nrc_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class InferCtx:
+    """Mirror of nr_model::InferCtx (crates/nr-model/src/infer.rs:264-760)."""
+
+    MAX_BATCH = _lib.MAX_BATCH
+
+    def __init__(self, model, ctx_len):
+        self.model = model
+        h = C.c_void_p()
+        check(lib().nrc_ctx_new(model.h, ctx_len, C.byref(h)))
+        self.h = h
+        self.vocab = model.meta.vocab
+        self.ctx_len = ctx_len
+        self._logits = np.zeros(self.vocab, np.float32)
+        self._next = C.c_uint32()
+
+    def _lp(self):
+        return self._logits.ctypes.data_as(C.c_void_p)
+
+    def forward(self, token):
+        """One token at the current position (infer.rs:510-595); returns the logits."""
+        check(lib().nrc_ctx_forward(self.h, int(token), self._lp(), C.byref(self._next)))
+        return self._logits.copy()
+
+    def forward_greedy(self, token):
+        """forward + vec::argmax without copying the logits; returns the next token id."""
+        check(lib().nrc_ctx_forward(self.h, int(token), None, C.byref(self._next)))
+        return self._next.value
+
+    def prefill_chunk(self, tokens):
+        """Batched prefill of 1..=64 tokens (infer.rs:601-750); last token's logits."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        check(lib().nrc_ctx_prefill_chunk(self.h, t.ctypes.data_as(C.c_void_p), t.size, self._lp(),
+                                          C.byref(self._next)))
+        return self._logits.copy()
+
+    def prefill(self, tokens):
+        """Prefill of any length in chunks of 64 (infer.rs:753-759)."""
+        t = np.ascontiguousarray(tokens, np.uint32)
+        check(lib().nrc_ctx_prefill(self.h, t.ctypes.data_as(C.c_void_p), t.size, self._lp(), C.byref(self._next)))
+        return self._logits.copy()
+
+    def generate(self, first, n):
+        """Greedy generation of n tokens after `first`, entirely on the device."""
+        out = np.zeros(n, np.uint32)
+        check(lib().nrc_ctx_generate(self.h, int(first), n, out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def decode_async(self, n):
+        """Enqueue n device-side greedy decode steps (no host round trip)."""
+        check(lib().nrc_ctx_decode_async(self.h, n))
+
+    def sync(self):
+        """Wait for enqueued steps; returns the last greedy token."""
+        check(lib().nrc_ctx_sync(self.h, C.byref(self._next)))
+        return self._next.value
+
+    def forward_into(self, token, logits_out_ptr, next_out_ptr):
+        """forward() writing the logits/next token into caller-provided (pinned) host buffers."""
+        check(lib().nrc_ctx_forward(self.h, int(token), logits_out_ptr, next_out_ptr))
+
+    @property
+    def next_token(self):
+        """Greedy choice (argmax) of the most recent logits."""
+        return self._next.value
+
+    def logits(self):
+        return self._logits.copy()
+
+    def reset(self):
+        check(lib().nrc_ctx_reset(self.h))
+
+    @property
+    def pos(self):
+        return lib().nrc_ctx_pos(self.h)
+
+    def remaining(self):
+        return lib().nrc_ctx_remaining(self.h)
+
+    def kv(self, layer, pos):
+        kvd = self.model.meta.n_kv_heads * self.model.meta.head_dim
+        k = np.empty(kvd, np.uint16)
+        v = np.empty(kvd, np.uint16)
+        check(lib().nrc_ctx_kv(self.h, layer, pos, k.ctypes.data_as(C.c_void_p), v.ctypes.data_as(C.c_void_p)))
+        return k, v
+
+    def stream_handle(self):
+        return lib().nrc_ctx_stream(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().nrc_ctx_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,247 @@
+"""GPU parity of the kernel-level C ABI against the CPU oracle.
+
+Integer / byte work (quantizers, f16 conversion, dequantization) and the
+matvec/matmul outputs must be bit-identical to the reference's scalar code
+(the GEMV keeps the scalar summation order); norm/softmax/swiglu use expf and
+parallel reductions and are held to 1e-6 relative (the reference's own
+tolerance, crates/nr-tensor/tests/kernels.rs:130-165).
+"""
+import numpy as np
+import pytest
+import torch
+
+from tests.refdata import Rng
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+F = np.float32
+
+
+@pytest.fixture(scope="module")
+def K():
+    from nightrun_b200 import kernels
+    return kernels
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.view(dtype)
+    return t.cuda()
+
+
+def blocks_dev(b):
+    return dev(np.frombuffer(b.tobytes(), np.uint8).copy())
+
+
+def host_bytes(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy().tobytes()
+
+
+def rand_bits_f32(n, seed):
+    r = np.random.default_rng(seed)
+    x = r.standard_normal(n).astype(np.float32) * r.choice([1e-6, 1e-3, 1.0, 30.0, 1e4], n).astype(np.float32)
+    return x
+
+
+def test_f16_to_f32_all_patterns(K, orc):
+    bits = np.arange(65536, dtype=np.uint16)
+    out = torch.empty(65536, dtype=torch.float32, device="cuda")
+    K.f16_to_f32(dev(bits.view(np.int16)), out)
+    assert host_bytes(out) == orc.f16_to_f32(bits).tobytes()
+
+
+def test_f32_to_f16_matches_reference(K, orc):
+    r = np.random.default_rng(3)
+    vals = np.concatenate([
+        r.integers(0, 2 ** 32, 200000, dtype=np.uint64).astype(np.uint32).view(np.float32),
+        rand_bits_f32(100000, 4),
+        np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 65504.0, 65520.0, 1e30, 2.0 ** -25, 1.5 * 2.0 ** -24,
+                  2.5 * 2.0 ** -24, 6e-8, -6e-8, 2.0 ** -14, 2.0 ** -15], np.float32)])
+    out = torch.empty(vals.size, dtype=torch.int16, device="cuda")
+    K.f32_to_f16(dev(vals), out)
+    assert host_bytes(out) == orc.f32_to_f16(vals).tobytes()
+
+
+@pytest.mark.parametrize("gen", ["vec", "adversarial", "zeros"])
+def test_quantize_q8_0_bytes(K, orc, gen):
+    rng = Rng(7)
+    x = {"vec": lambda: rng.vec(4096), "adversarial": lambda: rng.adversarial(4096),
+         "zeros": lambda: np.zeros(4096, np.float32)}[gen]()
+    out = torch.empty(4096 // 32 * 34, dtype=torch.uint8, device="cuda")
+    K.quantize(dev(x), out)
+    assert host_bytes(out) == orc.q8_quantize(x).tobytes()
+    back = torch.empty(4096, dtype=torch.float32, device="cuda")
+    K.dequantize(out, back)
+    assert host_bytes(back) == orc.q8_dequantize(orc.q8_quantize(x)).tobytes()
+
+
+@pytest.mark.parametrize("gen", ["vec", "adversarial", "zeros"])
+def test_quantize_q8k_bytes(K, orc, gen):
+    rng = Rng(11)
+    x = {"vec": lambda: rng.vec(2048), "adversarial": lambda: rng.adversarial(2048),
+         "zeros": lambda: np.zeros(2048, np.float32)}[gen]()
+    out = torch.empty(2048 // 256 * 292, dtype=torch.uint8, device="cuda")
+    K.quantize_q8k(dev(x), out)
+    assert host_bytes(out) == orc.quantize_q8k(x).tobytes()
+
+
+@pytest.mark.parametrize("fmt", ["q4k", "q6k"])
+def test_dequant_kquant_bit_exact(K, orc, fmt):
+    rng = Rng(21)
+    src = np.concatenate([rng.vec(256 * 8), rng.adversarial(256 * 8)])
+    b = orc.quantize_q4k_ref(src) if fmt == "q4k" else orc.quantize_q6k_ref(src)
+    out = torch.empty(src.size, dtype=torch.float32, device="cuda")
+    (K.dequant_q4k if fmt == "q4k" else K.dequant_q6k)(blocks_dev(b), out)
+    ref = orc.dequant_q4k(b) if fmt == "q4k" else orc.dequant_q6k(b)
+    assert host_bytes(out) == ref.tobytes()
+
+
+def make_weights(orc, fmt, rows, cols, seed, adversarial=False):
+    rng = Rng(seed)
+    src = rng.adversarial(rows * cols) if adversarial else rng.vec(rows * cols)
+    if fmt == "q8_0":
+        return orc.q8_quantize(src)
+    return orc.quantize_q4k_ref(src) if fmt == "q4k" else orc.quantize_q6k_ref(src)
+
+
+def make_acts(orc, fmt, n, seed, batch=1):
+    x = Rng(seed).vec(n * batch)
+    return orc.q8_quantize(x) if fmt == "q8_0" else orc.quantize_q8k(x)
+
+
+def gpu_matmul(K, fmt, w, xs, rows, cols, batch, w_offset=0):
+    wb = np.frombuffer(w.tobytes(), np.uint8)
+    if w_offset:
+        wd = torch.empty(wb.size + 64, dtype=torch.uint8, device="cuda")
+        wd[w_offset:w_offset + wb.size].copy_(dev(wb.copy()))
+        wt = wd[w_offset:w_offset + wb.size]
+    else:
+        wt = dev(wb.copy())
+    y = torch.full((batch, rows), float("nan"), dtype=torch.float32, device="cuda")
+    fn = {"q8_0": (K.matvec_q8, K.matmul_q8), "q4k": (K.matvec_q4k, K.matmul_q4k),
+          "q6k": (K.matvec_q6k, K.matmul_q6k)}[fmt]
+    if batch == 1:
+        fn[0](y, wt, blocks_dev(xs), rows, cols)
+    else:
+        fn[1](y, wt, blocks_dev(xs), rows, cols, batch)
+    K.sync_check()
+    return y.cpu().numpy()
+
+
+SHAPES = {
+    "q8_0": [(48, 128), (48, 256), (7, 32), (33, 96), (2048, 2048), (512, 2048), (100, 8192), (64, 9728),
+             (300, 2560)],
+    "q4k": [(48, 512), (32, 512), (5, 256), (2048, 2048), (9728 // 64, 2560), (64, 9728), (37, 3072)],
+    "q6k": [(32, 512), (3, 256), (2048, 2048), (70, 2560), (64, 9728), (41, 3072)],
+}
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4k", "q6k"])
+def test_matvec_bit_exact_vs_scalar(K, orc, fmt):
+    for i, (rows, cols) in enumerate(SHAPES[fmt]):
+        w = make_weights(orc, fmt, rows, cols, 100 + i, adversarial=(i % 2 == 1))
+        x = make_acts(orc, fmt, cols, 200 + i)
+        ref = orc.matvec(fmt, w, x, rows, cols)
+        got = gpu_matmul(K, fmt, w, x, rows, cols, 1)[0]
+        assert got.tobytes() == ref.tobytes(), f"{fmt} {rows}x{cols}: max diff {np.max(np.abs(got - ref))}"
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4k", "q6k"])
+@pytest.mark.parametrize("batch", [2, 3, 5, 8, 9, 17, 64])
+def test_matmul_bit_exact_and_equals_matvec(K, orc, fmt, batch):
+    rows, cols = (96, 512) if fmt != "q8_0" else (96, 320)
+    w = make_weights(orc, fmt, rows, cols, 7)
+    xs = make_acts(orc, fmt, cols, 8, batch)
+    ref = orc.matmul(fmt, w, xs, rows, cols, batch)
+    got = gpu_matmul(K, fmt, w, xs, rows, cols, batch)
+    assert got.tobytes() == ref.tobytes()
+    bpr = cols // (32 if fmt == "q8_0" else 256)
+    for b in range(batch):  # matmul == matvec, kernels.rs:277-292 / kquant.rs:297-329
+        one = gpu_matmul(K, fmt, w, xs[b * bpr:(b + 1) * bpr].copy(), rows, cols, 1)[0]
+        assert one.tobytes() == got[b].tobytes()
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4k", "q6k"])
+@pytest.mark.parametrize("offset", [2, 4, 6, 8, 14])
+def test_matvec_unaligned_weights(K, orc, fmt, offset):
+    rows, cols = (37, 512)
+    w = make_weights(orc, fmt, rows, cols, 31)
+    x = make_acts(orc, fmt, cols, 32)
+    ref = orc.matvec(fmt, w, x, rows, cols)
+    got = gpu_matmul(K, fmt, w, x, rows, cols, 1, w_offset=offset)[0]
+    assert got.tobytes() == ref.tobytes()
+
+
+def test_saturated_blocks(K, orc):  # kquant.rs:210-245 blocks, bit-exact vs scalar
+    from tests.test_oracle import saturated_blocks
+    q4, q6 = saturated_blocks(orc)
+    x = orc.quantize_q8k(Rng(81).adversarial(256))
+    for fmt, blk in (("q4k", q4), ("q6k", q6)):
+        w = np.concatenate([blk] * 16)
+        ref = orc.matvec(fmt, w, x, 16, 256)
+        got = gpu_matmul(K, fmt, w, x, 16, 256, 1)[0]
+        assert got.tobytes() == ref.tobytes()
+    # Q8_0 with -128 weight bytes (outside the quantizer's range, valid in GGUF files).
+    w8 = np.zeros(64, O.Q8_0)
+    w8["d"] = orc.f32_to_f16(np.array([0.75], np.float32))[0]
+    w8["qs"] = -128
+    x8 = orc.q8_quantize(Rng(5).adversarial(256))
+    ref = orc.matvec("q8_0", w8, x8, 8, 256)
+    got = gpu_matmul(K, "q8_0", w8, x8, 8, 256, 1)[0]
+    assert got.tobytes() == ref.tobytes()
+
+
+def test_matvec_empty_and_invalid(K):
+    from nightrun_b200 import NrcError
+    y = torch.empty(4, dtype=torch.float32, device="cuda")
+    w = torch.zeros(34 * 4, dtype=torch.uint8, device="cuda")
+    with pytest.raises(NrcError) as e:
+        K.matvec_q8(y, w, w, 4, 33)
+    assert e.value.name == "INVALID"
+    K.matvec_q8(y, w, w, 0, 32)  # zero rows: no-op
+    y.fill_(1.0)
+    K.matvec_q8(y, w, w, 4, 0)  # zero cols: y = 0 like the empty dot
+    assert torch.all(y == 0)
+
+
+def test_rmsnorm_softmax_swiglu(K, orc):
+    rng = Rng(9)
+    x = rng.vec(2048) * F(3)
+    w = rng.vec(2048) + F(1)
+    out = torch.empty(2048, dtype=torch.float32, device="cuda")
+    K.rmsnorm(out, dev(x), dev(w), 1e-5)
+    ref = orc.rmsnorm(x, w, 1e-5)
+    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-6, atol=1e-7)
+    s = rng.vec(1000) * F(8)
+    st = dev(s)
+    K.softmax(st)
+    np.testing.assert_allclose(st.cpu().numpy(), orc.softmax(s), rtol=1e-6, atol=1e-8)
+    g, u = rng.vec(4096) * F(6), rng.vec(4096)
+    gt = dev(g)
+    K.swiglu(gt, dev(u))
+    np.testing.assert_allclose(gt.cpu().numpy(), orc.swiglu(g, u), rtol=1e-6, atol=1e-7)
+
+
+def test_argmax_first_max_and_edges(K):
+    assert K.argmax(dev(np.array([0.1, 4.0, -2.0, 4.0], np.float32))) == 1  # kernels.rs:228-231
+    assert K.argmax(dev(np.array([np.nan, -np.inf, 3.0, 3.0], np.float32))) == 2
+    assert K.argmax(dev(np.array([np.nan, -np.inf], np.float32))) == 0
+    assert K.argmax(dev(np.full(5, -np.inf, np.float32))) == 0
+    big = np.random.default_rng(1).standard_normal(151936).astype(np.float32)
+    big[100000] = big[5] = 99.0
+    assert K.argmax(dev(big)) == 5
+
+
+@pytest.mark.parametrize("style,hd", [(0, 64), (1, 128), (0, 128)])
+def test_rope_bit_exact(K, orc, style, hd):
+    freqs = K.rope_freqs(hd, 500000.0, (32.0, 1.0, 4.0, 8192.0))
+    ref_f = orc.rope_freqs(hd, 500000.0, (32.0, 1.0, 4.0, 8192.0))
+    assert np.array(freqs, np.float32).tobytes() == ref_f.tobytes()
+    x = Rng(5).vec(hd * 6)
+    for pos in (0, 1, 17, 4095):
+        t = dev(x)
+        K.rope_apply(t, hd, freqs, pos, style)
+        assert host_bytes(t) == orc.rope_apply(x, hd, ref_f, pos, style).tobytes()
