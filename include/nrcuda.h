@@ -89,6 +89,12 @@ int nrc_rmsnorm(float* out, const float* x, const float* w, size_t n, size_t row
 int nrc_softmax(float* x, size_t n, size_t rows, void* stream);
 /* vec::swiglu (vec.rs:44-50): gate[i] = silu(gate[i]) * up[i]. */
 int nrc_swiglu(float* gate, const float* up, size_t n, void* stream);
+/* The expf of vec::softmax / vec::swiglu (vec.rs:34, 47; crate libm 0.2.16), elementwise. This
+ * library evaluates a correctly rounded binary32 exp (the test oracle evaluates the same one). */
+int nrc_expf(const float* x, float* y, size_t n, void* stream);
+/* Test support: hash of nrc_expf's output bits over every binary32 input, one 64-bit value per
+ * chunk of 2^20 consecutive bit patterns, chunks [chunk0, chunk0 + nchunks) of 4096. */
+int nrc_expf_hash(uint64_t* out_dev, int chunk0, int nchunks, void* stream);
 /* vec::argmax (vec.rs:80-90): first maximum; writes the index to *out_dev (uint32, device). */
 int nrc_argmax(const float* x, size_t n, uint32_t* out_dev, void* stream);
 /* rope::rope_freqs (crates/nr-tensor/src/rope.rs:14-34), computed on the host into out_host

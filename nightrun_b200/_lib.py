@@ -80,6 +80,8 @@ SIGNATURES = [
     ("nrc_softmax", I, [P, S, S, P]),
     ("nrc_swiglu", I, [P, P, S, P]),
     ("nrc_argmax", I, [P, S, P, P]),
+    ("nrc_expf", I, [P, P, S, P]),
+    ("nrc_expf_hash", I, [P, I, I, P]),
     ("nrc_rope_freqs", I, [P, S, F, F, F, F, F]),
     ("nrc_rope_apply", I, [P, S, S, P, S, I, P]),
     ("nrc_model_load", I, [P, S, I, I, C.POINTER(P)]),

@@ -10,6 +10,7 @@
 
 #include "common.cuh"
 #include "gemv.cuh"
+#include "mma.cuh"
 #include "nrcuda.h"
 #include "ops.cuh"
 
@@ -69,6 +70,41 @@ int matvec_common(int fmt, float* y, const void* w, const void* x, size_t rows, 
   int rc = dev_scratch(&sc);
   if (rc) return rc;
   const size_t xblk = fmt == FMT_Q8_0 ? 34 : 292;
+  if (fmt == FMT_Q8_0 && batch > 8 && cols % 256 == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+    // Tensor-core path (tcgen05 kind::i8), 64 tokens per pass.
+    const int tiles = (int)((rows + 127) / 128);
+    for (size_t t0 = 0; t0 < batch; t0 += 64) {
+      const int nt = (int)(batch - t0 < 64 ? batch - t0 : 64);
+      int NS, ntg;
+      mma_choose(tiles, nt, &NS, &ntg);
+      const size_t bpr = cols / 32;
+      uint8_t* xq = nullptr;
+      float* xd = nullptr;
+      if (cudaMallocAsync((void**)&xq, (size_t)ntg * NS * cols, S(stream)) != cudaSuccess ||
+          cudaMallocAsync((void**)&xd, (size_t)ntg * NS * bpr * 4, S(stream)) != cudaSuccess)
+        return nrc_fail_api(NRC_ERR_ALLOC, "activation tile allocation failed");
+      rc = cuda_rc(mma_pack_q8_run(static_cast<const uint8_t*>(x) + t0 * bpr * 34, nt, (int)cols, NS, ntg, xq, xd,
+                                   S(stream)),
+                   "mma pack");
+      MmaArgs m{};
+      m.seg[0] = MmaSeg{w, y + t0 * rows, (int)rows, (int)rows};
+      m.nseg = 1;
+      m.K = (int)cols;
+      m.xq = xq;
+      m.xd = xd;
+      m.nt = nt;
+      m.NS = NS;
+      m.ntg = ntg;
+      m.epi = EPI_STORE;
+      m.scale = 1.0f;
+      m.err = sc.err;
+      if (!rc) rc = cuda_rc(mma_q8_run(m, S(stream), false), "mma launch");
+      cudaFreeAsync(xq, S(stream));
+      cudaFreeAsync(xd, S(stream));
+      if (rc) return rc;
+    }
+    return NRC_OK;
+  }
   for (size_t t0 = 0; t0 < batch; t0 += 8) {
     GemvArgs a{};
     a.fmt = fmt;
@@ -213,6 +249,18 @@ int nrc_rope_apply(float* x, size_t len, size_t head_dim, const float* freqs, si
   if (npairs == 0) return NRC_OK;
   k_rope_one_param<<<(npairs + 255) / 256, 256, 0, S(stream)>>>(x, (int)len, (int)head_dim, style, cs);
   return cuda_rc(cudaGetLastError(), "rope_apply");
+}
+
+int nrc_expf(const float* x, float* y, size_t n, void* stream) {
+  if (n && (!x || !y)) return nrc_fail_api(NRC_ERR_INVALID, "null pointer");
+  return cuda_rc(op_expf(x, y, n, S(stream)), "expf");
+}
+
+int nrc_expf_hash(uint64_t* out_dev, int chunk0, int nchunks, void* stream) {
+  if (!out_dev || chunk0 < 0 || nchunks < 0 || chunk0 + nchunks > 4096)
+    return nrc_fail_api(NRC_ERR_INVALID, "bad expf_hash range");
+  return cuda_rc(op_expf_hash(reinterpret_cast<unsigned long long*>(out_dev), chunk0, nchunks, S(stream)),
+                 "expf_hash");
 }
 
 int nrc_sync_check(void* stream) {

@@ -2,18 +2,23 @@
 //  * rope_append: Qwen3 per-head q/k RMSNorm (vec.rs:17-27), RoPE (rope.rs:49-65,
 //    from host-built cos/sin tables) and the f16 KV-cache append
 //    (crates/nr-model/src/infer.rs:533-551, 639-659);
-//  * attention: GQA attention over the f16 cache (infer.rs:553-572, 661-685),
-//    split over positions in chunks of ATTN_SPLIT, partial softmax states
-//    combined by the last CTA of each (token, kv head);
+//  * attention: GQA attention over the f16 cache (infer.rs:553-572, 661-685);
 //  * embed: token-embedding row dequantization (infer.rs:37-56, 516-521);
 //  * step_finish: position advance and greedy-token decode.
-// Every per-token result depends only on that token's position, so batched
-// prefill and token-by-token decode produce bit-identical outputs.
+// Every reduction keeps the reference's sequential order (index order for
+// sums of squares and softmax sums, position order for the V accumulation),
+// so results are bit-identical to the scalar reference, and every per-token
+// result depends only on that token's position: batched prefill and
+// token-by-token decode agree bit for bit.
 #include "common.cuh"
+#include "expf_cr.cuh"
 #include "ops.cuh"
 
 namespace nrc {
 namespace {
+
+constexpr int ATT_THREADS = 256;
+constexpr int VCHUNK = 128;  // V rows staged per pass
 
 __global__ void k_rope_append(const RopeArgs a) {
   pdl_wait();
@@ -29,32 +34,37 @@ __global__ void k_rope_append(const RopeArgs a) {
   const uint32_t pos = a.pos_dev[0] + (uint32_t)tok;
   const bool is_q = h < a.n_heads;
   const int kvh = h - a.n_heads;
-  float vals[4];  // head_dim <= 128: 4 values per lane
+  __shared__ float buf[8][128];
+  float* hb = buf[threadIdx.x / 32];
   const float* src = is_q ? a.q + (size_t)tok * att_dim + h * hd : a.k + (size_t)tok * kv_dim + kvh * hd;
   const int per = hd / 32;
+  float vals[4];
 #pragma unroll
   for (int i = 0; i < 4; i++)
-    if (i < per) vals[i] = src[lane + 32 * i];
+    if (i < per) {
+      vals[i] = src[lane + 32 * i];
+      hb[lane + 32 * i] = vals[i];
+    }
+  __syncwarp();
   const float* nw = is_q ? a.q_norm : a.k_norm;
   if (nw) {
-    // rmsnorm_inplace: x *= scale * w, scale = 1 / sqrtf(ss / n + eps)
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-      if (i < per) ss = __fadd_rn(ss, __fmul_rn(vals[i], vals[i]));
-    ss = warp_sum(ss);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), a.eps)));
+    // rmsnorm_inplace (vec.rs:17-27): ss in index order, then x *= scale * w.
+    float scale = 0.0f;
+    if (lane == 0) {
+      float ss = 0.0f;
+      for (int i = 0; i < hd; i++) ss = __fadd_rn(ss, __fmul_rn(hb[i], hb[i]));
+      scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), a.eps)));
+    }
+    scale = __shfl_sync(0xffffffffu, scale, 0);
 #pragma unroll
     for (int i = 0; i < 4; i++)
       if (i < per) vals[i] = __fmul_rn(vals[i], __fmul_rn(scale, nw[lane + 32 * i]));
-  }
-  // Rotation: each lane owns elements lane + 32*i; partners are exchanged via smem.
-  __shared__ float buf[8][128];
-  float* hb = buf[threadIdx.x / 32];
+    __syncwarp();
 #pragma unroll
-  for (int i = 0; i < 4; i++)
-    if (i < per) hb[lane + 32 * i] = vals[i];
-  __syncwarp();
+    for (int i = 0; i < 4; i++)
+      if (i < per) hb[lane + 32 * i] = vals[i];
+    __syncwarp();
+  }
   const float* ct = a.cos_tab + (size_t)pos * half;
   const float* st = a.sin_tab + (size_t)pos * half;
   float outv[4];
@@ -97,36 +107,37 @@ __global__ void k_rope_append(const RopeArgs a) {
   }
 }
 
-// One CTA per (kv head, position split, token); ATTN_SPLIT threads, one per position.
-__global__ void __launch_bounds__(ATTN_SPLIT) k_attention(const AttnArgs a) {
+// One CTA per (kv head, token) over every position 0..=pos:
+//  1. scores: one thread per position, dot_f16 in the scalar order
+//     (kernels.rs:146-157) times the score scale, for each query head of the group;
+//  2. softmax per head (vec.rs:30-41): max, expf, the sum in position order
+//     (one thread per head), normalisation;
+//  3. out[h][d] = sum over positions, in position order, of p_t * v_t[d]
+//     (axpy_f16, kernels.rs:160-169), V rows staged in shared memory.
+__global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   pdl_wait();
   pdl_trigger();
-  const int g = blockIdx.x, split = blockIdx.y, tok = blockIdx.z;
+  const int g = blockIdx.x, tok = blockIdx.z;
   const uint32_t pos = a.pos_dev[0] + (uint32_t)tok;
   const int npos = (int)pos + 1;
-  const int nsplit = (npos + ATTN_SPLIT - 1) / ATTN_SPLIT;
-  if (split >= nsplit) return;
   const int hd = a.head_dim;
   const int gqa = a.n_heads / a.n_kv_heads;
   const int att_dim = a.n_heads * hd, kv_dim = a.n_kv_heads * hd;
-  const int max_splits = (a.ctx + ATTN_SPLIT - 1) / ATTN_SPLIT;
-  const int t0 = split * ATTN_SPLIT;
-  const int tn = min(ATTN_SPLIT, npos - t0);
-  extern __shared__ float sm[];
-  float* qs = sm;                      // [gqa][hd]
-  float* sc = qs + gqa * hd;           // [gqa][ATTN_SPLIT]
-  __shared__ float red[ATTN_SPLIT / 32];
-  __shared__ float mh[8], lh[8];
-  __shared__ int is_last;
+  const int cap = a.ctx;  // score row capacity
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                    // [gqa][hd]
+  float* sc = qs + gqa * hd;         // [gqa][cap]
+  uint16_t* vs = reinterpret_cast<uint16_t*>(sc + gqa * cap);  // [VCHUNK][hd]
+  __shared__ float red[ATT_THREADS / 32];
+  __shared__ float mh[8], inv_h[8];
   const int tid = threadIdx.x;
-  for (int i = tid; i < gqa * hd; i += blockDim.x) qs[i] = a.q[(size_t)tok * att_dim + g * gqa * hd + i];
+  for (int i = tid; i < gqa * hd; i += ATT_THREADS) qs[i] = a.q[(size_t)tok * att_dim + g * gqa * hd + i];
   __syncthreads();
-  // Scores: dot_f16 in the scalar order (kernels.rs:146-157), times the score scale.
-  if (tid < tn) {
-    const uint16_t* kr = a.kcache + (size_t)(t0 + tid) * kv_dim + g * hd;
+  for (int t = tid; t < npos; t += ATT_THREADS) {
+    const uint16_t* kr = a.kcache + (size_t)t * kv_dim + g * hd;
     for (int h = 0; h < gqa; h++) {
-      float s = 0.0f;
       const float* qh = qs + h * hd;
+      float s = 0.0f;
       for (int d0 = 0; d0 < hd; d0 += 8) {
         const uint4 kv8 = *reinterpret_cast<const uint4*>(kr + d0);
         const uint32_t w[4] = {kv8.x, kv8.y, kv8.z, kv8.w};
@@ -136,91 +147,66 @@ __global__ void __launch_bounds__(ATTN_SPLIT) k_attention(const AttnArgs a) {
           s = __fadd_rn(s, __fmul_rn(f16_to_f32(w[j] >> 16), qh[d0 + 2 * j + 1]));
         }
       }
-      sc[h * ATTN_SPLIT + tid] = __fmul_rn(s, a.scale);
+      sc[h * cap + t] = __fmul_rn(s, a.scale);
     }
   }
   __syncthreads();
-  // Per-head max and exp-sum over this split.
   for (int h = 0; h < gqa; h++) {
-    float m = tid < tn ? sc[h * ATTN_SPLIT + tid] : -INFINITY;
+    float m = -INFINITY;
+    for (int t = tid; t < npos; t += ATT_THREADS) m = fmaxf(m, sc[h * cap + t]);
     m = warp_max(m);
     if ((tid & 31) == 0) red[tid >> 5] = m;
     __syncthreads();
     if (tid == 0) {
       float mm = -INFINITY;
-      for (int w = 0; w < ATTN_SPLIT / 32; w++) mm = fmaxf(mm, red[w]);
+      for (int w = 0; w < ATT_THREADS / 32; w++) mm = fmaxf(mm, red[w]);
       mh[h] = mm;
     }
     __syncthreads();
-    float e = 0.0f;
-    if (tid < tn) {
-      e = expf(__fsub_rn(sc[h * ATTN_SPLIT + tid], mh[h]));
-      sc[h * ATTN_SPLIT + tid] = e;
-    }
-    e = warp_sum(e);
-    if ((tid & 31) == 0) red[tid >> 5] = e;
-    __syncthreads();
-    if (tid == 0) {
-      float ll = 0.0f;
-      for (int w = 0; w < ATTN_SPLIT / 32; w++) ll = __fadd_rn(ll, red[w]);
-      lh[h] = ll;
-    }
-    __syncthreads();
+    const float mx = mh[h];
+    for (int t = tid; t < npos; t += ATT_THREADS) sc[h * cap + t] = expf_cr(__fsub_rn(sc[h * cap + t], mx));
   }
-  const int nout = gqa * hd;
-  if (nsplit == 1) {
-    // softmax normalisation then axpy_f16 in position order (infer.rs:565-571).
-    for (int o = tid; o < nout; o += blockDim.x) {
-      const int h = o / hd, d = o % hd;
-      const float inv = __fdiv_rn(1.0f, lh[h]);
-      float acc = 0.0f;
-      const uint16_t* vr = a.vcache + g * hd + d;
-      for (int t = 0; t < tn; t++) {
-        const float p = __fmul_rn(sc[h * ATTN_SPLIT + t], inv);
-        acc = __fadd_rn(acc, __fmul_rn(p, f16_to_f32(vr[(size_t)(t0 + t) * kv_dim])));
-      }
-      a.out[(size_t)tok * att_dim + g * gqa * hd + o] = acc;
-    }
-    return;
-  }
-  // Multi-split: unnormalised partial state, combined by the last CTA.
-  float* part = a.partial + ((size_t)tok * a.n_heads + g * gqa) * max_splits * (hd + 2);
-  for (int o = tid; o < nout; o += blockDim.x) {
-    const int h = o / hd, d = o % hd;
-    float acc = 0.0f;
-    const uint16_t* vr = a.vcache + g * hd + d;
-    for (int t = 0; t < tn; t++)
-      acc = __fadd_rn(acc, __fmul_rn(sc[h * ATTN_SPLIT + t], f16_to_f32(vr[(size_t)(t0 + t) * kv_dim])));
-    part[((size_t)h * max_splits + split) * (hd + 2) + d] = acc;
-  }
+  __syncthreads();
   if (tid < gqa) {
-    part[((size_t)tid * max_splits + split) * (hd + 2) + hd] = mh[tid];
-    part[((size_t)tid * max_splits + split) * (hd + 2) + hd + 1] = lh[tid];
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    unsigned* ctr = a.counters + (size_t)tok * a.n_kv_heads + g;
-    const unsigned prev = atomicAdd(ctr, 1u);
-    is_last = (prev == (unsigned)nsplit - 1);
-    if (is_last) *ctr = 0u;  // ready for the next launch
+    const float* e = sc + tid * cap;
+    float s = 0.0f;
+    for (int t = 0; t < npos; t++) s = __fadd_rn(s, e[t]);
+    inv_h[tid] = __fdiv_rn(1.0f, s);
   }
   __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  for (int o = tid; o < nout; o += blockDim.x) {
-    const int h = o / hd, d = o % hd;
-    const float* ph = part + (size_t)h * max_splits * (hd + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(ph + (size_t)s * (hd + 2) + hd));
-    float L = 0.0f, O = 0.0f;
-    for (int s = 0; s < nsplit; s++) {
-      const float* ps = ph + (size_t)s * (hd + 2);
-      const float f = expf(__fsub_rn(__ldcg(ps + hd), M));
-      L = __fadd_rn(L, __fmul_rn(__ldcg(ps + hd + 1), f));
-      O = __fadd_rn(O, __fmul_rn(__ldcg(ps + d), f));
+  for (int h = 0; h < gqa; h++) {
+    const float inv = inv_h[h];
+    for (int t = tid; t < npos; t += ATT_THREADS) sc[h * cap + t] = __fmul_rn(sc[h * cap + t], inv);
+  }
+  // Output chains: thread owns outputs o = tid + i*ATT_THREADS (i < 4), o = h*hd + d.
+  const int nout = gqa * hd;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const int cpr = hd / 8;  // 16-byte chunks per V row
+  for (int t0 = 0; t0 < npos; t0 += VCHUNK) {
+    const int tn = npos - t0 < VCHUNK ? npos - t0 : VCHUNK;
+    __syncthreads();
+    for (int i = tid; i < tn * cpr; i += ATT_THREADS) {
+      const int r = i / cpr, c = i - r * cpr;
+      *reinterpret_cast<uint4*>(vs + r * hd + c * 8) =
+          *reinterpret_cast<const uint4*>(a.vcache + (size_t)(t0 + r) * kv_dim + g * hd + c * 8);
     }
-    a.out[(size_t)tok * att_dim + g * gqa * hd + o] = __fdiv_rn(O, L);
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int o = tid + i * ATT_THREADS;
+      if (o < nout) {
+        const int h = o / hd, d = o - h * hd;
+        const float* p = sc + h * cap + t0;
+        float ac = acc[i];
+        for (int t = 0; t < tn; t++) ac = __fadd_rn(ac, __fmul_rn(p[t], f16_to_f32(vs[t * hd + d])));
+        acc[i] = ac;
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int o = tid + i * ATT_THREADS;
+    if (o < nout) a.out[(size_t)tok * att_dim + g * gqa * hd + o] = acc[i];
   }
 }
 
@@ -312,15 +298,26 @@ cudaError_t rope_append_run(const RopeArgs& a, cudaStream_t s, bool pdl) {
   return launch((const void*)k_rope_append, dim3((items + wpb - 1) / wpb), dim3(32 * wpb), 0, s, pdl, args);
 }
 
+size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx) {
+  const int gqa = n_heads / n_kv_heads;
+  return (size_t)gqa * head_dim * 4 + (size_t)gqa * ctx * 4 + (size_t)VCHUNK * head_dim * 2 + 16;
+}
+
 cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl) {
   const int gqa = a.n_heads / a.n_kv_heads;
-  if (gqa > 8 || a.head_dim % 8) return cudaErrorInvalidValue;
-  const int max_splits = (a.ctx + ATTN_SPLIT - 1) / ATTN_SPLIT;
-  const size_t smem = (size_t)gqa * a.head_dim * 4 + (size_t)gqa * ATTN_SPLIT * 4;
+  if (gqa > 8 || a.head_dim % 8 || a.head_dim > 128) return cudaErrorInvalidValue;
+  const size_t smem = attention_smem_bytes(a.n_heads, a.n_kv_heads, a.head_dim, a.ctx);
+  if (smem > ATTN_MAX_SMEM) return cudaErrorInvalidValue;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute((const void*)k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATTN_MAX_SMEM);
+    attr_done[dev] = true;
+  }
   AttnArgs aa = a;
   void* args[] = {&aa};
-  return launch((const void*)k_attention, dim3(a.n_kv_heads, max_splits, a.nt), dim3(ATTN_SPLIT), smem, s, pdl,
-                args);
+  return launch((const void*)k_attention, dim3(a.n_kv_heads, 1, a.nt), dim3(ATT_THREADS), smem, s, pdl, args);
 }
 
 cudaError_t embed_run(const EmbedArgs& a, cudaStream_t s, bool pdl) {

@@ -13,6 +13,7 @@
 
 #include "common.cuh"
 #include "gemv.cuh"
+#include "mma.cuh"
 #include "nrcuda.h"
 #include "ops.cuh"
 #include "synth.cuh"
@@ -463,7 +464,7 @@ struct Status {
 };
 
 struct Layout {
-  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, partial, counters, status, hist, total;
+  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, status, hist, total;
 };
 
 size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -472,7 +473,8 @@ Layout layout_for(const nrc_meta& mt, size_t ctx) {
   Layout L{};
   const size_t dim = mt.dim, att = (size_t)mt.n_heads * mt.head_dim, kv = (size_t)mt.n_kv_heads * mt.head_dim;
   const size_t B = NRC_MAX_BATCH;
-  const size_t splits = (ctx + ATTN_SPLIT - 1) / ATTN_SPLIT;
+  size_t maxk = dim > att ? dim : att;
+  if (mt.ffn_dim > maxk) maxk = mt.ffn_dim;
   size_t o = 0;
   auto take = [&](size_t bytes) {
     size_t r = o;
@@ -491,8 +493,8 @@ Layout layout_for(const nrc_meta& mt, size_t ctx) {
   L.logits = take((size_t)mt.vocab * 4);
   L.cos_t = take(ctx * (mt.head_dim / 2) * 4);
   L.sin_t = take(ctx * (mt.head_dim / 2) * 4);
-  L.partial = take(B * mt.n_heads * splits * (mt.head_dim + 2) * 4);
-  L.counters = take(B * mt.n_kv_heads * 4);
+  L.mxq = take(B * maxk);            // tensor-core activation tiles (prefill)
+  L.mxd = take(B * (maxk / 32) * 4);  // and their block scales
   L.status = take(sizeof(Status));
   L.hist = take((ctx + 1) * 4);
   L.total = o;
@@ -543,8 +545,9 @@ struct nrc_ctx {
   uint8_t* arena = nullptr;
   Layout lay;
   uint16_t *kc, *vc;
-  float *x, *q, *k, *v, *att, *g, *u, *logits, *cos_t, *sin_t, *partial;
-  unsigned* counters;
+  float *x, *q, *k, *v, *att, *g, *u, *logits, *cos_t, *sin_t;
+  uint8_t* mxq;  // tensor-core activation tiles (prefill)
+  float* mxd;
   Status* st;
   uint32_t* hist;
   uint32_t* h_stage = nullptr;  // pinned host staging: tokens in, status out
@@ -570,6 +573,8 @@ extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
       mt.n_heads / mt.n_kv_heads > 8)
     return fail(NRC_ERR_INVALID, "unsupported attention shape (head_dim %u, heads %u/%u)", mt.head_dim, mt.n_heads,
                 mt.n_kv_heads);
+  if (attention_smem_bytes(mt.n_heads, mt.n_kv_heads, mt.head_dim, (int)ctx) > ATTN_MAX_SMEM)
+    return fail(NRC_ERR_INVALID, "context of %zu positions exceeds the attention kernel's score buffer", ctx);
   nrc_ctx* c = new nrc_ctx();
   c->m = m;
   c->device = m->device;
@@ -655,8 +660,8 @@ extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
   c->logits = reinterpret_cast<float*>(A + c->lay.logits);
   c->cos_t = reinterpret_cast<float*>(A + c->lay.cos_t);
   c->sin_t = reinterpret_cast<float*>(A + c->lay.sin_t);
-  c->partial = reinterpret_cast<float*>(A + c->lay.partial);
-  c->counters = reinterpret_cast<unsigned*>(A + c->lay.counters);
+  c->mxq = A + c->lay.mxq;
+  c->mxd = reinterpret_cast<float*>(A + c->lay.mxd);
   c->st = reinterpret_cast<Status*>(A + c->lay.status);
   c->hist = reinterpret_cast<uint32_t*>(A + c->lay.hist);
 
@@ -728,6 +733,75 @@ GemvArgs gemv_base(nrc_ctx* c, int fmt, int K) {
   return a;
 }
 
+// One linear layer over nt tokens: x [nt][K] f32 (optionally RMS-normalised
+// with norm_w) times up to three weight matrices of one format. EPI_SWIGLU
+// takes gate = w[0] -> y[0] and up = w[1] (-> y[1] on the tensor-core path)
+// and leaves silu(gate)*up in y[0]; EPI_RESID adds rs * result into c->x.
+// Prefill chunks of more than 8 tokens over Q8_0 weights run on the tensor
+// cores (mma.cu), everything else on the streaming GEMV (gemv.cu); both are
+// bit-identical to the reference's scalar dots.
+struct Lin {
+  int fmt, K;
+  const float* x;
+  const float* norm_w;
+  const uint8_t* w[3];
+  float* y[3];
+  int rows[3];
+  int nseg;
+  int epi;
+};
+
+cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
+  cudaStream_t s = c->stream;
+  const bool pdl = c->pdl;
+  bool mma = nt > 8 && L.fmt == FMT_Q8_0 && L.K % 256 == 0 && L.K <= 16384;
+  for (int i = 0; i < L.nseg; i++) mma = mma && (reinterpret_cast<uintptr_t>(L.w[i]) & 15) == 0;
+  if (mma) {
+    int tiles = 0;
+    for (int i = 0; i < L.nseg; i++) tiles += (L.rows[i] + 127) / 128;
+    int NS, ntg;
+    mma_choose(tiles, nt, &NS, &ntg);
+    MmaActArgs qa{L.x, L.K, L.norm_w, c->eps, nt, L.K, NS, ntg, c->mxq, c->mxd};
+    cudaError_t e = mma_quant_act_run(qa, s, pdl);
+    if (e) return e;
+    MmaArgs m{};
+    for (int i = 0; i < L.nseg; i++) m.seg[i] = MmaSeg{L.w[i], L.y[i], L.rows[i], L.rows[i]};
+    m.nseg = L.nseg;
+    m.K = L.K;
+    m.xq = c->mxq;
+    m.xd = c->mxd;
+    m.nt = nt;
+    m.NS = NS;
+    m.ntg = ntg;
+    m.epi = L.epi == EPI_RESID ? EPI_RESID : EPI_STORE;
+    m.scale = 1.0f;
+    m.resid = c->x;
+    m.resid_ld = c->dim;
+    m.rs = c->rs;
+    m.err = &c->st->err;
+    if ((e = mma_q8_run(m, s, pdl))) return e;
+    if (L.epi == EPI_SWIGLU) return op_swiglu(L.y[0], L.y[1], (size_t)nt * L.rows[0], s);
+    return cudaSuccess;
+  }
+  GemvArgs a = gemv_base(c, L.fmt, L.K);
+  a.xf = L.x;
+  a.xf_ld = L.K;
+  a.norm_w = L.norm_w;
+  a.epi = L.epi;
+  for (int i = 0; i < L.nseg; i++) a.seg[i] = GemvSegArg{L.w[i], L.y[i], L.rows[i], L.rows[i]};
+  a.nseg = L.nseg;
+  if (L.epi == EPI_SWIGLU) {
+    a.pair = 1;
+    a.seg[1].y = nullptr;
+  }
+  if (L.epi == EPI_RESID) {
+    a.resid = c->x;
+    a.resid_ld = c->dim;
+    a.rs = c->rs;
+  }
+  return gemv_tokens(a, nt, L.K, s, pdl);
+}
+
 // Enqueue one forward step over nt tokens at positions st->pos .. +nt-1
 // (infer.rs:510-595 for nt == 1, infer.rs:601-750 otherwise).
 cudaError_t enqueue_step(nrc_ctx* c, int nt) {
@@ -738,7 +812,8 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
   if ((e = embed_run(ea, s, pdl))) return e;
   for (int l = 0; l < c->n_layers; l++) {
     const LayerW& w = c->L[l];
-    // QKV: one launch per weight format (rmsnorm + quantize in the prologue).
+    // QKV (infer.rs:527-531 / 620-637): rmsnorm + activation quantization fused
+    // into the consumer; one launch per weight format.
     {
       const uint8_t* ws[3] = {w.wq, w.wk, w.wv};
       const int fs[3] = {w.fq, w.fk, w.fv};
@@ -747,17 +822,20 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
       bool done[3] = {false, false, false};
       for (int i = 0; i < 3; i++) {
         if (done[i]) continue;
-        GemvArgs a = gemv_base(c, fs[i], c->dim);
-        a.xf = c->x;
-        a.xf_ld = c->dim;
-        a.norm_w = w.attn_norm;
-        a.epi = EPI_STORE;
+        Lin L{};
+        L.fmt = fs[i];
+        L.K = c->dim;
+        L.x = c->x;
+        L.norm_w = w.attn_norm;
+        L.epi = EPI_STORE;
         for (int j = i; j < 3; j++)
           if (!done[j] && fs[j] == fs[i]) {
-            a.seg[a.nseg++] = GemvSegArg{ws[j], ys[j], rows[j], rows[j]};
+            L.w[L.nseg] = ws[j];
+            L.y[L.nseg] = ys[j];
+            L.rows[L.nseg++] = rows[j];
             done[j] = true;
           }
-        if ((e = gemv_tokens(a, nt, c->dim, s, pdl))) return e;
+        if ((e = linear(c, L, nt))) return e;
       }
     }
     RopeArgs ra{c->q, c->k, c->v, w.q_norm, w.k_norm, c->eps, c->cos_t, c->sin_t, c->style,
@@ -765,56 +843,56 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
                 nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
     if ((e = rope_append_run(ra, s, pdl))) return e;
     AttnArgs aa{c->q, c->att, c->kc + (size_t)l * c->ctx * c->kv_dim, c->vc + (size_t)l * c->ctx * c->kv_dim,
-                c->partial, c->counters, c->att_scale, nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
+                c->att_scale, nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
     if ((e = attention_run(aa, s, pdl))) return e;
-    {
-      GemvArgs a = gemv_base(c, w.fo, c->att_dim);
-      a.xf = c->att;
-      a.xf_ld = c->att_dim;
-      a.seg[0] = GemvSegArg{w.wo, nullptr, c->dim, c->dim};
-      a.nseg = 1;
-      a.epi = EPI_RESID;
-      a.resid = c->x;
-      a.resid_ld = c->dim;
-      a.rs = c->rs;
-      if ((e = gemv_tokens(a, nt, c->att_dim, s, pdl))) return e;
+    {  // output projection + residual (infer.rs:574-575)
+      Lin L{};
+      L.fmt = w.fo;
+      L.K = c->att_dim;
+      L.x = c->att;
+      L.w[0] = w.wo;
+      L.rows[0] = c->dim;
+      L.nseg = 1;
+      L.epi = EPI_RESID;
+      if ((e = linear(c, L, nt))) return e;
     }
-    if (w.fg == w.fu) {
-      GemvArgs a = gemv_base(c, w.fg, c->dim);
-      a.xf = c->x;
-      a.xf_ld = c->dim;
-      a.norm_w = w.ffn_norm;
-      a.seg[0] = GemvSegArg{w.wg, c->g, c->ffn, c->ffn};
-      a.seg[1] = GemvSegArg{w.wu, nullptr, c->ffn, c->ffn};
-      a.nseg = 2;
-      a.pair = 1;
-      a.epi = EPI_SWIGLU;
-      if ((e = gemv_tokens(a, nt, c->dim, s, pdl))) return e;
-    } else {
-      GemvArgs a = gemv_base(c, w.fg, c->dim);
-      a.xf = c->x;
-      a.xf_ld = c->dim;
-      a.norm_w = w.ffn_norm;
-      a.seg[0] = GemvSegArg{w.wg, c->g, c->ffn, c->ffn};
-      a.nseg = 1;
-      a.epi = EPI_STORE;
-      if ((e = gemv_tokens(a, nt, c->dim, s, pdl))) return e;
-      a.fmt = w.fu;
-      a.seg[0] = GemvSegArg{w.wu, c->u, c->ffn, c->ffn};
-      if ((e = gemv_tokens(a, nt, c->dim, s, pdl))) return e;
-      if ((e = op_swiglu(c->g, c->u, (size_t)nt * c->ffn, s))) return e;
+    {  // SwiGLU MLP gate/up (infer.rs:577-581)
+      Lin L{};
+      L.fmt = w.fg;
+      L.K = c->dim;
+      L.x = c->x;
+      L.norm_w = w.ffn_norm;
+      L.w[0] = w.wg;
+      L.y[0] = c->g;
+      L.rows[0] = c->ffn;
+      L.nseg = 1;
+      L.epi = EPI_STORE;
+      if (w.fg == w.fu) {
+        L.w[1] = w.wu;
+        L.y[1] = c->u;
+        L.rows[1] = c->ffn;
+        L.nseg = 2;
+        L.epi = EPI_SWIGLU;
+        if ((e = linear(c, L, nt))) return e;
+      } else {
+        if ((e = linear(c, L, nt))) return e;
+        L.fmt = w.fu;
+        L.w[0] = w.wu;
+        L.y[0] = c->u;
+        if ((e = linear(c, L, nt))) return e;
+        if ((e = op_swiglu(c->g, c->u, (size_t)nt * c->ffn, s))) return e;
+      }
     }
-    {
-      GemvArgs a = gemv_base(c, w.fd, c->ffn);
-      a.xf = c->g;
-      a.xf_ld = c->ffn;
-      a.seg[0] = GemvSegArg{w.wd, nullptr, c->dim, c->dim};
-      a.nseg = 1;
-      a.epi = EPI_RESID;
-      a.resid = c->x;
-      a.resid_ld = c->dim;
-      a.rs = c->rs;
-      if ((e = gemv_tokens(a, nt, c->ffn, s, pdl))) return e;
+    {  // down projection + residual (infer.rs:582-583)
+      Lin L{};
+      L.fmt = w.fd;
+      L.K = c->ffn;
+      L.x = c->g;
+      L.w[0] = w.wd;
+      L.rows[0] = c->dim;
+      L.nseg = 1;
+      L.epi = EPI_RESID;
+      if ((e = linear(c, L, nt))) return e;
     }
   }
   // Final norm + classifier on the last token, fused greedy argmax (infer.rs:586-591, 740-746).

@@ -1,0 +1,544 @@
+// Batched Q8_0 GEMM (prefill, up to 64 tokens per pass) on sm_100a tensor
+// cores: tcgen05.mma kind::i8 with TMEM accumulators.
+//
+// Reference: kernels::matmul_q8 (crates/nr-tensor/src/kernels.rs:91-143) with the
+// scalar dot order of dot_q8_scalar (kernels.rs:72-82): for every (row, token)
+//   sum = 0; for each block b: sum += (i32 dot_b as f32 * d_w[b]) * d_x[b]
+// The tensor core produces each block's exact i32 dot (one K=32 MMA per block,
+// written to its own TMEM slot, never accumulated across blocks); the epilogue
+// warps apply the per-block scales with the reference's two roundings and add
+// the terms in block order, so outputs are bit-identical to the scalar path.
+//
+// CTA = 128 weight rows x NS tokens, 10 warps:
+//   warps 0-3  epilogue: TMEM lane = weight row; per block tcgen05.ld of the
+//              slot, exact scaling, running f32 sums in registers;
+//   warps 4-7  repack: raw Q8_0 rows (TMA-staged) -> UMMA K-major canonical
+//              int8 tiles + f32 row scales;
+//   warp 8     producer: 1-D bulk copies of raw weight rows, activation tiles
+//              and activation scales into a 2-stage ring (no multicast);
+//   warp 9     TMEM allocator and single-thread MMA issuer.
+// Every mbarrier wait is bounded (error word + clean exit, never a trap).
+#include <algorithm>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "mma.cuh"
+
+namespace nrc {
+namespace {
+
+constexpr int TM = 128;      // weight rows per tile (MMA M)
+constexpr int KB = 8;        // Q8_0 blocks per stage (K = 256; 272-byte row chunks are 16-byte aligned)
+constexpr int NST = 2;       // pipeline stages
+constexpr int NSLOT = 4;     // TMEM accumulator slots
+constexpr int NTHR = 320;
+constexpr int WP = 8, WM = 9;
+constexpr int EPI_WARPS = 4, REP_WARPS = 4;
+constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 12582912.0f = 1.5 * 2^23
+constexpr float MAGIC_F = 12582912.0f;
+
+struct Params {
+  const uint8_t* w[3];
+  float* yseg[3];
+  int rows[3];
+  int ldseg[3];
+  int tile_start[4];
+  int nseg;
+  int bpr, row_bytes;
+  const uint8_t* xq;
+  const float* xd;
+  int nt, NS, ntg;
+  int epi;
+  float scale;
+  float* resid;
+  int resid_ld;
+  float rs;
+  unsigned* err;
+  int off_raw, off_a, off_b, off_dw, off_dx, off_bar, stage_bytes;
+  uint32_t tmem_cols;
+};
+
+// ------------------------------------------------------------ tcgen05 helpers
+NRC_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+NRC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+NRC_DEV void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+NRC_DEV void tc_mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+NRC_DEV void tc_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+NRC_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// UMMA shared-memory descriptor, K-major, no swizzle: 8x16-byte core matrices,
+// `lbo` = byte distance between the two 16-byte K halves, `sbo` = between
+// consecutive 8-row groups; version 1 (sm_100).
+NRC_DEV uint64_t smem_desc(const void* p, uint32_t lbo, uint32_t sbo) {
+  const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
+  return a | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor: D s32, A/B signed int8, both K-major, N = ns, M = 128.
+NRC_DEV uint32_t idesc_i8(int ns) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(ns >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+}
+NRC_DEV uint32_t canon_off(int r, int c) { return (uint32_t)((r & 7) * 16 + (r >> 3) * 256 + c * 128); }
+
+template <int NS>
+__global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
+  uint64_t* full = bars;               // producer -> repack / epilogue (tx bytes)
+  uint64_t* aready = bars + NST;       // repack -> MMA (canonical A + row scales written)
+  uint64_t* empty = bars + 2 * NST;    // MMA commit + epilogue warps -> producer
+  uint64_t* mdone = bars + 3 * NST;    // MMA commit -> epilogue (slot written)
+  uint64_t* tfree = bars + 3 * NST + NSLOT;  // epilogue warps -> MMA (slot drained)
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x / p.ntg, tg = blockIdx.x % p.ntg;
+  int sg = 0;
+  while (sg + 1 < p.nseg && tile >= p.tile_start[sg + 1]) sg++;
+  const int row0 = (tile - p.tile_start[sg]) * TM;
+  const int nrows = min(TM, p.rows[sg] - row0);
+  const uint8_t* wseg = p.w[sg];
+  const int nstages = p.bpr / KB;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&aready[s], REP_WARPS);
+      mbar_init(&empty[s], 1 + EPI_WARPS);
+    }
+    for (int k = 0; k < NSLOT; k++) {
+      mbar_init(&mdone[k], 1);
+      mbar_init(&tfree[k], EPI_WARPS);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == WM) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                 "r"(p.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_trigger();
+  pdl_wait();  // activations (B) and the residual stream come from the previous kernel
+  const uint32_t tbase = tmem_base_sh;
+
+  auto st_raw = [&](int s) { return smem + p.off_raw + s * p.stage_bytes; };
+  auto st_a = [&](int s) { return smem + p.off_a + s * p.stage_bytes; };
+  auto st_b = [&](int s) { return smem + p.off_b + s * p.stage_bytes; };
+  auto st_dw = [&](int s) { return reinterpret_cast<float*>(smem + p.off_dw + s * p.stage_bytes); };
+  auto st_dx = [&](int s) { return reinterpret_cast<float*>(smem + p.off_dx + s * p.stage_bytes); };
+  auto fail = [&](unsigned bit) {
+    if (!abort_flag) {
+      abort_flag = 1;
+      atomicOr(p.err, bit);
+    }
+  };
+
+  if (warp == WP) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol = l2_evict_first();
+    const uint32_t raw_bytes = (uint32_t)nrows * KB * 34;
+    const uint32_t b_bytes = (uint32_t)KB * NS * 32;
+    const uint32_t dx_bytes = (uint32_t)KB * NS * 4;
+    int st = 0;
+    for (; st < nstages; st++) {
+      const int s = st % NST, u = st / NST;
+      if (u >= 1) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(&empty[s], (u - 1) & 1);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) fail(ERR_WAIT_EMPTY);
+      }
+      if (abort_flag) break;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], raw_bytes + b_bytes + dx_bytes);
+      __syncwarp();
+      for (int r = lane; r < nrows; r += 32) {
+        const uint8_t* src = wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * KB * 34;
+        bulk_g2s(st_raw(s) + r * KB * 34, src, KB * 34, &full[s], pol);
+      }
+      if (lane == 0) {
+        const size_t tile = ((size_t)tg * p.bpr + (size_t)st * KB);
+        bulk_g2s(st_b(s), p.xq + tile * NS * 32, b_bytes, &full[s], 0ull);
+        bulk_g2s(st_dx(s), p.xd + tile * NS, dx_bytes, &full[s], 0ull);
+      }
+    }
+    // Drain the copies of the last issued stages before exit.
+    if (lane == 0)
+      for (int k = st - 1; k >= 0 && k >= st - NST; k--)
+        if (!mbar_wait(&full[k % NST], (k / NST) & 1)) atomicOr(p.err, ERR_DRAIN);
+  } else if (warp >= EPI_WARPS && warp < EPI_WARPS + REP_WARPS) {
+    // -------------------------------------------------------------- repack
+    const int r = tid - EPI_WARPS * 32;  // weight row of this thread
+    for (int st = 0; st < nstages; st++) {
+      const int s = st % NST, u = st / NST;
+      const bool ok = !abort_flag && mbar_wait(&full[s], u & 1);
+      if (!ok) {
+        fail(ERR_WAIT_FULL);
+        break;
+      }
+      uint8_t* a = st_a(s);
+      float* dw = st_dw(s);
+      if (r < nrows) {
+        const uint8_t* src = st_raw(s) + r * KB * 34;
+#pragma unroll
+        for (int blk = 0; blk < KB; blk++) {
+          // Block blk of this row: d (2 bytes) + 32 int8 quants, 2-byte aligned.
+          const uint32_t* base = reinterpret_cast<const uint32_t*>(src + blk * 34 - ((blk & 1) ? 2 : 0));
+          uint32_t wv[9];
+#pragma unroll
+          for (int i = 0; i < 9; i++) wv[i] = base[i];
+          uint32_t q[8];
+          uint32_t dbits;
+          if ((blk & 1) == 0) {
+            dbits = wv[0] & 0xffffu;
+#pragma unroll
+            for (int k = 0; k < 8; k++) q[k] = __byte_perm(wv[k], wv[k + 1], 0x5432);
+          } else {
+            dbits = wv[0] >> 16;
+#pragma unroll
+            for (int k = 0; k < 8; k++) q[k] = wv[k + 1];
+          }
+          uint8_t* ab = a + blk * (TM * 32);
+          *reinterpret_cast<uint4*>(ab + canon_off(r, 0)) = make_uint4(q[0], q[1], q[2], q[3]);
+          *reinterpret_cast<uint4*>(ab + canon_off(r, 1)) = make_uint4(q[4], q[5], q[6], q[7]);
+          dw[blk * TM + r] = f16_to_f32(dbits);
+        }
+      } else {
+#pragma unroll
+        for (int blk = 0; blk < KB; blk++) {
+          uint8_t* ab = a + blk * (TM * 32);
+          *reinterpret_cast<uint4*>(ab + canon_off(r, 0)) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(ab + canon_off(r, 1)) = make_uint4(0, 0, 0, 0);
+          dw[blk * TM + r] = 0.0f;
+        }
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&aready[s]);
+    }
+  } else if (warp == WM) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(NS);
+      int issued = 0;  // blocks whose MMA was issued
+      for (int st = 0; st < nstages && !abort_flag; st++) {
+        const int s = st % NST, u = st / NST;
+        if (!mbar_wait(&aready[s], u & 1)) {
+          fail(ERR_WAIT_FULL);
+          break;
+        }
+        tc_fence_after();
+        for (int blk = 0; blk < KB; blk++) {
+          const int b = st * KB + blk;
+          const int slot = b % NSLOT;
+          if (b >= NSLOT && !mbar_wait(&tfree[slot], ((b / NSLOT) - 1) & 1)) {
+            fail(ERR_WAIT_EMPTY);
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = smem_desc(st_a(s) + blk * (TM * 32), 128, 256);
+          const uint64_t bd = smem_desc(st_b(s) + blk * (NS * 32), 128, 256);
+          tc_mma_i8(tbase + (uint32_t)(slot * NS), ad, bd, idesc, 0u);
+          tc_commit(&mdone[slot]);
+          issued = b + 1;
+        }
+        tc_commit(&empty[s]);  // stage's smem free once these MMAs completed
+      }
+      // Never release TMEM with an MMA in flight: wait (bounded) for the last commit.
+      if (issued > 0) {
+        const int b = issued - 1;
+        if (!mbar_wait(&mdone[b % NSLOT], (b / NSLOT) & 1)) atomicOr(p.err, ERR_DRAIN);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int r = tid;  // warps 0-3: TMEM lanes 0-127 = weight rows
+    float acc[NS];
+#pragma unroll
+    for (int i = 0; i < NS; i++) acc[i] = 0.0f;
+    const uint32_t lane_base = tbase + ((uint32_t)(warp * 32) << 16);
+    for (int st = 0; st < nstages && !abort_flag; st++) {
+      const int s = st % NST, u = st / NST;
+      if (!mbar_wait(&full[s], u & 1) || !mbar_wait(&aready[s], u & 1)) {
+        fail(ERR_WAIT_FULL);
+        break;
+      }
+      const float* dw = st_dw(s);
+      const float* dx = st_dx(s);
+      bool bad = false;
+      for (int blk = 0; blk < KB; blk++) {
+        const int b = st * KB + blk;
+        const int slot = b % NSLOT;
+        if (!mbar_wait(&mdone[slot], (b / NSLOT) & 1)) {
+          fail(ERR_WAIT_FULL);
+          bad = true;
+          break;
+        }
+        tc_fence_after();
+        const float d = dw[blk * TM + r];
+        const float negmd = -MAGIC_F * d;  // exact: d has <= 11 significant bits
+        const bool fin = isfinite(d);
+        const float* dxb = dx + blk * NS;
+#pragma unroll
+        for (int c0 = 0; c0 < NS; c0 += 16) {
+          uint32_t v[16];
+          tc_ld16(lane_base + (uint32_t)(slot * NS + c0), v);
+          tc_wait_ld();
+          if (c0 + 16 >= NS) {
+            // Slot drained: hand it back to the MMA issuer.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tfree[slot]);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; j += 2) {
+            // (acc as f32 * d_w) * d_x, then sum += term (kernels.rs:79).
+            // M + acc is exact (|acc| < 2^22), and fma(M + acc, d, -M*d)
+            // rounds acc*d once, exactly like the reference's multiply.
+            float2 t1;
+            const float fa = __uint_as_float(v[j] + MAGIC_BITS), fb = __uint_as_float(v[j + 1] + MAGIC_BITS);
+            if (fin) {
+              t1 = __ffma2_rn(make_float2(fa, fb), make_float2(d, d), make_float2(negmd, negmd));
+            } else {
+              t1 = make_float2(__fmul_rn(i2f((int)v[j]), d), __fmul_rn(i2f((int)v[j + 1]), d));
+            }
+            const float2 x2 = *reinterpret_cast<const float2*>(dxb + c0 + j);
+            const float2 t = __fmul2_rn(t1, x2);
+            float2 a2 = make_float2(acc[c0 + j], acc[c0 + j + 1]);
+            a2 = __fadd2_rn(a2, t);
+            acc[c0 + j] = a2.x;
+            acc[c0 + j + 1] = a2.y;
+          }
+        }
+      }
+      if (bad) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (!abort_flag && r < nrows) {
+      const int row = row0 + r;
+#pragma unroll
+      for (int n = 0; n < NS; n++) {
+        const int tok = tg * NS + n;
+        if (tok >= p.nt) break;
+        float sv = acc[n];
+        if (p.epi == EPI_RESID) {
+          float* dst = p.resid + (size_t)tok * p.resid_ld + row;
+          *dst = __fadd_rn(*dst, __fmul_rn(p.rs, sv));
+        } else {
+          if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
+          p.yseg[sg][(size_t)tok * p.ldseg[sg] + row] = sv;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == WM) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(p.tmem_cols) : "memory");
+  }
+}
+
+// ------------------------------------------------------------ activation quantization
+// One CTA (256 threads) per token: optional RMSNorm (the same reduction order
+// as the GEMV prologue, so both paths derive identical activations), then
+// q8::quantize per 32-value block into the canonical per-block tiles.
+__global__ void __launch_bounds__(256) k_mma_quant_act(const MmaActArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int n = blockIdx.x;  // token slot (0 .. ntg*NS - 1)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int bpr = a.K / 32;
+  const int tg = n / a.NS, nn = n % a.NS;
+  __shared__ float red[8];
+  if (n >= a.nt) {
+    for (int b = tid; b < bpr; b += 256) {
+      uint8_t* t = a.xq + ((size_t)tg * bpr + b) * a.NS * 32;
+      *reinterpret_cast<uint4*>(t + canon_off(nn, 0)) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(t + canon_off(nn, 1)) = make_uint4(0, 0, 0, 0);
+      a.xd[((size_t)tg * bpr + b) * a.NS + nn] = 0.0f;
+    }
+    return;
+  }
+  extern __shared__ float xrow[];  // the token's K values
+  const float* x = a.x + (size_t)n * a.x_ld;
+  for (int i = tid; i < a.K; i += 256) xrow[i] = x[i];
+  __syncthreads();
+  float sc = 1.0f;
+  if (a.norm_w) {
+    // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order.
+    if (tid == 0) {
+      float ss = 0.0f;
+#pragma unroll 8
+      for (int i = 0; i < a.K; i++) ss = __fadd_rn(ss, __fmul_rn(xrow[i], xrow[i]));
+      red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps)));
+    }
+    __syncthreads();
+    sc = red[0];
+  }
+  for (int b = warp; b < bpr; b += 8) {
+    float v = xrow[b * 32 + lane];
+    if (a.norm_w) v = __fmul_rn(__fmul_rn(v, sc), a.norm_w[b * 32 + lane]);
+    const float amax = warp_max(fabsf(v));
+    const uint16_t dbits = f32_to_f16(__fdiv_rn(amax, 127.0f));
+    const float d = f16_to_f32(dbits);
+    const float inv = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    const float xs = __fmul_rn(v, inv);
+    const float r = xs >= 0.0f ? __fadd_rn(xs, 0.5f) : __fsub_rn(xs, 0.5f);
+    int q = rust_f2i(r);
+    q = q < -127 ? -127 : (q > 127 ? 127 : q);
+    uint8_t* t = a.xq + ((size_t)tg * bpr + b) * a.NS * 32;
+    t[canon_off(nn, lane >> 4) + (lane & 15)] = (uint8_t)(int8_t)q;
+    if (lane == 0) a.xd[((size_t)tg * bpr + b) * a.NS + nn] = d;
+  }
+}
+
+// Pre-quantized Q8_0 activation blocks [nt][bpr] -> canonical per-block tiles.
+__global__ void k_mma_pack_q8(const uint8_t* __restrict__ x, int nt, int bpr, int NS, int ntg, uint8_t* xq,
+                              float* xd) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // (token slot, block)
+  if (i >= NS * ntg * bpr) return;
+  const int n = i / bpr, b = i % bpr;
+  const int tg = n / NS, nn = n % NS;
+  uint8_t* t = xq + ((size_t)tg * bpr + b) * NS * 32;
+  uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float d = 0.0f;
+  if (n < nt) {
+    const uint8_t* s = x + ((size_t)n * bpr + b) * 34;
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      w[k] = (uint32_t)s[2 + 4 * k] | ((uint32_t)s[3 + 4 * k] << 8) | ((uint32_t)s[4 + 4 * k] << 16) |
+             ((uint32_t)s[5 + 4 * k] << 24);
+    d = f16_to_f32((uint32_t)s[0] | ((uint32_t)s[1] << 8));
+  }
+  *reinterpret_cast<uint4*>(t + canon_off(nn, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(t + canon_off(nn, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+  xd[((size_t)tg * bpr + b) * NS + nn] = d;
+}
+
+cudaError_t launch(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, void** args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace
+
+cudaError_t mma_quant_act_run(const MmaActArgs& a, cudaStream_t s, bool pdl) {
+  if (a.K % 256 || (a.NS != 16 && a.NS != 32 && a.NS != 64) || a.nt > a.NS * a.ntg) return cudaErrorInvalidValue;
+  MmaActArgs aa = a;
+  void* args[] = {&aa};
+  const size_t smem = (size_t)a.K * 4;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    cudaFuncSetAttribute((const void*)k_mma_quant_act, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    attr_done[dev] = true;
+  }
+  if (smem > 64 * 1024) return cudaErrorInvalidValue;
+  return launch((const void*)k_mma_quant_act, dim3(a.NS * a.ntg), dim3(256), smem, s, pdl, args);
+}
+
+cudaError_t mma_pack_q8_run(const uint8_t* x, int nt, int K, int NS, int ntg, uint8_t* xq, float* xd, cudaStream_t s) {
+  if (K % 256 || nt > NS * ntg) return cudaErrorInvalidValue;
+  const int bpr = K / 32;
+  const int total = NS * ntg * bpr;
+  k_mma_pack_q8<<<(total + 255) / 256, 256, 0, s>>>(x, nt, bpr, NS, ntg, xq, xd);
+  return cudaGetLastError();
+}
+
+cudaError_t mma_q8_run(const MmaArgs& a, cudaStream_t s, bool pdl) {
+  if (a.K % 256 || (a.NS != 16 && a.NS != 32 && a.NS != 64) || a.nseg < 1 || a.nseg > 3)
+    return cudaErrorInvalidValue;
+  Params p{};
+  int tiles = 0;
+  for (int i = 0; i < a.nseg; i++) {
+    if (reinterpret_cast<uintptr_t>(a.seg[i].w) & 15) return cudaErrorInvalidValue;
+    p.w[i] = static_cast<const uint8_t*>(a.seg[i].w);
+    p.yseg[i] = a.seg[i].y;
+    p.rows[i] = a.seg[i].rows;
+    p.ldseg[i] = a.seg[i].ld > 0 ? a.seg[i].ld : a.seg[i].rows;
+    p.tile_start[i] = tiles;
+    tiles += (a.seg[i].rows + TM - 1) / TM;
+  }
+  p.tile_start[a.nseg] = tiles;
+  p.nseg = a.nseg;
+  p.bpr = a.K / 32;
+  p.row_bytes = p.bpr * 34;
+  p.xq = a.xq;
+  p.xd = a.xd;
+  p.nt = a.nt;
+  p.NS = a.NS;
+  p.ntg = a.ntg;
+  p.epi = a.epi;
+  p.scale = a.scale;
+  p.resid = a.resid;
+  p.resid_ld = a.resid_ld;
+  p.rs = a.rs;
+  p.err = a.err;
+  // Stage layout: A canonical (1024-aligned) | raw rows | B | dw | dx.
+  size_t o = 0;
+  p.off_a = (int)o;
+  o += (size_t)KB * TM * 32;
+  p.off_raw = (int)o;
+  o += (size_t)TM * KB * 34;
+  o = (o + 127) & ~(size_t)127;
+  p.off_b = (int)o;
+  o += (size_t)KB * a.NS * 32;
+  p.off_dw = (int)o;
+  o += (size_t)KB * TM * 4;
+  p.off_dx = (int)o;
+  o += (size_t)KB * a.NS * 4;
+  o = (o + 1023) & ~(size_t)1023;
+  p.stage_bytes = (int)o;
+  p.off_bar = (int)(o * NST);
+  const size_t smem = o * NST + (3 * NST + 2 * NSLOT) * 8;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(NSLOT * a.NS)) cols <<= 1;
+  p.tmem_cols = cols;
+  const void* fn = a.NS == 16 ? (const void*)k_mma_q8<16> : (a.NS == 32 ? (const void*)k_mma_q8<32> : (const void*)k_mma_q8<64>);
+  static bool attr_done[64][3] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int ki = a.NS == 16 ? 0 : (a.NS == 32 ? 1 : 2);
+  if (dev < 64 && !attr_done[dev][ki]) {
+    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
+    attr_done[dev][ki] = true;
+  }
+  if (smem > 225 * 1024) return cudaErrorInvalidValue;
+  if (tiles == 0) return cudaSuccess;
+  void* args[] = {&p};
+  return launch(fn, dim3(tiles * a.ntg), dim3(NTHR), smem, s, pdl, args);
+}
+
+}  // namespace nrc

@@ -2,6 +2,7 @@
 // (crates/nr-tensor/src/{q8,kquant,f16,vec,rope}.rs). The fused forward path
 // uses the same arithmetic inside its GEMV prologues/epilogues and attention.
 #include "common.cuh"
+#include "expf_cr.cuh"
 #include "ops.cuh"
 
 namespace nrc {
@@ -172,34 +173,48 @@ NRC_DEV float block_max(float m, float* red) {
   return t;
 }
 
-// vec::rmsnorm (vec.rs:4-14), one CTA per row.
+// Sequential f32 sum of v[0..n) in index order (the reference's `+=` loops).
+NRC_DEV float seq_sum_sq(const float* v, int n) {
+  float s = 0.0f;
+#pragma unroll 8
+  for (int i = 0; i < n; i++) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
+  return s;
+}
+
+// vec::rmsnorm (vec.rs:4-14), one CTA per row: the sum of squares runs in
+// index order (one thread), the scaling in parallel.
 __global__ void k_rmsnorm(float* __restrict__ out, const float* __restrict__ x, const float* __restrict__ w,
                           int n, float eps) {
-  __shared__ float red[32];
+  __shared__ float scale_sh;
   const float* xr = x + (size_t)blockIdx.x * n;
   float* orow = out + (size_t)blockIdx.x * n;
-  float s = 0.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) s = __fadd_rn(s, __fmul_rn(xr[i], xr[i]));
-  const float ss = block_sum(s, red);
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+  if (threadIdx.x == 0) {
+    const float ss = seq_sum_sq(xr, n);
+    scale_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+  }
+  __syncthreads();
+  const float scale = scale_sh;
   for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
 }
 
-// vec::softmax (vec.rs:30-41), one CTA per row, in place.
+// vec::softmax (vec.rs:30-41), one CTA per row, in place: max (order-free),
+// exponentials in parallel, their sum in index order, then the scaling.
 __global__ void k_softmax(float* __restrict__ x, int n) {
   __shared__ float red[32];
+  __shared__ float inv_sh;
   float* xr = x + (size_t)blockIdx.x * n;
   float m = -INFINITY;
   for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, xr[i]);
   m = block_max(m, red);
-  float s = 0.0f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float e = expf(__fsub_rn(xr[i], m));
-    xr[i] = e;
-    s = __fadd_rn(s, e);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = expf_cr(__fsub_rn(xr[i], m));
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.0f;
+    for (int i = 0; i < n; i++) s = __fadd_rn(s, xr[i]);
+    inv_sh = __fdiv_rn(1.0f, s);
   }
-  const float sum = block_sum(s, red);
-  const float inv = __fdiv_rn(1.0f, sum);
+  __syncthreads();
+  const float inv = inv_sh;
   for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __fmul_rn(xr[i], inv);
 }
 
@@ -208,7 +223,29 @@ __global__ void k_swiglu(float* __restrict__ g, const float* __restrict__ u, siz
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const float x = g[i];
-  g[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf(-x))), u[i]);
+  g[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf_cr(-x))), u[i]);
+}
+
+// Elementwise correctly rounded expf (checked against the CPU oracle bit for bit).
+__global__ void k_expf(const float* __restrict__ x, float* __restrict__ y, size_t n) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = expf_cr(x[i]);
+}
+
+// Hash of expf_cr over every binary32 input, 2^20 inputs per chunk (same
+// mixing as the oracle's exhaustive check), one thread per chunk, one warp
+// per CTA so the chunks spread over every SM.
+__global__ void k_expf_hash(unsigned long long* out, int chunk0, int nchunks) {
+  const int c = chunk0 + blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= chunk0 + nchunks) return;
+  unsigned long long h = 0;
+  for (uint32_t i = 0; i < (1u << 20); i++) {
+    const uint32_t bits = ((uint32_t)c << 20) | i;
+    const uint32_t y = __float_as_uint(expf_cr(__uint_as_float(bits)));
+    h ^= y + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+    h *= 0xBF58476D1CE4E5B9ull;
+  }
+  out[c - chunk0] = h;
 }
 
 // vec::argmax (vec.rs:80-90): packed (value, index) keys, max over the grid.
@@ -278,6 +315,14 @@ cudaError_t op_softmax(float* x, size_t n, size_t rows, cudaStream_t s) {
 }
 cudaError_t op_swiglu(float* g, const float* u, size_t n, cudaStream_t s) {
   if (n) k_swiglu<<<blocks_for(n, 256), 256, 0, s>>>(g, u, n);
+  return cudaGetLastError();
+}
+cudaError_t op_expf(const float* x, float* y, size_t n, cudaStream_t s) {
+  if (n) k_expf<<<blocks_for(n, 256), 256, 0, s>>>(x, y, n);
+  return cudaGetLastError();
+}
+cudaError_t op_expf_hash(unsigned long long* out, int chunk0, int nchunks, cudaStream_t s) {
+  if (nchunks > 0) k_expf_hash<<<(nchunks + 31) / 32, 32, 0, s>>>(out, chunk0, nchunks);
   return cudaGetLastError();
 }
 cudaError_t op_argmax(const float* x, size_t n, unsigned long long* key_scratch, uint32_t* out, cudaStream_t s) {

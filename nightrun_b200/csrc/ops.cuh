@@ -17,6 +17,8 @@ cudaError_t op_rmsnorm(float* out, const float* x, const float* w, size_t n, siz
 cudaError_t op_softmax(float* x, size_t n, size_t rows, cudaStream_t s);
 cudaError_t op_swiglu(float* g, const float* u, size_t n, cudaStream_t s);
 cudaError_t op_argmax(const float* x, size_t n, unsigned long long* key_scratch, uint32_t* out, cudaStream_t s);
+cudaError_t op_expf(const float* x, float* y, size_t n, cudaStream_t s);
+cudaError_t op_expf_hash(unsigned long long* out, int chunk0, int nchunks, cudaStream_t s);
 
 // Position-dependent kernels of the forward pass. Positions are read from
 // device memory (pos_dev[0] + token index) so a captured CUDA graph replays
@@ -43,13 +45,14 @@ struct AttnArgs {
   float* out;      // [nt][att_dim]
   const uint16_t* kcache;
   const uint16_t* vcache;
-  float* partial;      // scratch [nt][n_heads][max_splits][head_dim + 2]
-  unsigned* counters;  // [nt][n_kv_heads], zero between launches
   float scale;
   int nt, n_heads, n_kv_heads, head_dim, ctx;
   const uint32_t* pos_dev;
 };
-constexpr int ATTN_SPLIT = 128;
+// Shared memory of one attention CTA (its score rows hold `ctx` positions);
+// contexts needing more than ATTN_MAX_SMEM are rejected at context creation.
+constexpr size_t ATTN_MAX_SMEM = 200 * 1024;
+size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx);
 cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl);
 
 // Embedding rows (QMat::dequant_row, infer.rs:37-56) times embed_scale for nt

@@ -109,6 +109,16 @@ def swiglu(gate, up, stream=None):
     check(lib().nrc_swiglu(_ptr(gate), _ptr(up), gate.numel(), _stream(stream)))
 
 
+def expf(x, out, stream=None):
+    """The expf of vec.rs:34,47 / sample.rs:70, correctly rounded, elementwise."""
+    check(lib().nrc_expf(_ptr(x), _ptr(out), x.numel(), _stream(stream)))
+
+
+def expf_hash(out, chunk0, nchunks, stream=None):
+    """Per-chunk hashes of expf over every binary32 input (2^20 inputs per chunk)."""
+    check(lib().nrc_expf_hash(_ptr(out), chunk0, nchunks, _stream(stream)))
+
+
 def argmax(x, stream=None):
     """vec::argmax (vec.rs:80-90): index of the first maximum (host int)."""
     out = torch.zeros(1, dtype=torch.int32, device=x.device)

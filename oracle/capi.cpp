@@ -3,6 +3,7 @@
 // named in its comment.
 #include <vector>
 
+#include "expf_cr.h"
 #include "model.h"
 #include "synth.h"
 
@@ -15,6 +16,29 @@ void or_set_mode(int fast_path, int fast_f16) {  // cpu.rs:46-55
   g_fast_f16 = fast_f16 != 0;
 }
 void or_pool_start(int threads) { pool_start(threads); }
+
+// expf as called by vec.rs:34,47 and sample.rs:70 (correctly rounded).
+void or_expf(const float* x, float* y, size_t n) {
+  for (size_t i = 0; i < n; i++) y[i] = expf_cr(x[i]);
+}
+// Per-chunk hashes of expf_cr's output bits over every binary32 input, 2^20
+// inputs per chunk (the mixing of oracle/check_expf.cpp).
+void or_expf_hash(uint64_t* out, int chunk0, int nchunks) {
+  for (int c = chunk0; c < chunk0 + nchunks; c++) {
+    uint64_t h = 0;
+    for (uint32_t i = 0; i < (1u << 20); i++) {
+      const uint32_t bits = ((uint32_t)c << 20) | i;
+      float x, y;
+      memcpy(&x, &bits, 4);
+      y = expf_cr(x);
+      uint32_t yb;
+      memcpy(&yb, &y, 4);
+      h ^= yb + 0x9E3779B97F4A7C15ull + (h << 6) + (h >> 2);
+      h *= 0xBF58476D1CE4E5B9ull;
+    }
+    out[c - chunk0] = h;
+  }
+}
 int or_pool_threads() { return pool_threads(); }
 
 void or_f16_to_f32(const uint16_t* in, float* out, size_t n) {

@@ -6,6 +6,7 @@
 #include <vector>
 
 #include "model.h"
+#include "expf_cr.h"
 
 namespace oracle {
 
@@ -539,7 +540,7 @@ uint32_t sampler_sample(Sampler* s, const float* logits, size_t n) {
   }
   float max = hv[0], sum = 0.0f, probs[TOP_K];
   for (int i = 0; i < TOP_K; i++) {
-    probs[i] = expf((hv[i] - max) / s->temperature);
+    probs[i] = expf_cr((hv[i] - max) / s->temperature);  // libm::expf (sample.rs:70)
     sum += probs[i];
   }
   float cut = s->top_p * sum, cum = 0.0f;

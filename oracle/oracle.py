@@ -68,6 +68,7 @@ class Oracle:
         P, S, F, I, U32, U64 = C.c_void_p, C.c_size_t, C.c_float, C.c_int, C.c_uint32, C.c_uint64
         sig = {
             "or_set_mode": (None, [I, I]), "or_pool_start": (None, [I]), "or_pool_threads": (I, []),
+            "or_expf": (None, [P, P, S]), "or_expf_hash": (None, [P, I, I]),
             "or_f16_to_f32": (None, [P, P, S]), "or_f32_to_f16": (None, [P, P, S]),
             "or_q8_quantize": (None, [P, S, P]), "or_q8_dequantize": (None, [P, S, P]),
             "or_quantize_q8k": (None, [P, S, P]), "or_dequant_q4k": (None, [P, S, P]),
@@ -194,6 +195,17 @@ class Oracle:
         w = np.ascontiguousarray(w, np.float32)
         self.L.or_rmsnorm_inplace(self._p(x), self._p(w), x.size, eps)
         return x
+
+    def expf(self, x):
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.empty_like(x)
+        self.L.or_expf(self._p(x), self._p(y), x.size)
+        return y
+
+    def expf_hash(self, chunk0, nchunks):
+        out = np.empty(nchunks, np.uint64)
+        self.L.or_expf_hash(self._p(out), chunk0, nchunks)
+        return out
 
     def softmax(self, x):
         x = np.array(x, np.float32)

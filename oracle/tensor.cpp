@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "oracle.h"
+#include "expf_cr.h"
 
 namespace oracle {
 
@@ -829,7 +830,7 @@ void softmax(float* x, size_t n) {
   for (size_t i = 0; i < n; i++) max = rust_max(max, x[i]);
   float sum = 0.0f;
   for (size_t i = 0; i < n; i++) {
-    x[i] = expf(x[i] - max);
+    x[i] = expf_cr(x[i] - max);  // libm::expf (vec.rs:34) -> correctly rounded expf
     sum += x[i];
   }
   float inv = 1.0f / sum;
@@ -839,7 +840,7 @@ void softmax(float* x, size_t n) {
 void swiglu(float* gate, const float* up, size_t n) {
   for (size_t i = 0; i < n; i++) {
     float x = gate[i];
-    float silu = x / (1.0f + expf(-x));
+    float silu = x / (1.0f + expf_cr(-x));  // libm::expf (vec.rs:47)
     gate[i] = silu * up[i];
   }
 }

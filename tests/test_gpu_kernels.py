@@ -2,10 +2,13 @@
 
 Integer / byte work (quantizers, f16 conversion, dequantization) and the
 matvec/matmul outputs must be bit-identical to the reference's scalar code
-(the GEMV keeps the scalar summation order); norm/softmax/swiglu use expf and
-parallel reductions and are held to 1e-6 relative (the reference's own
-tolerance, crates/nr-tensor/tests/kernels.rs:130-165).
+(the GEMV and the tensor-core GEMM keep the scalar summation order);
+rmsnorm/softmax/swiglu keep the reference's sequential sums and a correctly
+rounded expf, so they are bit-identical too (stricter than the reference's own
+1e-6 relative tolerance, crates/nr-tensor/tests/kernels.rs:130-165).
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -164,6 +167,22 @@ def test_matmul_bit_exact_and_equals_matvec(K, orc, fmt, batch):
         assert one.tobytes() == got[b].tobytes()
 
 
+@pytest.mark.parametrize("shape", [(300, 2048), (130, 512), (2048, 2048), (64, 8192), (128, 256), (1, 768)])
+@pytest.mark.parametrize("batch", [9, 16, 17, 33, 64, 100])
+def test_matmul_q8_tensor_core_bit_exact(K, orc, shape, batch):
+    """Q8_0 with cols % 256 == 0 and batch > 8 runs on tcgen05 (kind::i8, one
+    MMA per block, scales applied in block order by the epilogue)."""
+    rows, cols = shape
+    w = make_weights(orc, "q8_0", rows, cols, 40 + rows, adversarial=(batch % 2 == 1))
+    xs = make_acts(orc, "q8_0", cols, 41 + batch, batch)
+    ref = orc.matmul("q8_0", w, xs, rows, cols, batch)
+    got = gpu_matmul(K, "q8_0", w, xs, rows, cols, batch)
+    if got.tobytes() != ref.tobytes():
+        bad = np.argwhere(got.view(np.uint32) != ref.view(np.uint32))
+        raise AssertionError(f"{rows}x{cols} b{batch}: {len(bad)} differ, first {bad[:4].tolist()}, "
+                             f"max diff {np.nanmax(np.abs(got - ref))}")
+
+
 @pytest.mark.parametrize("fmt", ["q8_0", "q4k", "q6k"])
 @pytest.mark.parametrize("offset", [2, 4, 6, 8, 14])
 def test_matvec_unaligned_weights(K, orc, fmt, offset):
@@ -207,22 +226,62 @@ def test_matvec_empty_and_invalid(K):
     assert torch.all(y == 0)
 
 
-def test_rmsnorm_softmax_swiglu(K, orc):
-    rng = Rng(9)
-    x = rng.vec(2048) * F(3)
-    w = rng.vec(2048) + F(1)
-    out = torch.empty(2048, dtype=torch.float32, device="cuda")
+@pytest.mark.parametrize("n", [1, 31, 256, 2048, 8192, 9728])
+def test_rmsnorm_softmax_swiglu_bit_exact(K, orc, n):
+    rng = Rng(9 + n)
+    x = rng.vec(n) * F(3)
+    w = rng.vec(n) + F(1)
+    out = torch.empty(n, dtype=torch.float32, device="cuda")
     K.rmsnorm(out, dev(x), dev(w), 1e-5)
-    ref = orc.rmsnorm(x, w, 1e-5)
-    np.testing.assert_allclose(out.cpu().numpy(), ref, rtol=1e-6, atol=1e-7)
-    s = rng.vec(1000) * F(8)
+    assert host_bytes(out) == orc.rmsnorm(x, w, 1e-5).tobytes()
+    s = rng.vec(n) * F(8)
     st = dev(s)
     K.softmax(st)
-    np.testing.assert_allclose(st.cpu().numpy(), orc.softmax(s), rtol=1e-6, atol=1e-8)
-    g, u = rng.vec(4096) * F(6), rng.vec(4096)
+    assert host_bytes(st) == orc.softmax(s).tobytes()
+    g, u = rng.vec(n) * F(6), rng.vec(n)
     gt = dev(g)
     K.swiglu(gt, dev(u))
-    np.testing.assert_allclose(gt.cpu().numpy(), orc.swiglu(g, u), rtol=1e-6, atol=1e-7)
+    assert host_bytes(gt) == orc.swiglu(g, u).tobytes()
+
+
+def test_rmsnorm_softmax_rows(K, orc):
+    rows, n = 5, 1000
+    x = Rng(3).vec(rows * n) * F(4)
+    w = Rng(4).vec(n)
+    out = torch.empty(rows * n, dtype=torch.float32, device="cuda")
+    K.rmsnorm(out, dev(x), dev(w), 1e-6, rows=rows)
+    ref = np.concatenate([orc.rmsnorm(x[r * n:(r + 1) * n], w, 1e-6) for r in range(rows)])
+    assert host_bytes(out) == ref.tobytes()
+    st = dev(x)
+    K.softmax(st, rows=rows)
+    ref = np.concatenate([orc.softmax(x[r * n:(r + 1) * n]) for r in range(rows)])
+    assert host_bytes(st) == ref.tobytes()
+
+
+def test_expf_elementwise_matches_oracle(K, orc):
+    r = np.random.default_rng(11)
+    x = np.concatenate([
+        r.integers(0, 2 ** 32, 1 << 20, dtype=np.uint64).astype(np.uint32).view(np.float32),
+        r.uniform(-104.0, 89.0, 1 << 20).astype(np.float32),
+        np.array([0.0, -0.0, np.inf, -np.inf, np.nan, 88.72283, 88.72284, -87.33655, -103.97208, -103.97209,
+                  1e-8, -1e-8], np.float32),
+    ])
+    y = torch.empty(x.size, dtype=torch.float32, device="cuda")
+    K.expf(dev(x), y)
+    got, ref = y.cpu().numpy(), orc.expf(x)
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)
+    assert got[~nan].tobytes() == ref[~nan].tobytes()
+
+
+def test_expf_every_binary32_input(K):
+    """Hashes of the device expf over all 2^32 inputs equal the oracle's, whose
+    values were checked against long-double expl at generation time."""
+    gold = np.fromfile(os.path.join(os.path.dirname(__file__), "golden", "expf_cr_hashes.bin"), np.uint64)
+    out = torch.zeros(gold.size, dtype=torch.int64, device="cuda")
+    K.expf_hash(out, 0, gold.size)
+    K.sync_check()
+    assert np.array_equal(out.cpu().numpy().view(np.uint64), gold)
 
 
 def test_argmax_first_max_and_edges(K):
