@@ -96,7 +96,9 @@ namespace nrc {
 __constant__ const double EXPCR_T_DEV[128] = {EXPCR_TABLE};
 
 NRC_DEV float expf_cr(float xf) {
-  if (xf != xf) return xf + xf;
+  // NaN: the quieted input, sign and payload kept (what x + x gives on the
+  // x86 host the reference runs on; GPU arithmetic would return a canonical NaN).
+  if (xf != xf) return __uint_as_float(__float_as_uint(xf) | 0x00400000u);
   if (xf > 88.72283172607421875f) return __int_as_float(0x7f800000);
   if (xf < -110.0f) return 0.0f;
   const double x = (double)xf;

@@ -322,12 +322,12 @@ __global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Para
             } else {
               t1 = make_float2(__fmul_rn(i2f((int)v[j]), d), __fmul_rn(i2f((int)v[j + 1]), d));
             }
+            // The product and the sum stay two roundings: the packed
+            // __fmul2_rn/__fadd2_rn pair is contracted into one FFMA2 by the
+            // compiler, the scalar _rn intrinsics never are.
             const float2 x2 = *reinterpret_cast<const float2*>(dxb + c0 + j);
-            const float2 t = __fmul2_rn(t1, x2);
-            float2 a2 = make_float2(acc[c0 + j], acc[c0 + j + 1]);
-            a2 = __fadd2_rn(a2, t);
-            acc[c0 + j] = a2.x;
-            acc[c0 + j + 1] = a2.y;
+            acc[c0 + j] = __fadd_rn(acc[c0 + j], __fmul_rn(t1.x, x2.x));
+            acc[c0 + j + 1] = __fadd_rn(acc[c0 + j + 1], __fmul_rn(t1.y, x2.y));
           }
         }
       }
