@@ -70,6 +70,25 @@ int nrc_matvec_q8_0(float* y, const void* w, const void* x, size_t rows, size_t 
 /* kernels::matmul_q8 (kernels.rs:91-143): y is [batch][rows], xs is [batch][cols/32]. */
 int nrc_matmul_q8_0(float* y, const void* w, const void* xs, size_t rows, size_t cols, size_t batch,
                     void* stream);
+/* nrc_matmul_q8_0 that allocates nothing. No counterpart in the reference:
+ * kernels::matmul_q8 (kernels.rs:91-143) needs no memory of its own on the CPU,
+ * while the device version's tensor-core path stages activation tiles. This
+ * variant keeps them in a static device array of NRC_NOALLOC_SCRATCH_BYTES
+ * (error word, 64 tokens x NRC_NOALLOC_MAX_COLS int8 tiles, their f32
+ * scales), so callers without an allocator can use it. Results are
+ * bit-identical to nrc_matmul_q8_0.
+ *  - cols > NRC_NOALLOC_MAX_COLS is rejected with NRC_ERR_INVALID.
+ *  - Only the error word must start at zero; every call clears it itself.
+ *  - The first call on a device resolves the array's address
+ *    (cudaGetSymbolAddress) and sets kernel attributes: make it outside any
+ *    stream capture.
+ *  - Calls overlapping in time on one device (several streams or threads)
+ *    race on the array: serialize them.
+ *  - Returns after its kernels finished (it reads the error word back). */
+#define NRC_NOALLOC_MAX_COLS 16384
+#define NRC_NOALLOC_SCRATCH_BYTES (256 + 64 * NRC_NOALLOC_MAX_COLS + 64 * (NRC_NOALLOC_MAX_COLS / 32) * 4)
+int nrc_matmul_q8_0_noalloc(float* y, const void* w, const void* xs, size_t rows, size_t cols, size_t batch,
+                            void* stream);
 /* kquant::matvec_q4k / matvec_q6k (kquant.rs:536-564), Q8_K activations;
  * bit-identical to dot_q4k_scalar / dot_q6k_scalar (kquant.rs:192-250). */
 int nrc_matvec_q4k(float* y, const void* w, const void* x, size_t rows, size_t cols, void* stream);

@@ -15,6 +15,7 @@ ERRORS = {
     -20: "CTX_FULL", -21: "BAD_BATCH", -22: "BAD_TOKEN",
 }
 MAX_BATCH = 64
+NOALLOC_MAX_COLS = 16384
 
 
 class NrcError(RuntimeError):
@@ -70,6 +71,7 @@ SIGNATURES = [
     ("nrc_dequant_q6k", I, [P, P, S, P]),
     ("nrc_matvec_q8_0", I, [P, P, P, S, S, P]),
     ("nrc_matmul_q8_0", I, [P, P, P, S, S, S, P]),
+    ("nrc_matmul_q8_0_noalloc", I, [P, P, P, S, S, S, P]),
     ("nrc_matvec_q4k", I, [P, P, P, S, S, P]),
     ("nrc_matvec_q6k", I, [P, P, P, S, S, P]),
     ("nrc_matmul_q4k", I, [P, P, P, S, S, S, P]),

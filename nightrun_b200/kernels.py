@@ -64,6 +64,12 @@ def matmul_q8(y, w, xs, rows, cols, batch, stream=None):
     check(lib().nrc_matmul_q8_0(_ptr(y), _ptr(w), _ptr(xs), rows, cols, batch, _stream(stream)))
 
 
+def matmul_q8_noalloc(y, w, xs, rows, cols, batch, stream=None):
+    """matmul_q8 through the entry point that allocates nothing (static device
+    scratch, cols <= 16384, synchronous); same results as matmul_q8."""
+    check(lib().nrc_matmul_q8_0_noalloc(_ptr(y), _ptr(w), _ptr(xs), rows, cols, batch, _stream(stream)))
+
+
 def matvec_q4k(y, w, x, rows, cols, stream=None):
     """kquant::matvec_q4k (kquant.rs:563)."""
     check(lib().nrc_matvec_q4k(_ptr(y), _ptr(w), _ptr(x), rows, cols, _stream(stream)))

@@ -76,3 +76,11 @@ def test_invalid_arguments_rejected_without_gpu(L):
     assert L.nrc_quantize_q8k(None, None, 100, None) == -1
     assert L.nrc_ctx_forward(None, 0, None, None) == -1
     assert b"null" in L.nrc_last_error()
+
+
+def test_noalloc_limits_checked_before_any_device_call(L):
+    # Argument validation of the no-allocation matmul runs on the host only.
+    fake = C.c_void_p(0x1000)
+    assert L.nrc_matmul_q8_0_noalloc(fake, fake, fake, 4, 16384 + 32, 2, None) == -1
+    assert b"scratch" in L.nrc_last_error()
+    assert L.nrc_matmul_q8_0_noalloc(fake, fake, fake, 4, 33, 2, None) == -1
