@@ -109,8 +109,8 @@ class ClockSampler:
 
 
 def launches_per_step(cfg):
-    # embed + per layer (QKV, rope/append, attention, wo, gate/up, down) + classifier + finish
-    return 1 + cfg["n_layers"] * 6 + 2
+    # embed + per layer (QKV, attention with RoPE/KV append fused, wo, gate/up, down) + classifier + finish
+    return 1 + cfg["n_layers"] * 5 + 2
 
 
 def cpu_decode(blob, cfg, steps, warmup, threads):

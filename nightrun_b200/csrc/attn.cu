@@ -10,16 +10,78 @@
 // so results are bit-identical to the scalar reference, and every per-token
 // result depends only on that token's position: batched prefill and
 // token-by-token decode agree bit for bit.
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "expf_cr.cuh"
 #include "ops.cuh"
+#include "seqsum.cuh"
 
 namespace nrc {
 namespace {
 
-constexpr int ATT_THREADS = 256;
-constexpr int VCHUNK = 128;  // V rows staged per pass
+constexpr int ATT_THREADS = 128;  // >= head_dim: one V output chain per thread
+constexpr int ATT_VCH = 128;      // V rows staged per pass
 
+NRC_DEV float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }  // exact
+
+// One warp: a head vector src[hd] -> optional per-head RMSNorm
+// (rmsnorm_inplace, vec.rs:17-27: ss in index order, x *= scale * w) -> RoPE
+// at the position whose cos/sin rows are ct/st (rope.rs:49-65: Adjacent pairs
+// (2i, 2i+1) or Neox halves (i, i + hd/2)). Lane holds elements lane + 32 i.
+// hb is hd floats of shared scratch for the warp.
+NRC_DEV void warp_rope_head(const float* src, const float* nw, float eps, const float* ct, const float* st,
+                            int style, int hd, float* hb, int lane, float* outv) {
+  const int per = hd / 32, half = hd / 2;
+  float vals[4];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+    if (i < per) {
+      vals[i] = src[lane + 32 * i];
+      hb[lane + 32 * i] = vals[i];
+    }
+  __syncwarp();
+  if (nw) {
+    float scale = 0.0f;
+    if (lane == 0) {
+      float ss = 0.0f;
+      for (int i = 0; i < hd; i++) ss = __fadd_rn(ss, __fmul_rn(hb[i], hb[i]));
+      scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), eps)));
+    }
+    scale = __shfl_sync(0xffffffffu, scale, 0);
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (i < per) vals[i] = __fmul_rn(vals[i], __fmul_rn(scale, nw[lane + 32 * i]));
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (i < per) hb[lane + 32 * i] = vals[i];
+    __syncwarp();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    if (i < per) {
+      const int e = lane + 32 * i;
+      int pi, ia, ib;
+      if (style == 0) {
+        pi = e / 2;
+        ia = 2 * pi;
+        ib = ia + 1;
+      } else {
+        pi = e % half;
+        ia = pi;
+        ib = pi + half;
+      }
+      const float c = ct[pi], sn = st[pi];
+      const float av = hb[ia], bv = hb[ib];
+      // head[ia] = a*cos - b*sin; head[ib] = a*sin + b*cos
+      outv[i] = (e == ia) ? __fsub_rn(__fmul_rn(av, c), __fmul_rn(bv, sn)) : __fadd_rn(__fmul_rn(av, sn), __fmul_rn(bv, c));
+    }
+  }
+  __syncwarp();  // hb is free again
+}
+
+// Prefill (nt tokens): one warp per (token, head).
 __global__ void k_rope_append(const RopeArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -35,60 +97,11 @@ __global__ void k_rope_append(const RopeArgs a) {
   const bool is_q = h < a.n_heads;
   const int kvh = h - a.n_heads;
   __shared__ float buf[8][128];
-  float* hb = buf[threadIdx.x / 32];
-  const float* src = is_q ? a.q + (size_t)tok * att_dim + h * hd : a.k + (size_t)tok * kv_dim + kvh * hd;
   const int per = hd / 32;
-  float vals[4];
-#pragma unroll
-  for (int i = 0; i < 4; i++)
-    if (i < per) {
-      vals[i] = src[lane + 32 * i];
-      hb[lane + 32 * i] = vals[i];
-    }
-  __syncwarp();
-  const float* nw = is_q ? a.q_norm : a.k_norm;
-  if (nw) {
-    // rmsnorm_inplace (vec.rs:17-27): ss in index order, then x *= scale * w.
-    float scale = 0.0f;
-    if (lane == 0) {
-      float ss = 0.0f;
-      for (int i = 0; i < hd; i++) ss = __fadd_rn(ss, __fmul_rn(hb[i], hb[i]));
-      scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)hd), a.eps)));
-    }
-    scale = __shfl_sync(0xffffffffu, scale, 0);
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-      if (i < per) vals[i] = __fmul_rn(vals[i], __fmul_rn(scale, nw[lane + 32 * i]));
-    __syncwarp();
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-      if (i < per) hb[lane + 32 * i] = vals[i];
-    __syncwarp();
-  }
-  const float* ct = a.cos_tab + (size_t)pos * half;
-  const float* st = a.sin_tab + (size_t)pos * half;
   float outv[4];
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    if (i < per) {
-      const int e = lane + 32 * i;
-      int pi, ia, ib;
-      if (a.style == 0) {
-        pi = e / 2;
-        ia = 2 * pi;
-        ib = ia + 1;
-      } else {
-        pi = e % half;
-        ia = pi;
-        ib = pi + half;
-      }
-      const float c = ct[pi], sn = st[pi];
-      const float av = hb[ia], bv = hb[ib];
-      // head[ia] = a*cos - b*sin; head[ib] = a*sin + b*cos
-      outv[i] = (e == ia) ? __fsub_rn(__fmul_rn(av, c), __fmul_rn(bv, sn))
-                          : __fadd_rn(__fmul_rn(av, sn), __fmul_rn(bv, c));
-    }
-  }
+  const float* src = is_q ? a.q + (size_t)tok * att_dim + h * hd : a.k + (size_t)tok * kv_dim + kvh * hd;
+  warp_rope_head(src, is_q ? a.q_norm : a.k_norm, a.eps, a.cos_tab + (size_t)pos * half,
+                 a.sin_tab + (size_t)pos * half, a.style, hd, buf[threadIdx.x / 32], lane, outv);
   if (is_q) {
     float* dst = a.q + (size_t)tok * att_dim + h * hd;
 #pragma unroll
@@ -107,107 +120,169 @@ __global__ void k_rope_append(const RopeArgs a) {
   }
 }
 
-// One CTA per (kv head, token) over every position 0..=pos:
-//  1. scores: one thread per position, dot_f16 in the scalar order
-//     (kernels.rs:146-157) times the score scale, for each query head of the group;
-//  2. softmax per head (vec.rs:30-41): max, expf, the sum in position order
-//     (one thread per head), normalisation;
-//  3. out[h][d] = sum over positions, in position order, of p_t * v_t[d]
-//     (axpy_f16, kernels.rs:160-169), V rows staged in shared memory.
+// cp.async 16-byte global -> shared copies (L2 only), grouped by commit.
+NRC_DEV void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+NRC_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+NRC_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// One CTA per (query head, token) over every position 0..=pos
+// (infer.rs:553-572 decode, 661-685 prefill):
+//  0. decode only (fused): warp 0 normalizes and rotates this query head,
+//     warp 1 the new k row, warp 2 converts the new v row of the head's KV
+//     group to f16; the first query head of the group stores both in the
+//     cache. Every head of the group reads the new position from shared
+//     memory (the cache row is being written concurrently);
+//  1. scores: one thread per position, the whole K row loaded before the
+//     dot_f16 chain in the scalar order (kernels.rs:146-157), times the scale;
+//  2. softmax (vec.rs:30-41): max, expf, the sum in position order (one
+//     chain), then p_t = e_t * (1 / sum);
+//  3. out[d] = sum over positions, in position order, of p_t * v_t[d]
+//     (axpy_f16, kernels.rs:160-169): one thread per d, V rows staged in
+//     shared memory by cp.async, double-buffered, the first chunk issued
+//     before the scores so its latency overlaps them.
+// f16 -> f32 uses the hardware conversion, exact for every f16 value.
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   pdl_wait();
   pdl_trigger();
-  const int g = blockIdx.x, tok = blockIdx.z;
+  const int h = blockIdx.x, tok = blockIdx.y;
+  const int hd = a.head_dim, half = hd / 2;
+  const int gqa = a.n_heads / a.n_kv_heads;
+  const int g = h / gqa;
+  const int att_dim = a.n_heads * hd, kv_dim = a.n_kv_heads * hd;
   const uint32_t pos = a.pos_dev[0] + (uint32_t)tok;
   const int npos = (int)pos + 1;
-  const int hd = a.head_dim;
-  const int gqa = a.n_heads / a.n_kv_heads;
-  const int att_dim = a.n_heads * hd, kv_dim = a.n_kv_heads * hd;
-  const int cap = a.ctx;  // score row capacity
+  const bool fused = a.fused != 0;
   extern __shared__ __align__(16) float sm[];
-  float* qs = sm;                    // [gqa][hd]
-  float* sc = qs + gqa * hd;         // [gqa][cap]
-  uint16_t* vs = reinterpret_cast<uint16_t*>(sc + gqa * cap);  // [VCHUNK][hd]
+  float* qs = sm;                                               // [hd]
+  float* hbuf = qs + hd;                                        // [3][hd] rope scratch (fused)
+  uint16_t* knew = reinterpret_cast<uint16_t*>(hbuf + 3 * hd);  // [hd] new k (f16, fused)
+  uint16_t* vnew = knew + hd;                                   // [hd] new v (f16, fused)
+  float* sc = reinterpret_cast<float*>(vnew + hd);              // [ctx] scores, then probabilities
+  uint16_t* vs = reinterpret_cast<uint16_t*>(sc + ((a.ctx + 3) & ~3));  // [2][ATT_VCH][hd]
   __shared__ float red[ATT_THREADS / 32];
-  __shared__ float mh[8], inv_h[8];
-  const int tid = threadIdx.x;
-  for (int i = tid; i < gqa * hd; i += ATT_THREADS) qs[i] = a.q[(size_t)tok * att_dim + g * gqa * hd + i];
-  __syncthreads();
-  for (int t = tid; t < npos; t += ATT_THREADS) {
-    const uint16_t* kr = a.kcache + (size_t)t * kv_dim + g * hd;
-    for (int h = 0; h < gqa; h++) {
-      const float* qh = qs + h * hd;
-      float s = 0.0f;
-      for (int d0 = 0; d0 < hd; d0 += 8) {
-        const uint4 kv8 = *reinterpret_cast<const uint4*>(kr + d0);
-        const uint32_t w[4] = {kv8.x, kv8.y, kv8.z, kv8.w};
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          s = __fadd_rn(s, __fmul_rn(f16_to_f32(w[j] & 0xffffu), qh[d0 + 2 * j]));
-          s = __fadd_rn(s, __fmul_rn(f16_to_f32(w[j] >> 16), qh[d0 + 2 * j + 1]));
-        }
-      }
-      sc[h * cap + t] = __fmul_rn(s, a.scale);
-    }
-  }
-  __syncthreads();
-  for (int h = 0; h < gqa; h++) {
-    float m = -INFINITY;
-    for (int t = tid; t < npos; t += ATT_THREADS) m = fmaxf(m, sc[h * cap + t]);
-    m = warp_max(m);
-    if ((tid & 31) == 0) red[tid >> 5] = m;
-    __syncthreads();
-    if (tid == 0) {
-      float mm = -INFINITY;
-      for (int w = 0; w < ATT_THREADS / 32; w++) mm = fmaxf(mm, red[w]);
-      mh[h] = mm;
-    }
-    __syncthreads();
-    const float mx = mh[h];
-    for (int t = tid; t < npos; t += ATT_THREADS) sc[h * cap + t] = expf_cr(__fsub_rn(sc[h * cap + t], mx));
-  }
-  __syncthreads();
-  if (tid < gqa) {
-    const float* e = sc + tid * cap;
-    float s = 0.0f;
-    for (int t = 0; t < npos; t++) s = __fadd_rn(s, e[t]);
-    inv_h[tid] = __fdiv_rn(1.0f, s);
-  }
-  __syncthreads();
-  for (int h = 0; h < gqa; h++) {
-    const float inv = inv_h[h];
-    for (int t = tid; t < npos; t += ATT_THREADS) sc[h * cap + t] = __fmul_rn(sc[h * cap + t], inv);
-  }
-  // Output chains: thread owns outputs o = tid + i*ATT_THREADS (i < 4), o = h*hd + d.
-  const int nout = gqa * hd;
-  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  const int cpr = hd / 8;  // 16-byte chunks per V row
-  for (int t0 = 0; t0 < npos; t0 += VCHUNK) {
-    const int tn = npos - t0 < VCHUNK ? npos - t0 : VCHUNK;
-    __syncthreads();
+  __shared__ SeqSumShared ssh;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint16_t* kbase = a.kcache + (size_t)g * hd;
+  uint16_t* vbase = a.vcache + (size_t)g * hd;
+  const int cpr = hd / 8;  // 16-byte chunks per K/V row
+  // Rows [0, cached) come from the cache; with the append fused, row `pos`
+  // comes from shared memory.
+  const int cached = fused ? (int)pos : npos;
+  auto stage_v = [&](int t0, int buf) {
+    const int tn = min(ATT_VCH, cached - t0);
+    uint16_t* dst = vs + (size_t)buf * ATT_VCH * hd;
     for (int i = tid; i < tn * cpr; i += ATT_THREADS) {
       const int r = i / cpr, c = i - r * cpr;
-      *reinterpret_cast<uint4*>(vs + r * hd + c * 8) =
-          *reinterpret_cast<const uint4*>(a.vcache + (size_t)(t0 + r) * kv_dim + g * hd + c * 8);
+      cp_async16(dst + r * hd + c * 8, vbase + (size_t)(t0 + r) * kv_dim + c * 8);
     }
-    __syncthreads();
+    cp_async_commit();
+  };
+  stage_v(0, 0);
+  if (fused) {
+    const float* ct = a.cos_tab + (size_t)pos * half;
+    const float* st = a.sin_tab + (size_t)pos * half;
+    const int per = hd / 32;
+    float outv[4];
+    if (warp == 0) {
+      warp_rope_head(a.q + (size_t)h * hd, a.q_norm, a.eps, ct, st, a.style, hd, hbuf, lane, outv);
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int o = tid + i * ATT_THREADS;
-      if (o < nout) {
-        const int h = o / hd, d = o - h * hd;
-        const float* p = sc + h * cap + t0;
-        float ac = acc[i];
-        for (int t = 0; t < tn; t++) ac = __fadd_rn(ac, __fmul_rn(p[t], f16_to_f32(vs[t * hd + d])));
-        acc[i] = ac;
+      for (int i = 0; i < 4; i++)
+        if (i < per) qs[lane + 32 * i] = outv[i];
+    } else if (warp == 1) {
+      warp_rope_head(a.k + (size_t)g * hd, a.k_norm, a.eps, ct, st, a.style, hd, hbuf + hd, lane, outv);
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        if (i < per) {
+          const uint16_t kb = f32_to_f16(outv[i]);
+          knew[lane + 32 * i] = kb;
+          if (h % gqa == 0) kbase[(size_t)pos * kv_dim + lane + 32 * i] = kb;
+        }
+    } else if (warp == 2) {
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        if (i < per) {
+          const uint16_t vb = f32_to_f16(a.v[(size_t)g * hd + lane + 32 * i]);
+          vnew[lane + 32 * i] = vb;
+          if (h % gqa == 0) vbase[(size_t)pos * kv_dim + lane + 32 * i] = vb;
+        }
+    }
+  } else {
+    for (int i = tid; i < hd; i += ATT_THREADS) qs[i] = a.q[(size_t)tok * att_dim + (size_t)h * hd + i];
+  }
+  __syncthreads();
+
+  float mloc = -INFINITY;
+  for (int t = tid; t < npos; t += ATT_THREADS) {
+    float s = 0.0f;
+    if (t < cached) {
+      const uint4* kr = reinterpret_cast<const uint4*>(kbase + (size_t)t * kv_dim);
+      for (int c0 = 0; c0 < cpr; c0 += 8) {
+        uint4 k8[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+          if (c0 + c < cpr) k8[c] = kr[c0 + c];
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          if (c0 + c < cpr) {
+            const uint32_t w[4] = {k8[c].x, k8[c].y, k8[c].z, k8[c].w};
+            const float* qd = qs + (c0 + c) * 8;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              s = __fadd_rn(s, __fmul_rn(h2f(w[j] & 0xffffu), qd[2 * j]));
+              s = __fadd_rn(s, __fmul_rn(h2f(w[j] >> 16), qd[2 * j + 1]));
+            }
+          }
+        }
       }
+    } else {
+      for (int d = 0; d < hd; d++) s = __fadd_rn(s, __fmul_rn(h2f(knew[d]), qs[d]));
     }
+    s = __fmul_rn(s, a.scale);
+    sc[t] = s;
+    mloc = fmaxf(mloc, s);
   }
+  mloc = warp_max(mloc);
+  if (lane == 0) red[warp] = mloc;
+  __syncthreads();
+  float mx = red[0];
 #pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int o = tid + i * ATT_THREADS;
-    if (o < nout) a.out[(size_t)tok * att_dim + g * gqa * hd + o] = acc[i];
+  for (int w = 1; w < ATT_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
+  for (int t = tid; t < npos; t += ATT_THREADS) sc[t] = expf_cr(__fsub_rn(sc[t], mx));
+  __syncthreads();
+  // The sum in position order (vec.rs:35-36), one chain (seqsum.cuh).
+  const float sum = seq_sum_group<ATT_THREADS>(npos, [&](int t) { return sc[t]; }, ssh, tid, [] { __syncthreads(); });
+  const float inv = __fdiv_rn(1.0f, sum);
+  for (int t = tid; t < npos; t += ATT_THREADS) sc[t] = __fmul_rn(sc[t], inv);
+
+  float acc = 0.0f;
+  const int d = tid;
+  int buf = 0;
+  for (int t0 = 0; t0 < npos; t0 += ATT_VCH, buf ^= 1) {
+    const int tn = min(ATT_VCH, npos - t0);
+    if (t0 + ATT_VCH < cached) {
+      stage_v(t0 + ATT_VCH, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    uint16_t* vb = vs + (size_t)buf * ATT_VCH * hd;
+    if (fused && (int)pos < t0 + tn)
+      for (int i = tid; i < hd; i += ATT_THREADS) vb[((int)pos - t0) * hd + i] = vnew[i];
+    __syncthreads();
+    if (d < hd) {
+      const uint16_t* vr = vb + d;
+      const float* p = sc + t0;
+#pragma unroll 4
+      for (int t = 0; t < tn; t++) acc = __fadd_rn(acc, __fmul_rn(p[t], h2f(vr[(size_t)t * hd])));
+    }
+    __syncthreads();  // the buffer is restaged two chunks later
   }
+  if (d < hd) a.out[(size_t)tok * att_dim + (size_t)h * hd + d] = acc;
 }
 
 __global__ void k_embed(const EmbedArgs a) {
@@ -299,13 +374,17 @@ cudaError_t rope_append_run(const RopeArgs& a, cudaStream_t s, bool pdl) {
 }
 
 size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx) {
-  const int gqa = n_heads / n_kv_heads;
-  return (size_t)gqa * head_dim * 4 + (size_t)gqa * ctx * 4 + (size_t)VCHUNK * head_dim * 2 + 16;
+  (void)n_heads;
+  (void)n_kv_heads;
+  // q + rope scratch (4 hd floats) | new k, v (2 hd f16) | scores | 2 V chunks
+  return (size_t)head_dim * 4 * 4 + (size_t)head_dim * 2 * 2 + (size_t)((ctx + 3) & ~3) * 4 +
+         (size_t)2 * ATT_VCH * head_dim * 2;
 }
 
 cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl) {
-  const int gqa = a.n_heads / a.n_kv_heads;
-  if (gqa > 8 || a.head_dim % 8 || a.head_dim > 128) return cudaErrorInvalidValue;
+  if (a.n_kv_heads < 1 || a.n_heads % a.n_kv_heads || a.head_dim % 32 || a.head_dim > ATT_THREADS ||
+      (a.fused && a.nt != 1))
+    return cudaErrorInvalidValue;
   const size_t smem = attention_smem_bytes(a.n_heads, a.n_kv_heads, a.head_dim, a.ctx);
   if (smem > ATTN_MAX_SMEM) return cudaErrorInvalidValue;
   static bool attr_done[64] = {false};
@@ -317,7 +396,7 @@ cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl) {
   }
   AttnArgs aa = a;
   void* args[] = {&aa};
-  return launch((const void*)k_attention, dim3(a.n_kv_heads, 1, a.nt), dim3(ATT_THREADS), smem, s, pdl, args);
+  return launch((const void*)k_attention, dim3(a.n_heads, a.nt), dim3(ATT_THREADS), smem, s, pdl, args);
 }
 
 cudaError_t embed_run(const EmbedArgs& a, cudaStream_t s, bool pdl) {

@@ -569,8 +569,7 @@ extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
   if (ctx == 0) return fail(NRC_ERR_INVALID, "ctx must be > 0");
   *out = nullptr;
   const nrc_meta& mt = m->meta;
-  if (mt.head_dim % 32 || mt.head_dim > 128 || mt.n_kv_heads == 0 || mt.n_heads % mt.n_kv_heads ||
-      mt.n_heads / mt.n_kv_heads > 8)
+  if (mt.head_dim % 32 || mt.head_dim > 128 || mt.n_kv_heads == 0 || mt.n_heads % mt.n_kv_heads)
     return fail(NRC_ERR_INVALID, "unsupported attention shape (head_dim %u, heads %u/%u)", mt.head_dim, mt.n_heads,
                 mt.n_kv_heads);
   if (attention_smem_bytes(mt.n_heads, mt.n_kv_heads, mt.head_dim, (int)ctx) > ATTN_MAX_SMEM)
@@ -838,12 +837,36 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
         if ((e = linear(c, L, nt))) return e;
       }
     }
-    RopeArgs ra{c->q, c->k, c->v, w.q_norm, w.k_norm, c->eps, c->cos_t, c->sin_t, c->style,
-                c->kc + (size_t)l * c->ctx * c->kv_dim, c->vc + (size_t)l * c->ctx * c->kv_dim,
-                nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
-    if ((e = rope_append_run(ra, s, pdl))) return e;
-    AttnArgs aa{c->q, c->att, c->kc + (size_t)l * c->ctx * c->kv_dim, c->vc + (size_t)l * c->ctx * c->kv_dim,
-                c->att_scale, nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
+    uint16_t* kc_l = c->kc + (size_t)l * c->ctx * c->kv_dim;
+    uint16_t* vc_l = c->vc + (size_t)l * c->ctx * c->kv_dim;
+    AttnArgs aa{};
+    aa.q = c->q;
+    aa.out = c->att;
+    aa.kcache = kc_l;
+    aa.vcache = vc_l;
+    aa.scale = c->att_scale;
+    aa.nt = nt;
+    aa.n_heads = c->n_heads;
+    aa.n_kv_heads = c->n_kv;
+    aa.head_dim = c->hd;
+    aa.ctx = (int)c->ctx;
+    aa.pos_dev = &c->st->pos;
+    if (nt == 1) {
+      // Decode: per-head norms, RoPE and the KV append fused into attention.
+      aa.fused = 1;
+      aa.k = c->k;
+      aa.v = c->v;
+      aa.q_norm = w.q_norm;
+      aa.k_norm = w.k_norm;
+      aa.eps = c->eps;
+      aa.cos_tab = c->cos_t;
+      aa.sin_tab = c->sin_t;
+      aa.style = c->style;
+    } else {
+      RopeArgs ra{c->q, c->k, c->v, w.q_norm, w.k_norm, c->eps, c->cos_t, c->sin_t, c->style, kc_l, vc_l,
+                  nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
+      if ((e = rope_append_run(ra, s, pdl))) return e;
+    }
     if ((e = attention_run(aa, s, pdl))) return e;
     {  // output projection + residual (infer.rs:574-575)
       Lin L{};

@@ -4,30 +4,37 @@
 // Reference: crates/nr-tensor/src/kernels.rs:36-143 (Q8_0) and
 // crates/nr-tensor/src/kquant.rs:192-250, 536-639 (Q4_K / Q6_K).
 //
-// Structure (persistent CTAs, up to two per SM):
-//  * warp 8 (producer) streams the CTA's row tiles — contiguous byte ranges of
-//    the weight matrix — into a ring of 16 KB shared-memory stages with 1-D TMA
-//    bulk copies (cp.async.bulk, L2 evict-first, no cluster multicast), one
-//    full/empty mbarrier pair per stage;
-//  * warps 0-7 (consumers) stage the activations in shared memory once per
-//    CTA (coalesced load, optional RMSNorm, quantization exactly as the
-//    reference quantizes them), then split every stage into units — one Q8_0
-//    block or one K-quant super-block per thread — and compute each unit's
-//    exact integer dots with dp4a. For K-quants the consumers form two groups
-//    that work on alternate stages, so two stages are in flight;
-//  * each block's f32 term is rounded exactly as the reference's scalar dot
-//    rounds it (kernels.rs:79, kquant.rs:212-215, 244-247) and parked in a
-//    per-tile buffer; one thread per (row, token) then adds the terms in block
-//    order — the reference's summation order — so every output is
-//    bit-identical to dot_q8_scalar / dot_q4k_scalar / dot_q6k_scalar.
+// Structure (persistent, one CTA per SM, 8 consumer warps + 1 producer warp):
+//  * a tile is R consecutive weight rows (whole rows; gate and up are two
+//    spans of one tile in the SwiGLU pair), i.e. one or two contiguous byte
+//    ranges. The producer warp copies each tile HBM -> shared memory with one
+//    1-D TMA bulk copy per span (cp.async.bulk, L2 evict-first, no cluster
+//    multicast) into a ring of stage buffers, one full/empty mbarrier pair
+//    per stage; weights never depend on the previous kernel, so streaming
+//    starts before the programmatic-dependency wait;
+//  * the consumers stage the activations in shared memory once per CTA
+//    (optional RMSNorm, quantization exactly as the reference quantizes them,
+//    one thread per 32-value block);
+//  * tile k belongs to warp k mod ncw and every ring slot to one warp (the
+//    ring holds ncw or 2 ncw stages), so the warps run independently. The
+//    owning warp's lanes compute the tile's units — an aligned octet of 8
+//    Q8_0 blocks, one Q8_0 block, or one K-quant super-block — as exact
+//    integer dp4a dots, round each block's f32 term exactly as the
+//    reference's scalar dot rounds it (kernels.rs:79, kquant.rs:212-215,
+//    244-247) and park it in the warp's term buffer; then one lane per
+//    (row, token) adds the row's terms in block order, the reference's
+//    summation order, and applies the fused epilogue.
 #include <algorithm>
 #include <map>
 #include <mutex>
 #include <tuple>
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 #include "expf_cr.cuh"
 #include "gemv.cuh"
+#include "seqsum.cuh"
 
 namespace nrc {
 namespace {
@@ -35,9 +42,8 @@ namespace {
 constexpr int NCW = 8;             // consumer warps
 constexpr int NC = NCW * 32;       // consumer threads
 constexpr int NTHREADS = NC + 32;  // + producer warp
-constexpr int MAX_STAGES = 8;
-constexpr int STAGE_PAYLOAD = 16384;
-constexpr int STAGE_BUF = STAGE_PAYLOAD + 64;
+constexpr int MAX_STAGES = 16;
+constexpr int STAGE_TARGET = 12288;  // payload bytes per stage the host aims for
 constexpr int XW = 68;  // words per 256-byte activation group (64 + 4 pad: conflict-free LDS.128)
 constexpr int SMEM_RESERVE = 1024;  // static shared memory of the kernel, rounded up
 
@@ -49,11 +55,15 @@ struct Params {
   int tile_start[4];
   int nseg, pair;
   int K, bpr, row_bytes;
-  int RT;
-  int unit_bytes, units_per_stage;
+  int R;            // rows per tile (= per stage)
+  int unit_bytes;   // bytes per unit (272: Q8_0 octet, 34: Q8_0 block, 144 / 210: super-block)
+  int upr;          // units per row
+  int span_stride;  // stage bytes reserved per span (16-byte multiple)
+  int stage_bytes;
   int ntiles;
   int nt;
-  int nstage, groups;
+  int nstage;       // a multiple of ncw: every slot belongs to one warp
+  int ncw;          // consumer warps that own tiles (the others only help with the prologue)
   const uint8_t* xq;
   const float* xf;
   int xf_ld;
@@ -66,8 +76,9 @@ struct Params {
   float rs;
   unsigned long long* argmax_key;
   unsigned* err;
-  int off_x, off_xd, off_xb, off_t, t_elems;  // shared-memory layout (bytes / floats)
-  int xs_floats;                              // f32 staging floats at off_t (prologue)
+  int off_x, off_xd, off_xb, off_t;  // shared-memory layout (bytes)
+  int tb_warp;                       // floats of one warp's term buffer
+  int xs_floats;                     // f32 staging floats at off_t (prologue)
   int n_oct;
 };
 
@@ -113,6 +124,58 @@ NRC_DEV void unit_q8(const uint8_t* src, const uint32_t* xq, int xtok, const flo
       acc = __dp4a((int)q[7], (int)b.w, acc);
       // kernels.rs:79 — `acc as f32 * bw.scale() * bx.scale()`
       t[tok * tstride] = __fmul_rn(__fmul_rn(i2f(acc), dw), xd[tok * bpr]);
+    }
+  }
+}
+
+// Eight consecutive Q8_0 blocks (272 bytes, 16-byte aligned: 17 uint4).
+// Block j starts at byte 34j: even j at a word boundary (scale in the low
+// half, quants 2 bytes in), odd j at a half word (scale in the high half,
+// quants word aligned). kernels.rs:72-82 per block.
+template <int NT>
+NRC_DEV void unit_q8_oct(const uint8_t* src, const uint32_t* xq, int xtok, const float* xd, int nt, int bpr,
+                         float* t, int tstride) {
+  uint32_t w[68];
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < 17; i++) {
+    const uint4 v = s4[i];
+    w[4 * i] = v.x;
+    w[4 * i + 1] = v.y;
+    w[4 * i + 2] = v.z;
+    w[4 * i + 3] = v.w;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int base = (j / 2) * 17;
+    uint32_t q[8];
+    uint32_t dbits;
+    if ((j & 1) == 0) {
+      dbits = w[base] & 0xffffu;
+#pragma unroll
+      for (int k = 0; k < 8; k++) q[k] = __byte_perm(w[base + k], w[base + k + 1], 0x5432);
+    } else {
+      dbits = w[base + 8] >> 16;
+#pragma unroll
+      for (int k = 0; k < 8; k++) q[k] = w[base + 9 + k];
+    }
+    // f16 -> f32 is exact for every f16 value; the hardware conversion is used.
+    const float dw = __half2float(__ushort_as_half((unsigned short)dbits));
+#pragma unroll
+    for (int tok = 0; tok < NT; tok++) {
+      if (tok < nt) {
+        const uint4* xv = reinterpret_cast<const uint4*>(xq + tok * xtok + j * 8);
+        const uint4 a = xv[0], b = xv[1];
+        int acc = __dp4a((int)q[0], (int)a.x, 0);
+        acc = __dp4a((int)q[1], (int)a.y, acc);
+        acc = __dp4a((int)q[2], (int)a.z, acc);
+        acc = __dp4a((int)q[3], (int)a.w, acc);
+        acc = __dp4a((int)q[4], (int)b.x, acc);
+        acc = __dp4a((int)q[5], (int)b.y, acc);
+        acc = __dp4a((int)q[6], (int)b.z, acc);
+        acc = __dp4a((int)q[7], (int)b.w, acc);
+        t[tok * tstride + j] = __fmul_rn(__fmul_rn(i2f(acc), dw), xd[tok * bpr + j]);
+      }
     }
   }
 }
@@ -251,32 +314,9 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
   float* xd = reinterpret_cast<float*>(smem + p.off_xd);
   int* xb = reinterpret_cast<int*>(smem + p.off_xb);
   float* xs = reinterpret_cast<float*>(smem + p.off_t);
-  __shared__ float nscale[8];
+  __shared__ SeqSumShared ssh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int K = p.K;
-  if (p.norm_w) {
-    // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order, then
-    // scale = 1 / sqrtf(ss / n + eps). Thread `tok` runs token tok's chain
-    // over chunks staged in shared memory (row stride CH + 1: no bank conflicts).
-    const int CH = p.xs_floats / p.nt - 1;
-    float ss = 0.0f;
-    for (int c0 = 0; c0 < K; c0 += CH) {
-      const int cn = K - c0 < CH ? K - c0 : CH;
-      for (int i = tid; i < p.nt * cn; i += NC) {
-        const int tk = i / cn, k = i - tk * cn;
-        xs[tk * (CH + 1) + k] = p.xf[(size_t)tk * p.xf_ld + c0 + k];
-      }
-      named_sync(1, NC);
-      if (tid < p.nt) {
-        const float* r = xs + tid * (CH + 1);
-#pragma unroll 8
-        for (int k = 0; k < cn; k++) ss = __fadd_rn(ss, __fmul_rn(r[k], r[k]));
-      }
-      named_sync(1, NC);
-    }
-    if (tid < p.nt) nscale[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), p.eps)));
-    named_sync(1, NC);
-  }
   for (int tok = 0; tok < p.nt; tok++) {
     const float* src = p.xf + (size_t)tok * p.xf_ld;
     if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (K & 3) == 0) {
@@ -285,21 +325,57 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
       for (int i = tid; i < K; i += NC) xs[i] = src[i];
     }
     named_sync(1, NC);
-    const float sc = p.norm_w ? nscale[tok] : 1.0f;
+    float sc = 1.0f;
+    if (p.norm_w) {
+      // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain,
+      // seqsum.cuh), then scale = 1 / sqrtf(ss / n + eps).
+      const float ss = seq_sum_group<NC>(
+          K, [&](int i) { return __fmul_rn(xs[i], xs[i]); }, ssh, tid, [] { named_sync(1, NC); });
+      sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), p.eps)));
+    }
     if (FMT == FMT_Q8_0) {
-      for (int b = warp; b < p.bpr; b += NCW) {
-        float v = xs[b * 32 + lane];
-        if (p.norm_w) v = __fmul_rn(__fmul_rn(v, sc), p.norm_w[b * 32 + lane]);
-        const float amax = warp_max(fabsf(v));
+      // q8::quantize (q8.rs:27-44), one thread per 32-value block: all blocks
+      // of the row at once.
+      for (int b = tid; b < p.bpr; b += NC) {
+        const float4* x4 = reinterpret_cast<const float4*>(xs + b * 32);
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          const float4 f = x4[c];
+          v[4 * c] = f.x;
+          v[4 * c + 1] = f.y;
+          v[4 * c + 2] = f.z;
+          v[4 * c + 3] = f.w;
+        }
+        if (p.norm_w) {
+          const float* wn = p.norm_w + b * 32;
+#pragma unroll
+          for (int k = 0; k < 32; k++) v[k] = __fmul_rn(__fmul_rn(v[k], sc), __ldg(wn + k));
+        }
+        float amax = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
         const uint16_t dbits = f32_to_f16(__fdiv_rn(amax, 127.0f));
         const float d = f16_to_f32(dbits);
         const float inv = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        const float xsv = __fmul_rn(v, inv);
-        const float r = xsv >= 0.0f ? __fadd_rn(xsv, 0.5f) : __fsub_rn(xsv, 0.5f);
-        int q = rust_f2i(r);
-        q = q < -127 ? -127 : (q > 127 ? 127 : q);
-        reinterpret_cast<uint8_t*>(xq + xq_index(FMT_Q8_0, p, tok, b))[lane] = (uint8_t)(int8_t)q;
-        if (lane == 0) xd[tok * p.bpr + b] = d;
+        uint32_t pk[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+          uint32_t wv = 0;
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const float xsv = __fmul_rn(v[4 * c + k], inv);
+            const float r = xsv >= 0.0f ? __fadd_rn(xsv, 0.5f) : __fsub_rn(xsv, 0.5f);
+            int q = rust_f2i(r);
+            q = q < -127 ? -127 : (q > 127 ? 127 : q);
+            wv |= (uint32_t)(uint8_t)(int8_t)q << (8 * k);
+          }
+          pk[c] = wv;
+        }
+        uint4* dst = reinterpret_cast<uint4*>(xq + xq_index(FMT_Q8_0, p, tok, b));
+        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        xd[tok * p.bpr + b] = d;
       }
     } else {
       for (int b = warp; b < p.bpr; b += NCW) {
@@ -410,48 +486,64 @@ struct Span {
   int row0, nrows, seg;
 };
 
-NRC_DEV int tile_spans(const Params& p, int tile, Span* sp) {
-  if (p.pair) {
-    const int row0 = tile * p.RT;
-    const int nr = imin(p.RT, p.rows[0] - row0);
-    for (int s = 0; s < 2; s++) {
-      sp[s].base = p.w[s] + (size_t)row0 * p.row_bytes;
-      sp[s].wbeg = p.w[s];
-      sp[s].wend = p.w[s] + (size_t)p.rows[s] * p.row_bytes;
-      sp[s].row0 = row0;
-      sp[s].nrows = nr;
-      sp[s].seg = s;
-    }
-    return 2;
-  }
+// The tile's spans: span 0 (the tile's segment), span 1 (up rows in pair mode).
+NRC_DEV void tile_spans(const Params& p, int tile, Span& s0, Span& s1) {
   int s = 0;
-  while (s + 1 < p.nseg && tile >= p.tile_start[s + 1]) s++;
-  const int row0 = (tile - p.tile_start[s]) * p.RT;
-  sp[0].base = p.w[s] + (size_t)row0 * p.row_bytes;
-  sp[0].wbeg = p.w[s];
-  sp[0].wend = p.w[s] + (size_t)p.rows[s] * p.row_bytes;
-  sp[0].row0 = row0;
-  sp[0].nrows = imin(p.RT, p.rows[s] - row0);
-  sp[0].seg = s;
-  return 1;
+  if (!p.pair)
+    while (s + 1 < p.nseg && tile >= p.tile_start[s + 1]) s++;
+  const int row0 = (tile - p.tile_start[s]) * p.R;
+  const int nr = imin(p.R, p.rows[s] - row0);
+  s0.base = p.w[s] + (size_t)row0 * p.row_bytes;
+  s0.wbeg = p.w[s];
+  s0.wend = p.w[s] + (size_t)p.rows[s] * p.row_bytes;
+  s0.row0 = row0;
+  s0.nrows = nr;
+  s0.seg = s;
+  s1 = s0;
+  if (p.pair) {
+    s1.base = p.w[1] + (size_t)row0 * p.row_bytes;
+    s1.wbeg = p.w[1];
+    s1.wend = p.w[1] + (size_t)p.rows[1] * p.row_bytes;
+    s1.seg = 1;
+  }
+}
+
+// Byte range [g0, g1) of a span lands at slot + (addr - a0), a0 = floor16(g0).
+// The 16-byte aligned part inside the weight buffer goes by one bulk copy
+// [blo, bhi); the (at most 2x15) ragged bytes at unaligned buffer ends by
+// plain loads.
+struct SegRange {
+  uintptr_t g0, g1, a0, blo, bhi;
+};
+NRC_DEV SegRange seg_range(const Span& sp, int row_bytes) {
+  SegRange q;
+  q.g0 = reinterpret_cast<uintptr_t>(sp.base);
+  q.g1 = q.g0 + (size_t)sp.nrows * row_bytes;
+  q.a0 = q.g0 & ~(uintptr_t)15;
+  const uintptr_t wb = (reinterpret_cast<uintptr_t>(sp.wbeg) + 15) & ~(uintptr_t)15;
+  const uintptr_t we = reinterpret_cast<uintptr_t>(sp.wend) & ~(uintptr_t)15;
+  q.blo = q.a0 > wb ? q.a0 : wb;
+  q.bhi = (q.g1 + 15) & ~(uintptr_t)15;
+  if (q.bhi > we) q.bhi = we;
+  if (q.bhi <= q.blo) q.blo = q.bhi = q.g0;
+  return q;
 }
 
 template <int FMT, int NT, int XMODE, int ALIGNED>
-__global__ void __launch_bounds__(NTHREADS, (NT <= 2 ? 2 : 1)) gemv_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.nstage * STAGE_BUF);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)p.nstage * p.stage_bytes);
   uint64_t* empty = full + MAX_STAGES;
   __shared__ volatile int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int NS = p.nstage;
-  const int G = p.groups;            // consumer groups (stage `it` belongs to group it % G)
-  const int WPG = NCW / G;           // warps per group
+  const int nspan = p.pair ? 2 : 1;
 
   if (tid == 0) {
     for (int s = 0; s < NS; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], WPG);
+      mbar_init(&empty[s], 1);
     }
     abort_flag = 0;
     fence_barrier_init();
@@ -463,50 +555,45 @@ __global__ void __launch_bounds__(NTHREADS, (NT <= 2 ? 2 : 1)) gemv_kernel(const
     // ----------------------------------------------------------- producer
     const uint64_t pol = l2_evict_first();
     int it = 0;
-    Span sp[2];
-    for (int tile = blockIdx.x; tile < p.ntiles && !abort_flag; tile += gridDim.x) {
-      const int ns = tile_spans(p, tile, sp);
-      for (int si = 0; si < ns && !abort_flag; si++) {
-        const int nunits = sp[si].nrows * (p.row_bytes / p.unit_bytes);
-        for (int u0 = 0; u0 < nunits; u0 += p.units_per_stage, it++) {
-          const int u1 = imin(u0 + p.units_per_stage, nunits);
-          const int s = it % NS;
-          if (it >= NS) {
-            bool ok = true;
-            if (lane == 0) ok = mbar_wait(&empty[s], ((it / NS) - 1) & 1);
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok || abort_flag) {
-              if (lane == 0) {
-                abort_flag = 1;
-                atomicOr(p.err, ERR_WAIT_EMPTY);
-              }
-              break;
-            }
-          }
-          // Bytes [g0, g1) land at dst + (addr - floor16(g0)). The 16-byte
-          // aligned part inside the weight buffer goes by one bulk copy; the
-          // (at most 2x15) ragged bytes at unaligned buffer ends by plain loads.
-          const uintptr_t g0 = reinterpret_cast<uintptr_t>(sp[si].base) + (size_t)u0 * p.unit_bytes;
-          const uintptr_t g1 = reinterpret_cast<uintptr_t>(sp[si].base) + (size_t)u1 * p.unit_bytes;
-          const uintptr_t a0 = g0 & ~(uintptr_t)15;
-          const uintptr_t wb = (reinterpret_cast<uintptr_t>(sp[si].wbeg) + 15) & ~(uintptr_t)15;
-          const uintptr_t we = reinterpret_cast<uintptr_t>(sp[si].wend) & ~(uintptr_t)15;
-          uintptr_t blo = a0 > wb ? a0 : wb;
-          uintptr_t bhi = (g1 + 15) & ~(uintptr_t)15;
-          if (bhi > we) bhi = we;
-          if (bhi <= blo) blo = bhi = g0;
-          uint8_t* dst = stages + s * STAGE_BUF;
-          for (uintptr_t a = g0 + lane; a < blo; a += 32) dst[a - a0] = *reinterpret_cast<const uint8_t*>(a);
-          for (uintptr_t a = (bhi > g0 ? bhi : g0) + lane; a < g1; a += 32)
-            dst[a - a0] = *reinterpret_cast<const uint8_t*>(a);
-          __syncwarp();
+    Span sp0, sp1;
+    for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, it++) {
+      const int s = it % NS;
+      if (it >= NS) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(&empty[s], ((it / NS) - 1) & 1);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok || abort_flag) {
           if (lane == 0) {
-            const uint32_t nbytes = bhi > blo ? (uint32_t)(bhi - blo) : 0u;
-            mbar_arrive_expect_tx(&full[s], nbytes);
-            if (nbytes) bulk_g2s(dst + (blo - a0), reinterpret_cast<const void*>(blo), nbytes, &full[s], pol);
+            abort_flag = 1;
+            atomicOr(p.err, ERR_WAIT_EMPTY);
           }
+          break;
         }
       }
+      tile_spans(p, tile, sp0, sp1);
+      uint8_t* sbuf = stages + (size_t)s * p.stage_bytes;
+      const SegRange g0 = seg_range(sp0, p.row_bytes);
+      const SegRange g1 = seg_range(sp1, p.row_bytes);
+      uint32_t total = 0;
+      for (int si = 0; si < nspan; si++) {
+        const SegRange g = si ? g1 : g0;
+        uint8_t* dst = sbuf + (size_t)si * p.span_stride;
+        for (uintptr_t a = g.g0 + lane; a < g.blo; a += 32) dst[a - g.a0] = *reinterpret_cast<const uint8_t*>(a);
+        for (uintptr_t a = (g.bhi > g.g0 ? g.bhi : g.g0) + lane; a < g.g1; a += 32)
+          dst[a - g.a0] = *reinterpret_cast<const uint8_t*>(a);
+        total += (uint32_t)(g.bhi - g.blo);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&full[s], total);
+        for (int si = 0; si < nspan; si++) {
+          const SegRange g = si ? g1 : g0;
+          if (g.bhi > g.blo)
+            bulk_g2s(sbuf + (size_t)si * p.span_stride + (g.blo - g.a0), reinterpret_cast<const void*>(g.blo),
+                     (uint32_t)(g.bhi - g.blo), &full[s], pol);
+        }
+      }
+      __syncwarp();
     }
     // Drain: wait (bounded) for the copies of the last issued stages, so the
     // CTA never exits with a bulk copy in flight.
@@ -529,82 +616,101 @@ __global__ void __launch_bounds__(NTHREADS, (NT <= 2 ? 2 : 1)) gemv_kernel(const
   const uint32_t* xq = reinterpret_cast<const uint32_t*>(smem + p.off_x);
   const float* xd = reinterpret_cast<const float*>(smem + p.off_xd);
   const int* xb = reinterpret_cast<const int*>(smem + p.off_xb);
-  float* tbuf = reinterpret_cast<float*>(smem + p.off_t);
-  const int TS = p.bpr + 1;  // odd stride: conflict-free chains
-  const int grp = warp / WPG;
-  const int gtid = tid - grp * WPG * 32;
-  const int GN = WPG * 32;  // threads per group
-  const int upr = p.row_bytes / p.unit_bytes;
-  const int xtok = FMT == FMT_Q8_0 ? p.n_oct * XW : p.bpr * XW;
-  int it = 0, tc = 0;
-  Span sp[2];
+  float* tbw = reinterpret_cast<float*>(smem + p.off_t) + (size_t)warp * p.tb_warp;
+  const int bpr = p.bpr;
+  const int TS = bpr + 1;  // odd stride: conflict-free chains
+  const bool oct = FMT == FMT_Q8_0 && p.unit_bytes == 8 * Q8_0_BYTES;
+  const int bpu = oct ? 8 : 1;  // blocks per unit
+  const int xtok = FMT == FMT_Q8_0 ? p.n_oct * XW : bpr * XW;
+  const int R = p.R;
+  // This lane's (row, token) chain within a tile.
+  const int c_r = lane / NT, c_tok = lane % NT;
   unsigned long long best = 0ull;
-  for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, tc++) {
-    float* tb = tbuf + (tc & 1) * p.t_elems;
-    const int ns = tile_spans(p, tile, sp);
-    for (int si = 0; si < ns; si++) {
-      const int nunits = sp[si].nrows * upr;
-      for (int u0 = 0; u0 < nunits; u0 += p.units_per_stage, it++) {
-        if (it % G != grp) continue;
-        const int u1 = imin(u0 + p.units_per_stage, nunits);
-        const int s = it % NS;
-        const bool ok = !abort_flag && mbar_wait(&full[s], (it / NS) & 1);
-        if (!ok) {
-          if (lane == 0 && !abort_flag) {
-            abort_flag = 1;
-            atomicOr(p.err, ERR_WAIT_FULL);
-          }
-        } else {
-          const uintptr_t g0 = reinterpret_cast<uintptr_t>(sp[si].base) + (size_t)u0 * p.unit_bytes;
-          const uint8_t* sbase = stages + s * STAGE_BUF + (g0 & 15);
-          for (int j = gtid; j < u1 - u0; j += GN) {
-            const int u = u0 + j;
-            const int r = u / upr, g = u % upr;
-            const uint8_t* src = sbase + (size_t)j * p.unit_bytes;
-            float* t = tb + ((si * p.RT + r) * NT) * TS + g;
-            if (FMT == FMT_Q8_0)
-              unit_q8<NT>(src, xq + (g / 8) * XW + (g % 8) * 8, xtok, xd + g, p.nt, p.bpr, t, TS);
-            else if (FMT == FMT_Q4K)
-              unit_q4k<NT, ALIGNED>(src, xq + g * XW, xd + g, xb + g * 8, p.nt, p.bpr, t, TS);
-            else
-              unit_q6k<NT>(src, xq + g * XW, xd + g, p.nt, p.bpr, t, TS);
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+  Span sp0, sp1;
+  int k = 0;
+  for (int tile = blockIdx.x; tile < p.ntiles && warp < p.ncw; tile += gridDim.x, k++) {
+    if ((k % p.ncw) != warp) continue;
+    const int s = k % NS;
+    // Every lane waits (each acquires the stage); the decision is warp-uniform.
+    const bool ok = __all_sync(0xffffffffu, !abort_flag && mbar_wait(&full[s], (k / NS) & 1));
+    if (!ok) {
+      if (lane == 0 && !abort_flag) {
+        abort_flag = 1;
+        atomicOr(p.err, ERR_WAIT_FULL);
       }
+      break;
     }
-    named_sync(1, NC);
-    if (abort_flag) continue;
-    // Ordered per-(row, token) chains + epilogue.
-    const int nr = sp[0].nrows;
-    const int items = nr * p.nt;
-    for (int i = tid; i < items; i += NC) {
-      const int r = i / p.nt, tok = i % p.nt;
-      const float* tp = tb + (r * NT + tok) * TS;
-      float s = 0.0f;
-      for (int b = 0; b < p.bpr; b++) s = __fadd_rn(s, tp[b]);
-      const int row = sp[0].row0 + r;
-      const int sg = sp[0].seg;
-      if (p.epi == EPI_RESID) {
-        float* dst = p.resid + (size_t)tok * p.resid_ld + row;
-        *dst = __fadd_rn(*dst, __fmul_rn(p.rs, s));
-      } else if (p.epi == EPI_SWIGLU) {
-        const float* tu = tb + ((p.RT + r) * NT + tok) * TS;
-        float su = 0.0f;
-        for (int b = 0; b < p.bpr; b++) su = __fadd_rn(su, tu[b]);
-        // vec::swiglu: silu = x / (1 + expf(-x)); gate = silu * up
-        const float silu = __fdiv_rn(s, __fadd_rn(1.0f, expf_cr(-s)));
-        p.y[0][(size_t)tok * p.ld[0] + row] = __fmul_rn(silu, su);
+    tile_spans(p, tile, sp0, sp1);
+    const int nr = sp0.nrows;
+    const uint8_t* sbuf = stages + (size_t)s * p.stage_bytes;
+    const uint8_t* sb0 = sbuf + (reinterpret_cast<uintptr_t>(sp0.base) & 15);
+    const uint8_t* sb1 = sbuf + p.span_stride + (reinterpret_cast<uintptr_t>(sp1.base) & 15);
+    const int upr = p.upr;
+    const int nunits = nspan * nr * upr;
+    // Unit u = (span, row, unit-in-row), walked with counters (no divisions).
+    int uo = lane % upr, r = lane / upr, si = 0;
+    while (r >= nr) {
+      r -= nr;
+      si++;
+    }
+    for (int u = lane; u < nunits; u += 32) {
+      const uint8_t* src = (si ? sb1 : sb0) + (size_t)r * p.row_bytes + (size_t)uo * p.unit_bytes;
+      float* t = tbw + (size_t)((si * R + r) * NT) * TS + uo * bpu;
+      if (FMT == FMT_Q8_0) {
+        if (oct)
+          unit_q8_oct<NT>(src, xq + uo * XW, xtok, xd + 8 * uo, p.nt, bpr, t, TS);
+        else
+          unit_q8<NT>(src, xq + (uo / 8) * XW + (uo % 8) * 8, xtok, xd + uo, p.nt, bpr, t, TS);
+      } else if (FMT == FMT_Q4K) {
+        unit_q4k<NT, ALIGNED>(src, xq + uo * XW, xd + uo, xb + uo * 8, p.nt, bpr, t, TS);
       } else {
-        if (p.scale != 1.0f) s = __fmul_rn(s, p.scale);
-        p.y[sg][(size_t)tok * p.ld[sg] + row] = s;
-        if (p.epi == EPI_ARGMAX && tok == 0 && argmax_candidate(s)) {
-          const unsigned long long k = argmax_key(s, (uint32_t)row);
-          best = k > best ? k : best;
+        unit_q6k<NT>(src, xq + uo * XW, xd + uo, p.nt, bpr, t, TS);
+      }
+      uo += 32;
+      while (uo >= upr) {
+        uo -= upr;
+        if (++r == nr) {
+          r = 0;
+          si++;
         }
       }
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    // Ordered chains: lane (r, tok) sums its row's terms in block order.
+    const bool chain = lane < nr * NT && c_tok < p.nt;
+    float acc = 0.0f, acc_u = 0.0f;
+    if (chain) {
+      const float* tp = tbw + (size_t)(c_r * NT + c_tok) * TS;
+      if (nspan == 2) {
+        const float* tu = tbw + (size_t)((R + c_r) * NT + c_tok) * TS;
+        for (int b = 0; b < bpr; b++) {
+          acc = __fadd_rn(acc, tp[b]);
+          acc_u = __fadd_rn(acc_u, tu[b]);
+        }
+      } else {
+        for (int b = 0; b < bpr; b++) acc = __fadd_rn(acc, tp[b]);
+      }
+      const int row = sp0.row0 + c_r;
+      if (p.epi == EPI_SWIGLU) {
+        // vec::swiglu: silu = x / (1 + expf(-x)); gate = silu * up
+        const float silu = __fdiv_rn(acc, __fadd_rn(1.0f, expf_cr(-acc)));
+        p.y[0][(size_t)c_tok * p.ld[0] + row] = __fmul_rn(silu, acc_u);
+      } else if (p.epi == EPI_RESID) {
+        float* dst = p.resid + (size_t)c_tok * p.resid_ld + row;
+        *dst = __fadd_rn(*dst, __fmul_rn(p.rs, acc));
+      } else {
+        float sv = acc;
+        if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
+        const int sg = sp0.seg;
+        p.y[sg][(size_t)c_tok * p.ld[sg] + row] = sv;
+        if (p.epi == EPI_ARGMAX && c_tok == 0 && argmax_candidate(sv)) {
+          const unsigned long long key = argmax_key(sv, (uint32_t)row);
+          best = key > best ? key : best;
+        }
+      }
+    }
+    __syncwarp();  // the term buffer is rewritten by the warp's next tile
   }
   if (p.epi == EPI_ARGMAX) {
 #pragma unroll
@@ -688,6 +794,7 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   const int blk = a.fmt == FMT_Q8_0 ? QK8_0 : QK_K;
   const int bbytes = a.fmt == FMT_Q8_0 ? Q8_0_BYTES : (a.fmt == FMT_Q4K ? Q4K_BYTES : Q6K_BYTES);
   if (a.K <= 0 || a.K % blk || a.nt < 1 || a.nt > 8 || a.nseg < 1 || a.nseg > 3) return cudaErrorInvalidValue;
+  if (a.pair && (a.nseg != 2 || a.seg[0].rows != a.seg[1].rows)) return cudaErrorInvalidValue;
   p.K = a.K;
   p.bpr = a.K / blk;
   p.row_bytes = p.bpr * bbytes;
@@ -695,9 +802,6 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   const int NTc = a.nt <= 1 ? 1 : (a.nt <= 2 ? 2 : (a.nt <= 4 ? 4 : 8));
   bool aligned = true;
   for (int s = 0; s < a.nseg; s++) aligned = aligned && ((reinterpret_cast<uintptr_t>(a.seg[s].w) & 15) == 0);
-  p.unit_bytes = bbytes;
-  p.units_per_stage = STAGE_PAYLOAD / p.unit_bytes;
-  p.groups = a.fmt == FMT_Q8_0 ? 1 : 2;
   p.n_oct = (p.bpr + 7) / 8;
   p.nseg = a.nseg;
   p.pair = a.pair;
@@ -720,13 +824,22 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   p.argmax_key = a.argmax_key;
   p.err = a.err;
   const int xmode = a.xq ? 0 : 1;
-
-  // Shared memory: stages | barriers | activations | per-tile term buffers
-  // (the term buffers double as the f32 staging row of the prologue).
+  const int nspan = a.pair ? 2 : 1;
   const DevInfo di = dev_info();
-  size_t fixed = 2 * MAX_STAGES * 8;
-  const size_t x_off = fixed;
-  size_t off = x_off;
+  // Units: aligned octets of Q8_0 blocks when every row starts 16-byte aligned.
+  const bool oct = a.fmt == FMT_Q8_0 && p.bpr % 8 == 0 && aligned;
+  p.unit_bytes = oct ? 8 * bbytes : bbytes;
+  p.upr = oct ? p.bpr / 8 : p.bpr;
+  auto tiles_for = [&](int r) {
+    if (a.pair) return (a.seg[0].rows + r - 1) / r;
+    int n = 0;
+    for (int s = 0; s < a.nseg; s++) n += (a.seg[s].rows + r - 1) / r;
+    return n;
+  };
+  // Shared memory before the stage ring: barriers | activations | term buffers
+  // (which double as the f32 staging row of the prologue).
+  size_t off = 2 * MAX_STAGES * 8;
+  const size_t x_off = off;
   if (a.fmt == FMT_Q8_0)
     off += (size_t)NTc * p.n_oct * XW * 4;
   else
@@ -737,46 +850,44 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   if (a.fmt != FMT_Q8_0) off += (size_t)NTc * p.bpr * 8 * 4;
   off = (off + 15) & ~(size_t)15;
   const size_t t_off = off;
-  const int span_mult = a.pair ? 2 : 1;
-  auto tiles_for = [&](int rt) {
-    if (a.pair) return (a.seg[0].rows + rt - 1) / rt;
-    int n = 0;
-    for (int s = 0; s < a.nseg; s++) n += (a.seg[s].rows + rt - 1) / rt;
-    return n;
-  };
-  auto tbytes = [&](int rt) {
-    size_t t = (size_t)2 * span_mult * rt * NTc * (p.bpr + 1) * 4;
-    const size_t xs = xmode ? (size_t)a.K * 4 : 0;
-    return t > xs ? t : xs;
-  };
-  int RT = std::max(1, 32 / NTc);
-  while (RT > 1 && tiles_for(RT) < 4 * di.sms) RT /= 2;
   const size_t opt_limit = (size_t)di.smem_optin - SMEM_RESERVE;
-  const size_t two_limit = (size_t)di.smem_per_sm / 2 - SMEM_RESERVE;
-  // Two CTAs per SM when at least 3 stages fit in half an SM, else one CTA with up to 8 stages.
+  // Rows per tile: about STAGE_TARGET bytes, at most 32 (row, token) chains
+  // per warp, enough tiles for every SM. Then fewer rows, then fewer owning
+  // warps, until the term buffers and the ring fit.
+  int R = std::max(1, std::min(32 / NTc, STAGE_TARGET / (nspan * p.row_bytes)));
+  while (R > 1 && tiles_for(R) < di.sms) R--;
   int nstage = 0;
-  for (int rt = RT; rt >= 1 && nstage == 0; rt /= 2) {
-    const size_t rest = off + tbytes(rt);
-    if (NTc <= 2 && rest + 3 * (size_t)STAGE_BUF <= two_limit) {
-      nstage = (int)std::min<size_t>(MAX_STAGES, (two_limit - rest) / STAGE_BUF);
-      RT = rt;
-    } else if (rest + 3 * (size_t)STAGE_BUF <= opt_limit) {
-      nstage = (int)std::min<size_t>(MAX_STAGES, (opt_limit - rest) / STAGE_BUF);
-      RT = rt;
+  size_t tbytes = 0;
+  for (int ncw = NCW; ncw >= 1 && nstage == 0; ncw--) {
+    for (int r = R; r >= 1; r--) {
+      p.R = r;
+      p.ncw = ncw;
+      p.span_stride = (int)(((size_t)r * p.row_bytes + 32 + 15) & ~(size_t)15);
+      p.stage_bytes = nspan * p.span_stride;
+      p.tb_warp = nspan * r * NTc * (p.bpr + 1);
+      tbytes = (size_t)ncw * p.tb_warp * 4;
+      if (xmode && (size_t)a.K * 4 > tbytes) tbytes = (size_t)a.K * 4;
+      const size_t rest = off + tbytes;
+      if (2 * ncw <= MAX_STAGES && rest + (size_t)2 * ncw * p.stage_bytes <= opt_limit) {
+        nstage = 2 * ncw;
+        break;
+      }
+      if (rest + (size_t)ncw * p.stage_bytes <= opt_limit) {
+        nstage = ncw;
+        break;
+      }
     }
-    if (rt == 1) break;
   }
-  if (nstage < 3) return cudaErrorInvalidValue;
+  if (nstage == 0) return cudaErrorInvalidValue;
   p.nstage = nstage;
-  p.RT = RT;
-  p.t_elems = span_mult * RT * NTc * (p.bpr + 1);
-  p.xs_floats = (int)(tbytes(RT) / 4);
-  const size_t stage_bytes = (size_t)nstage * STAGE_BUF;
-  p.off_x = (int)(stage_bytes + x_off);
-  p.off_xd = (int)(stage_bytes + xd_off);
-  p.off_xb = (int)(stage_bytes + xb_off);
-  p.off_t = (int)(stage_bytes + t_off);
-  const size_t smem = stage_bytes + off + tbytes(RT);
+  p.xs_floats = (int)(tbytes / 4);
+  const size_t stage_total = (size_t)nstage * p.stage_bytes;
+  p.off_x = (int)(stage_total + x_off);
+  p.off_xd = (int)(stage_total + xd_off);
+  p.off_xb = (int)(stage_total + xb_off);
+  p.off_t = (int)(stage_total + t_off);
+  const size_t smem = stage_total + off + tbytes;
+  const int RT = p.R;
   p.ntiles = 0;
   if (a.pair) {
     p.ntiles = (a.seg[0].rows + RT - 1) / RT;
@@ -793,7 +904,7 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   KernelFn fn = pick_kernel(a.fmt, NTc, xmode, aligned ? 1 : 0);
   const int occ = occupancy(fn, (int)smem, di.smem_optin);
   if (occ < 1) return cudaErrorInvalidConfiguration;
-  const int grid = std::min(p.ntiles, di.sms * occ);
+  const int grid = std::min(p.ntiles, di.sms);
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);

@@ -23,6 +23,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "mma.cuh"
+#include "seqsum.cuh"
 
 namespace nrc {
 namespace {
@@ -363,15 +364,15 @@ __global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Para
 // ------------------------------------------------------------ activation quantization
 // One CTA (256 threads) per token: optional RMSNorm (the same reduction order
 // as the GEMV prologue, so both paths derive identical activations), then
-// q8::quantize per 32-value block into the canonical per-block tiles.
+// q8::quantize, one thread per 32-value block, into the canonical tiles.
 __global__ void __launch_bounds__(256) k_mma_quant_act(const MmaActArgs a) {
   pdl_wait();
   pdl_trigger();
   const int n = blockIdx.x;  // token slot (0 .. ntg*NS - 1)
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   const int bpr = a.K / 32;
   const int tg = n / a.NS, nn = n % a.NS;
-  __shared__ float red[8];
+  __shared__ SeqSumShared ssh;
   if (n >= a.nt) {
     for (int b = tid; b < bpr; b += 256) {
       uint8_t* t = a.xq + ((size_t)tg * bpr + b) * a.NS * 32;
@@ -387,30 +388,43 @@ __global__ void __launch_bounds__(256) k_mma_quant_act(const MmaActArgs a) {
   __syncthreads();
   float sc = 1.0f;
   if (a.norm_w) {
-    // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order.
-    if (tid == 0) {
-      float ss = 0.0f;
-#pragma unroll 8
-      for (int i = 0; i < a.K; i++) ss = __fadd_rn(ss, __fmul_rn(xrow[i], xrow[i]));
-      red[0] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps)));
-    }
-    __syncthreads();
-    sc = red[0];
+    // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain, seqsum.cuh).
+    const float ss = seq_sum_group<256>(
+        a.K, [&](int i) { return __fmul_rn(xrow[i], xrow[i]); }, ssh, tid, [] { __syncthreads(); });
+    sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps)));
   }
-  for (int b = warp; b < bpr; b += 8) {
-    float v = xrow[b * 32 + lane];
-    if (a.norm_w) v = __fmul_rn(__fmul_rn(v, sc), a.norm_w[b * 32 + lane]);
-    const float amax = warp_max(fabsf(v));
+  // q8::quantize (q8.rs:27-44), one thread per 32-value block.
+  for (int b = tid; b < bpr; b += 256) {
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; k++) {
+      v[k] = xrow[b * 32 + k];
+      if (a.norm_w) v[k] = __fmul_rn(__fmul_rn(v[k], sc), __ldg(a.norm_w + b * 32 + k));
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
     const uint16_t dbits = f32_to_f16(__fdiv_rn(amax, 127.0f));
     const float d = f16_to_f32(dbits);
     const float inv = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-    const float xs = __fmul_rn(v, inv);
-    const float r = xs >= 0.0f ? __fadd_rn(xs, 0.5f) : __fsub_rn(xs, 0.5f);
-    int q = rust_f2i(r);
-    q = q < -127 ? -127 : (q > 127 ? 127 : q);
+    uint32_t pk[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      uint32_t wv = 0;
+#pragma unroll
+      for (int k = 0; k < 4; k++) {
+        const float xsv = __fmul_rn(v[4 * c + k], inv);
+        const float r = xsv >= 0.0f ? __fadd_rn(xsv, 0.5f) : __fsub_rn(xsv, 0.5f);
+        int q = rust_f2i(r);
+        q = q < -127 ? -127 : (q > 127 ? 127 : q);
+        wv |= (uint32_t)(uint8_t)(int8_t)q << (8 * k);
+      }
+      pk[c] = wv;
+    }
     uint8_t* t = a.xq + ((size_t)tg * bpr + b) * a.NS * 32;
-    t[canon_off(nn, lane >> 4) + (lane & 15)] = (uint8_t)(int8_t)q;
-    if (lane == 0) a.xd[((size_t)tg * bpr + b) * a.NS + nn] = d;
+    *reinterpret_cast<uint4*>(t + canon_off(nn, 0)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    *reinterpret_cast<uint4*>(t + canon_off(nn, 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    a.xd[((size_t)tg * bpr + b) * a.NS + nn] = d;
   }
 }
 

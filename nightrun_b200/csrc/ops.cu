@@ -3,6 +3,7 @@
 // uses the same arithmetic inside its GEMV prologues/epilogues and attention.
 #include "common.cuh"
 #include "expf_cr.cuh"
+#include "seqsum.cuh"
 #include "ops.cuh"
 
 namespace nrc {
@@ -173,49 +174,43 @@ NRC_DEV float block_max(float m, float* red) {
   return t;
 }
 
-// Sequential f32 sum of v[0..n) in index order (the reference's `+=` loops).
-NRC_DEV float seq_sum_sq(const float* v, int n) {
-  float s = 0.0f;
-#pragma unroll 8
-  for (int i = 0; i < n; i++) s = __fadd_rn(s, __fmul_rn(v[i], v[i]));
-  return s;
-}
-
-// vec::rmsnorm (vec.rs:4-14), one CTA per row: the sum of squares runs in
-// index order (one thread), the scaling in parallel.
+// vec::rmsnorm (vec.rs:4-14), one CTA per row: the sum of squares in index
+// order (one chain, seqsum.cuh) over the row staged in shared memory when it
+// fits, the scaling in parallel.
 __global__ void k_rmsnorm(float* __restrict__ out, const float* __restrict__ x, const float* __restrict__ w,
-                          int n, float eps) {
-  __shared__ float scale_sh;
+                          int n, float eps, int staged) {
+  __shared__ SeqSumShared sh;
+  extern __shared__ float row[];
   const float* xr = x + (size_t)blockIdx.x * n;
   float* orow = out + (size_t)blockIdx.x * n;
-  if (threadIdx.x == 0) {
-    const float ss = seq_sum_sq(xr, n);
-    scale_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+  const float* src = xr;
+  if (staged) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) row[i] = xr[i];
+    __syncthreads();
+    src = row;
   }
-  __syncthreads();
-  const float scale = scale_sh;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(xr[i], scale), w[i]);
+  const float ss = seq_sum_group<256>(
+      n, [&](int i) { return __fmul_rn(src[i], src[i]); }, sh, (int)threadIdx.x, [] { __syncthreads(); });
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(src[i], scale), w[i]);
 }
 
 // vec::softmax (vec.rs:30-41), one CTA per row, in place: max (order-free),
-// exponentials in parallel, their sum in index order, then the scaling.
-__global__ void k_softmax(float* __restrict__ x, int n) {
+// exponentials in parallel, their sum in index order (one chain), then the scaling.
+__global__ void k_softmax(float* __restrict__ x, int n, int staged) {
   __shared__ float red[32];
-  __shared__ float inv_sh;
+  __shared__ SeqSumShared sh;
+  extern __shared__ float row[];
   float* xr = x + (size_t)blockIdx.x * n;
+  float* e = staged ? row : xr;
   float m = -INFINITY;
   for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, xr[i]);
   m = block_max(m, red);
-  for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = expf_cr(__fsub_rn(xr[i], m));
+  for (int i = threadIdx.x; i < n; i += blockDim.x) e[i] = expf_cr(__fsub_rn(xr[i], m));
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float s = 0.0f;
-    for (int i = 0; i < n; i++) s = __fadd_rn(s, xr[i]);
-    inv_sh = __fdiv_rn(1.0f, s);
-  }
-  __syncthreads();
-  const float inv = inv_sh;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __fmul_rn(xr[i], inv);
+  const float sum = seq_sum_group<256>(n, [&](int i) { return e[i]; }, sh, (int)threadIdx.x, [] { __syncthreads(); });
+  const float inv = __fdiv_rn(1.0f, sum);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __fmul_rn(e[i], inv);
 }
 
 // vec::swiglu (vec.rs:44-50).
@@ -306,11 +301,13 @@ cudaError_t op_f16_to_f32(const uint16_t* x, float* o, size_t n, cudaStream_t s)
 }
 cudaError_t op_rmsnorm(float* out, const float* x, const float* w, size_t n, size_t rows, float eps,
                        cudaStream_t s) {
-  if (rows && n) k_rmsnorm<<<(unsigned)rows, 256, 0, s>>>(out, x, w, (int)n, eps);
+  const int staged = n <= 12288;  // the row fits the default 48 KB of dynamic shared memory
+  if (rows && n) k_rmsnorm<<<(unsigned)rows, 256, staged ? n * 4 : 0, s>>>(out, x, w, (int)n, eps, staged);
   return cudaGetLastError();
 }
 cudaError_t op_softmax(float* x, size_t n, size_t rows, cudaStream_t s) {
-  if (rows && n) k_softmax<<<(unsigned)rows, 256, 0, s>>>(x, (int)n);
+  const int staged = n <= 12288;
+  if (rows && n) k_softmax<<<(unsigned)rows, 256, staged ? n * 4 : 0, s>>>(x, (int)n, staged);
   return cudaGetLastError();
 }
 cudaError_t op_swiglu(float* g, const float* u, size_t n, cudaStream_t s) {

@@ -41,13 +41,24 @@ struct RopeArgs {
 cudaError_t rope_append_run(const RopeArgs& a, cudaStream_t s, bool pdl);
 
 struct AttnArgs {
-  const float* q;  // [nt][att_dim] (rotated)
-  float* out;      // [nt][att_dim]
-  const uint16_t* kcache;
-  const uint16_t* vcache;
+  float* q;           // [nt][att_dim]: rotated by rope_append, or raw when fused
+  float* out;         // [nt][att_dim]
+  uint16_t* kcache;   // this layer's [ctx][kv_dim]
+  uint16_t* vcache;
   float scale;
   int nt, n_heads, n_kv_heads, head_dim, ctx;
   const uint32_t* pos_dev;
+  // Decode (nt == 1) with the per-head norms, RoPE and the KV append fused in
+  // (then q, k, v are the raw projections of the token).
+  int fused;
+  const float* k;
+  const float* v;
+  const float* q_norm;
+  const float* k_norm;
+  float eps;
+  const float* cos_tab;
+  const float* sin_tab;
+  int style;
 };
 // Shared memory of one attention CTA (its score rows hold `ctx` positions);
 // contexts needing more than ATTN_MAX_SMEM are rejected at context creation.
