@@ -277,8 +277,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
     if (d < hd) {
       const uint16_t* vr = vb + d;
       const float* p = sc + t0;
-#pragma unroll 4
-      for (int t = 0; t < tn; t++) acc = __fadd_rn(acc, __fmul_rn(p[t], h2f(vr[(size_t)t * hd])));
+      acc = seq_sum_serial(tn, [&](int t) { return __fmul_rn(p[t], h2f(vr[(size_t)t * hd])); }, acc);
     }
     __syncthreads();  // the buffer is restaged two chunks later
   }

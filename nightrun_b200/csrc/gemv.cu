@@ -684,12 +684,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
       const float* tp = tbw + (size_t)(c_r * NT + c_tok) * TS;
       if (nspan == 2) {
         const float* tu = tbw + (size_t)((R + c_r) * NT + c_tok) * TS;
-        for (int b = 0; b < bpr; b++) {
-          acc = __fadd_rn(acc, tp[b]);
-          acc_u = __fadd_rn(acc_u, tu[b]);
-        }
+        seq_sum_serial2(bpr, [&](int b) { return tp[b]; }, [&](int b) { return tu[b]; }, acc, acc_u);
       } else {
-        for (int b = 0; b < bpr; b++) acc = __fadd_rn(acc, tp[b]);
+        acc = seq_sum_serial(bpr, [&](int b) { return tp[b]; });
       }
       const int row = sp0.row0 + c_r;
       if (p.epi == EPI_SWIGLU) {

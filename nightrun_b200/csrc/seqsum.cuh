@@ -11,25 +11,72 @@
 
 namespace nrc {
 
-// ((0 + t(0)) + t(1)) + ... + t(n-1), on the calling thread.
+// ((init + t(0)) + t(1)) + ... + t(n-1), on the calling thread. Whole blocks of
+// W terms are fetched one block ahead of their adds with no per-term
+// conditions (so every fetch is issued before the adds that precede its use);
+// the last n mod W terms follow one by one.
 template <class Term>
-NRC_DEV float seq_sum_serial(int n, const Term& term) {
+NRC_DEV float seq_sum_serial(int n, const Term& term, float init = 0.0f) {
   constexpr int W = 16;
-  float s = 0.0f;
-  float cur[W];
+  float s = init;
+  const int nfull = n - n % W;
+  if (nfull > 0) {
+    float cur[W];
 #pragma unroll
-  for (int j = 0; j < W; j++) cur[j] = j < n ? term(j) : 0.0f;
-  for (int i = 0; i < n; i += W) {
-    float nxt[W];
+    for (int j = 0; j < W; j++) cur[j] = term(j);
+    for (int i = 0; i < nfull; i += W) {
+      const int nb = i + W < nfull ? i + W : i;  // the next block (the last one again at the end)
+      float nxt[W];
 #pragma unroll
-    for (int j = 0; j < W; j++) nxt[j] = i + W + j < n ? term(i + W + j) : 0.0f;
+      for (int j = 0; j < W; j++) nxt[j] = term(nb + j);
 #pragma unroll
-    for (int j = 0; j < W; j++)
-      if (i + j < n) s = __fadd_rn(s, cur[j]);
+      for (int j = 0; j < W; j++) s = __fadd_rn(s, cur[j]);
 #pragma unroll
-    for (int j = 0; j < W; j++) cur[j] = nxt[j];
+      for (int j = 0; j < W; j++) cur[j] = nxt[j];
+    }
   }
+  for (int i = nfull; i < n; i++) s = __fadd_rn(s, term(i));
   return s;
+}
+
+// Two independent chains over the same index range (their adds interleave).
+template <class TermA, class TermB>
+NRC_DEV void seq_sum_serial2(int n, const TermA& ta, const TermB& tb, float& sa, float& sb) {
+  constexpr int W = 8;
+  sa = 0.0f;
+  sb = 0.0f;
+  const int nfull = n - n % W;
+  if (nfull > 0) {
+    float ca[W], cb[W];
+#pragma unroll
+    for (int j = 0; j < W; j++) {
+      ca[j] = ta(j);
+      cb[j] = tb(j);
+    }
+    for (int i = 0; i < nfull; i += W) {
+      const int nb = i + W < nfull ? i + W : i;
+      float na[W], nbv[W];
+#pragma unroll
+      for (int j = 0; j < W; j++) {
+        na[j] = ta(nb + j);
+        nbv[j] = tb(nb + j);
+      }
+#pragma unroll
+      for (int j = 0; j < W; j++) {
+        sa = __fadd_rn(sa, ca[j]);
+        sb = __fadd_rn(sb, cb[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < W; j++) {
+        ca[j] = na[j];
+        cb[j] = nbv[j];
+      }
+    }
+  }
+  for (int i = nfull; i < n; i++) {
+    sa = __fadd_rn(sa, ta(i));
+    sb = __fadd_rn(sb, tb(i));
+  }
 }
 
 struct SeqSumShared {
