@@ -146,6 +146,11 @@ NRC_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// Fire-and-forget prefetch of [src, src + bytes) into L2 (both 16-byte
+// multiples); nothing waits for it.
+NRC_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 // L2 policy for weights that are streamed once per step: evict first, so the
 // activations and KV rows stay resident.
 NRC_DEV uint64_t l2_evict_first() {

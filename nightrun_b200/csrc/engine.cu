@@ -748,7 +748,23 @@ struct Lin {
   int rows[3];
   int nseg;
   int epi;
+  // Weights of the next linear layer, prefetched into L2 while this one runs.
+  const uint8_t* pf;
+  size_t pf_bytes;
 };
+
+// Bytes of a rows x K matrix of format fmt.
+size_t mat_bytes(int fmt, int rows, int K) {
+  const size_t bb = fmt == FMT_Q8_0 ? 34 : (fmt == FMT_Q4K ? 144 : 210);
+  const size_t blk = fmt == FMT_Q8_0 ? 32 : 256;
+  return (size_t)rows * (K / blk) * bb;
+}
+// One byte range covering matrices a and b when they sit back to back (the
+// .nrm layout keeps a layer's tensors together), else just a.
+void span2(const uint8_t* a, size_t na, const uint8_t* b, size_t nb, const uint8_t** p, size_t* n) {
+  *p = a;
+  *n = (b >= a && b <= a + na + 256) ? (size_t)(b - a) + nb : na;
+}
 
 cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
   cudaStream_t s = c->stream;
@@ -798,6 +814,8 @@ cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
     a.resid_ld = c->dim;
     a.rs = c->rs;
   }
+  a.pf = L.pf;
+  a.pf_bytes = L.pf_bytes;
   return gemv_tokens(a, nt, L.K, s, pdl);
 }
 
@@ -809,8 +827,24 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
   cudaError_t e;
   EmbedArgs ea{c->embed, c->f_embed, c->dim, c->embed_scale, c->st->tok, nt, c->x, &c->st->key};
   if ((e = embed_run(ea, s, pdl))) return e;
+  // Weight regions of each layer's linear layers, for the L2 prefetch hints.
+  auto qkv_region = [&](const LayerW& w, const uint8_t** p, size_t* n) {
+    const uint8_t* pq;
+    size_t nq;
+    span2(w.wq, mat_bytes(w.fq, c->att_dim, c->dim), w.wk, mat_bytes(w.fk, c->kv_dim, c->dim), &pq, &nq);
+    span2(pq, nq, w.wv, mat_bytes(w.fv, c->kv_dim, c->dim), p, n);
+  };
   for (int l = 0; l < c->n_layers; l++) {
     const LayerW& w = c->L[l];
+    const uint8_t *pf_o = w.wo, *pf_gu, *pf_d = w.wd, *pf_next;
+    size_t n_o = mat_bytes(w.fo, c->dim, c->att_dim), n_gu, n_d = mat_bytes(w.fd, c->dim, c->ffn), n_next;
+    span2(w.wg, mat_bytes(w.fg, c->ffn, c->dim), w.wu, mat_bytes(w.fu, c->ffn, c->dim), &pf_gu, &n_gu);
+    if (l + 1 < c->n_layers) {
+      qkv_region(c->L[l + 1], &pf_next, &n_next);
+    } else {
+      pf_next = c->out_w;  // the classifier: its first 48 MB (it is larger than L2)
+      n_next = std::min(mat_bytes(c->f_out, c->vocab, c->dim), (size_t)48 << 20);
+    }
     // QKV (infer.rs:527-531 / 620-637): rmsnorm + activation quantization fused
     // into the consumer; one launch per weight format.
     {
@@ -827,6 +861,8 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
         L.x = c->x;
         L.norm_w = w.attn_norm;
         L.epi = EPI_STORE;
+        L.pf = pf_o;
+        L.pf_bytes = n_o;
         for (int j = i; j < 3; j++)
           if (!done[j] && fs[j] == fs[i]) {
             L.w[L.nseg] = ws[j];
@@ -877,6 +913,8 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
       L.rows[0] = c->dim;
       L.nseg = 1;
       L.epi = EPI_RESID;
+      L.pf = pf_gu;
+      L.pf_bytes = n_gu;
       if ((e = linear(c, L, nt))) return e;
     }
     {  // SwiGLU MLP gate/up (infer.rs:577-581)
@@ -890,6 +928,8 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
       L.rows[0] = c->ffn;
       L.nseg = 1;
       L.epi = EPI_STORE;
+      L.pf = pf_d;
+      L.pf_bytes = n_d;
       if (w.fg == w.fu) {
         L.w[1] = w.wu;
         L.y[1] = c->u;
@@ -915,6 +955,8 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
       L.rows[0] = c->dim;
       L.nseg = 1;
       L.epi = EPI_RESID;
+      L.pf = pf_next;
+      L.pf_bytes = n_next;
       if ((e = linear(c, L, nt))) return e;
     }
   }

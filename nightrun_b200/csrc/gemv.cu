@@ -76,6 +76,8 @@ struct Params {
   float rs;
   unsigned long long* argmax_key;
   unsigned* err;
+  const uint8_t* pf;  // next kernel's weights to prefetch into L2 (16-byte aligned), or null
+  size_t pf_bytes;
   int off_x, off_xd, off_xb, off_t;  // shared-memory layout (bytes)
   int tb_warp;                       // floats of one warp's term buffer
   int xs_floats;                     // f32 staging floats at off_t (prologue)
@@ -554,9 +556,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
   if (warp == NCW) {
     // ----------------------------------------------------------- producer
     const uint64_t pol = l2_evict_first();
+    // This CTA's share of the next kernel's weights, split over the lanes.
+    bool pf_pending = p.pf != nullptr && p.pf_bytes >= 16;
+    auto prefetch_next = [&]() {
+      const size_t share = ((p.pf_bytes / gridDim.x) + 32 * 16 - 1) / (32 * 16) * (32 * 16);
+      const size_t lo = (size_t)blockIdx.x * share + (size_t)lane * (share / 32);
+      const size_t hi = lo + share / 32 < p.pf_bytes ? lo + share / 32 : (p.pf_bytes & ~(size_t)15);
+      for (size_t a = lo; a < hi; a += 65536) {
+        const size_t n = hi - a < 65536 ? hi - a : 65536;
+        bulk_prefetch_l2(p.pf + a, (uint32_t)n);
+      }
+      pf_pending = false;
+    };
     int it = 0;
     Span sp0, sp1;
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, it++) {
+      if (pf_pending && it == NS) prefetch_next();
       const int s = it % NS;
       if (it >= NS) {
         bool ok = true;
@@ -595,6 +610,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
       }
       __syncwarp();
     }
+    if (pf_pending) prefetch_next();
     // Drain: wait (bounded) for the copies of the last issued stages, so the
     // CTA never exits with a bulk copy in flight.
     if (lane == 0) {
@@ -820,6 +836,10 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   p.rs = a.rs;
   p.argmax_key = a.argmax_key;
   p.err = a.err;
+  if (a.pf && (reinterpret_cast<uintptr_t>(a.pf) & 15) == 0) {
+    p.pf = static_cast<const uint8_t*>(a.pf);
+    p.pf_bytes = a.pf_bytes & ~(size_t)15;
+  }
   const int xmode = a.xq ? 0 : 1;
   const int nspan = a.pair ? 2 : 1;
   const DevInfo di = dev_info();

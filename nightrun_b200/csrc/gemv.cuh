@@ -42,6 +42,11 @@ struct GemvArgs {
   float rs;
   unsigned long long* argmax_key;  // one key (token 0)
   unsigned* err;                   // device error word
+  // Optional L2 prefetch of the weights the next kernel will stream (a hint:
+  // results do not depend on it). Every CTA prefetches its share once its
+  // own first ring of stages is in flight.
+  const void* pf;
+  size_t pf_bytes;
 };
 
 // Launch on `stream`; `pdl` enables programmatic dependent launch.

@@ -154,16 +154,6 @@ __global__ void k_f16_to_f32(const uint16_t* __restrict__ x, float* __restrict__
   if (i < n) o[i] = f16_to_f32(x[i]);
 }
 
-// Deterministic block sum (fixed order: per-thread strided sums, xor tree, warps in order).
-NRC_DEV float block_sum(float s, float* red) {
-  s = warp_sum(s);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-  __syncthreads();
-  float t = 0.0f;
-  for (int w = 0; w < (int)(blockDim.x >> 5); w++) t = __fadd_rn(t, red[w]);
-  __syncthreads();
-  return t;
-}
 NRC_DEV float block_max(float m, float* red) {
   m = warp_max(m);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
