@@ -43,7 +43,6 @@ constexpr int NCW = 8;             // consumer warps
 constexpr int NC = NCW * 32;       // consumer threads
 constexpr int NTHREADS = NC + 32;  // + producer warp
 constexpr int MAX_STAGES = 16;
-constexpr int STAGE_TARGET = 12288;  // payload bytes per stage the host aims for
 constexpr int XW = 68;  // words per 256-byte activation group (64 + 4 pad: conflict-free LDS.128)
 constexpr int SMEM_RESERVE = 1024;  // static shared memory of the kernel, rounded up
 
@@ -113,7 +112,7 @@ NRC_DEV void unit_q8(const uint8_t* src, const uint32_t* xq, int xtok, const flo
   for (int k = 0; k < 8; k++) q[k] = __byte_perm(rw[k], rw[k + 1], 0x5432);
 #pragma unroll
   for (int tok = 0; tok < NT; tok++) {
-    if (tok < nt) {
+    if (NT == 1 || tok < nt) {
       const uint4* xv = reinterpret_cast<const uint4*>(xq + tok * xtok);
       const uint4 a = xv[0], b = xv[1];
       int acc = __dp4a((int)q[0], (int)a.x, 0);
@@ -130,14 +129,8 @@ NRC_DEV void unit_q8(const uint8_t* src, const uint32_t* xq, int xtok, const flo
   }
 }
 
-// Eight consecutive Q8_0 blocks (272 bytes, 16-byte aligned: 17 uint4).
-// Block j starts at byte 34j: even j at a word boundary (scale in the low
-// half, quants 2 bytes in), odd j at a half word (scale in the high half,
-// quants word aligned). kernels.rs:72-82 per block.
 template <int NT>
-NRC_DEV void unit_q8_oct(const uint8_t* src, const uint32_t* xq, int xtok, const float* xd, int nt, int bpr,
-                         float* t, int tstride) {
-  uint32_t w[68];
+NRC_DEV void oct_load(const uint8_t* src, uint32_t* w) {
   const uint4* s4 = reinterpret_cast<const uint4*>(src);
 #pragma unroll
   for (int i = 0; i < 17; i++) {
@@ -147,6 +140,10 @@ NRC_DEV void unit_q8_oct(const uint8_t* src, const uint32_t* xq, int xtok, const
     w[4 * i + 2] = v.z;
     w[4 * i + 3] = v.w;
   }
+}
+template <int NT>
+NRC_DEV void oct_compute(const uint32_t* w, const uint32_t* xq, int xtok, const float* xd, int nt, int bpr, float* t,
+                         int tstride) {
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int base = (j / 2) * 17;
@@ -165,7 +162,7 @@ NRC_DEV void unit_q8_oct(const uint8_t* src, const uint32_t* xq, int xtok, const
     const float dw = __half2float(__ushort_as_half((unsigned short)dbits));
 #pragma unroll
     for (int tok = 0; tok < NT; tok++) {
-      if (tok < nt) {
+      if (NT == 1 || tok < nt) {
         const uint4* xv = reinterpret_cast<const uint4*>(xq + tok * xtok + j * 8);
         const uint4 a = xv[0], b = xv[1];
         int acc = __dp4a((int)q[0], (int)a.x, 0);
@@ -180,6 +177,17 @@ NRC_DEV void unit_q8_oct(const uint8_t* src, const uint32_t* xq, int xtok, const
       }
     }
   }
+}
+// Eight consecutive Q8_0 blocks (272 bytes, 16-byte aligned: 17 uint4).
+// Block j starts at byte 34j: even j at a word boundary (scale in the low
+// half, quants 2 bytes in), odd j at a half word (scale in the high half,
+// quants word aligned). kernels.rs:72-82 per block.
+template <int NT>
+NRC_DEV void unit_q8_oct(const uint8_t* src, const uint32_t* xq, int xtok, const float* xd, int nt, int bpr,
+                         float* t, int tstride) {
+  uint32_t w[68];
+  oct_load<NT>(src, w);
+  oct_compute<NT>(w, xq, xtok, xd, nt, bpr, t, tstride);
 }
 
 // One Q4_K super-block (144 bytes). kquant.rs:192-218.
@@ -219,7 +227,7 @@ NRC_DEV void unit_q4k(const uint8_t* src, const uint32_t* xq, const float* xd, c
   }
 #pragma unroll
   for (int tok = 0; tok < NT; tok++) {
-    if (tok < nt) {
+    if (NT == 1 || tok < nt) {
       const uint32_t* xw = xq + tok * bpr * XW;
       float sum_q = 0.0f;
       int sum_m = 0;
@@ -260,7 +268,7 @@ NRC_DEV void unit_q6k(const uint8_t* src, const uint32_t* xq, const float* xd, i
   const float dw = f16_to_f32(rw[52] & 0xffffu);
 #pragma unroll
   for (int tok = 0; tok < NT; tok++) {
-    if (tok < nt) {
+    if (NT == 1 || tok < nt) {
       const uint32_t* xw = xq + tok * bpr * XW;
       float sum = 0.0f;
 #pragma unroll
@@ -555,51 +563,40 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
 
   if (warp == NCW) {
     // ----------------------------------------------------------- producer
-    const uint64_t pol = l2_evict_first();
-    // This CTA's share of the next kernel's weights, split over the lanes.
-    bool pf_pending = p.pf != nullptr && p.pf_bytes >= 16;
-    auto prefetch_next = [&]() {
-      const size_t share = ((p.pf_bytes / gridDim.x) + 32 * 16 - 1) / (32 * 16) * (32 * 16);
-      const size_t lo = (size_t)blockIdx.x * share + (size_t)lane * (share / 32);
-      const size_t hi = lo + share / 32 < p.pf_bytes ? lo + share / 32 : (p.pf_bytes & ~(size_t)15);
-      for (size_t a = lo; a < hi; a += 65536) {
-        const size_t n = hi - a < 65536 ? hi - a : 65536;
-        bulk_prefetch_l2(p.pf + a, (uint32_t)n);
-      }
-      pf_pending = false;
-    };
-    int it = 0;
-    Span sp0, sp1;
-    for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, it++) {
-      if (pf_pending && it == NS) prefetch_next();
-      const int s = it % NS;
-      if (it >= NS) {
-        bool ok = true;
-        if (lane == 0) ok = mbar_wait(&empty[s], ((it / NS) - 1) & 1);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok || abort_flag) {
-          if (lane == 0) {
-            abort_flag = 1;
-            atomicOr(p.err, ERR_WAIT_EMPTY);
-          }
+    // Lanes [0, nprod) issue the tiles (tile k by lane k mod nprod, which
+    // therefore owns the ring slots k mod NS); more issuing threads keep more
+    // copies in flight. The other lanes prefetch the next kernel's weights.
+    const int nprod = NS % 4 == 0 ? 4 : (NS % 2 == 0 ? 2 : 1);
+    if (lane < nprod) {
+      const uint64_t pol = l2_evict_first();
+      int last = -1;
+      int it = lane;
+      Span sp0, sp1;
+      for (int tile = blockIdx.x + lane * gridDim.x; tile < p.ntiles; tile += nprod * gridDim.x, it += nprod) {
+        const int s = it % NS;
+        if (it >= NS && (abort_flag || !mbar_wait(&empty[s], ((it / NS) - 1) & 1))) {
+          abort_flag = 1;
+          atomicOr(p.err, ERR_WAIT_EMPTY);
           break;
         }
-      }
-      tile_spans(p, tile, sp0, sp1);
-      uint8_t* sbuf = stages + (size_t)s * p.stage_bytes;
-      const SegRange g0 = seg_range(sp0, p.row_bytes);
-      const SegRange g1 = seg_range(sp1, p.row_bytes);
-      uint32_t total = 0;
-      for (int si = 0; si < nspan; si++) {
-        const SegRange g = si ? g1 : g0;
-        uint8_t* dst = sbuf + (size_t)si * p.span_stride;
-        for (uintptr_t a = g.g0 + lane; a < g.blo; a += 32) dst[a - g.a0] = *reinterpret_cast<const uint8_t*>(a);
-        for (uintptr_t a = (g.bhi > g.g0 ? g.bhi : g.g0) + lane; a < g.g1; a += 32)
-          dst[a - g.a0] = *reinterpret_cast<const uint8_t*>(a);
-        total += (uint32_t)(g.bhi - g.blo);
-      }
-      __syncwarp();
-      if (lane == 0) {
+        tile_spans(p, tile, sp0, sp1);
+        uint8_t* sbuf = stages + (size_t)s * p.stage_bytes;
+        const SegRange g0 = seg_range(sp0, p.row_bytes);
+        const SegRange g1 = seg_range(sp1, p.row_bytes);
+        uint32_t total = 0;
+        bool ragged = false;
+        for (int si = 0; si < nspan; si++) {
+          const SegRange g = si ? g1 : g0;
+          uint8_t* dst = sbuf + (size_t)si * p.span_stride;
+          for (uintptr_t a = g.g0; a < g.blo; a++) dst[a - g.a0] = *reinterpret_cast<const uint8_t*>(a);
+          for (uintptr_t a = (g.bhi > g.g0 ? g.bhi : g.g0); a < g.g1; a++)
+            dst[a - g.a0] = *reinterpret_cast<const uint8_t*>(a);
+          ragged |= g.g0 < g.blo || g.bhi < g.g1;
+          total += (uint32_t)(g.bhi - g.blo);
+        }
+        // Order these byte stores before this thread's later bulk copies into
+        // the same slot.
+        if (ragged) fence_proxy_async_smem();
         mbar_arrive_expect_tx(&full[s], total);
         for (int si = 0; si < nspan; si++) {
           const SegRange g = si ? g1 : g0;
@@ -607,15 +604,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
             bulk_g2s(sbuf + (size_t)si * p.span_stride + (g.blo - g.a0), reinterpret_cast<const void*>(g.blo),
                      (uint32_t)(g.bhi - g.blo), &full[s], pol);
         }
+        last = it;
       }
-      __syncwarp();
-    }
-    if (pf_pending) prefetch_next();
-    // Drain: wait (bounded) for the copies of the last issued stages, so the
-    // CTA never exits with a bulk copy in flight.
-    if (lane == 0) {
-      for (int k = it - 1; k >= 0 && k >= it - NS; k--) {
+      // Drain: wait (bounded) for this lane's copies still in flight, so the
+      // CTA never exits with a bulk copy pending.
+      for (int k = last; k >= 0 && k > last - NS; k -= nprod)
         if (!mbar_wait(&full[k % NS], (k / NS) & 1)) atomicOr(p.err, ERR_DRAIN);
+    } else if (p.pf != nullptr && p.pf_bytes >= 16 && blockIdx.x < p.ntiles) {
+      // Once this CTA's first tile has landed, prefetch its share of the next
+      // kernel's weights into L2 (a hint; nothing waits for it).
+      if (mbar_wait(&full[0], 0)) {
+        const int nl = 32 - nprod, l = lane - nprod;
+        const size_t share = ((p.pf_bytes / gridDim.x) + (size_t)nl * 16 - 1) / ((size_t)nl * 16) * ((size_t)nl * 16);
+        const size_t lo = (size_t)blockIdx.x * share + (size_t)l * (share / nl);
+        const size_t end = p.pf_bytes & ~(size_t)15;
+        const size_t hi = lo + share / nl < end ? lo + share / nl : end;
+        for (size_t a = lo; a < hi; a += 65536) {
+          const size_t n = hi - a < 65536 ? hi - a : 65536;
+          bulk_prefetch_l2(p.pf + a, (uint32_t)n);
+        }
       }
     }
     return;
@@ -665,11 +672,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
     const int nunits = nspan * nr * upr;
     // Unit u = (span, row, unit-in-row), walked with counters (no divisions).
     int uo = lane % upr, r = lane / upr, si = 0;
-    while (r >= nr) {
+    while (r >= nr && si < nspan) {
       r -= nr;
       si++;
     }
-    for (int u = lane; u < nunits; u += 32) {
+    bool released = false;
+    if (oct && nunits <= 32) {
+      // One octet per lane: copy it to registers and hand the stage back to
+      // the producer before the dot products, so the slot refills while this
+      // warp computes.
+      const bool has = lane < nunits;
+      uint32_t w[68];
+      const uint8_t* src = (si ? sb1 : sb0) + (size_t)r * p.row_bytes + (size_t)uo * p.unit_bytes;
+      if (has) oct_load<NT>(src, w);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      released = true;
+      if (has)
+        oct_compute<NT>(w, xq + uo * XW, xtok, xd + 8 * uo, p.nt, bpr,
+                        tbw + (size_t)((si * R + r) * NT) * TS + uo * 8, TS);
+    }
+    for (int u = released ? nunits : lane; u < nunits; u += 32) {
       const uint8_t* src = (si ? sb1 : sb0) + (size_t)r * p.row_bytes + (size_t)uo * p.unit_bytes;
       float* t = tbw + (size_t)((si * R + r) * NT) * TS + uo * bpu;
       if (FMT == FMT_Q8_0) {
@@ -692,7 +715,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (!released && lane == 0) mbar_arrive(&empty[s]);
     // Ordered chains: lane (r, tok) sums its row's terms in block order.
     const bool chain = lane < nr * NT && c_tok < p.nt;
     float acc = 0.0f, acc_u = 0.0f;
@@ -868,10 +891,11 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   off = (off + 15) & ~(size_t)15;
   const size_t t_off = off;
   const size_t opt_limit = (size_t)di.smem_optin - SMEM_RESERVE;
-  // Rows per tile: about STAGE_TARGET bytes, at most 32 (row, token) chains
-  // per warp, enough tiles for every SM. Then fewer rows, then fewer owning
-  // warps, until the term buffers and the ring fit.
-  int R = std::max(1, std::min(32 / NTc, STAGE_TARGET / (nspan * p.row_bytes)));
+  // Rows per tile: one unit per lane (one round) when rows are short, at
+  // least one row; at most 32 (row, token) chains per warp. Then fewer rows
+  // while tiles do not cover every SM, then fewer rows and owning warps until
+  // the term buffers and the ring fit.
+  int R = std::max(1, std::min(32 / NTc, 32 / (nspan * p.upr)));
   while (R > 1 && tiles_for(R) < di.sms) R--;
   int nstage = 0;
   size_t tbytes = 0;
@@ -883,7 +907,7 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
       p.stage_bytes = nspan * p.span_stride;
       p.tb_warp = nspan * r * NTc * (p.bpr + 1);
       tbytes = (size_t)ncw * p.tb_warp * 4;
-      if (xmode && (size_t)a.K * 4 > tbytes) tbytes = (size_t)a.K * 4;
+      if (xmode && (size_t)a.K * 4 > tbytes) tbytes = (size_t)a.K * 4;  // the prologue's f32 row
       const size_t rest = off + tbytes;
       if (2 * ncw <= MAX_STAGES && rest + (size_t)2 * ncw * p.stage_bytes <= opt_limit) {
         nstage = 2 * ncw;

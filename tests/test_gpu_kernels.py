@@ -284,6 +284,39 @@ def test_expf_every_binary32_input(K):
     assert np.array_equal(out.cpu().numpy().view(np.uint64), gold)
 
 
+def _sum_cases(n, seed):
+    r = np.random.default_rng(seed)
+    yield "normal", r.standard_normal(n).astype(F)
+    yield "wide", (r.standard_normal(n) * np.exp(r.uniform(-20, 20, n))).astype(F)
+    z = np.zeros(n, F)
+    z[r.integers(0, n, 3)] = 1.5
+    yield "mostly_zero", z
+    yield "integers", r.integers(-3, 4, n).astype(F)  # many exact half-way additions
+    yield "tiny", (r.standard_normal(n) * 1e-20).astype(F)  # subnormal squares
+    big = r.standard_normal(n).astype(F)
+    big[n // 2] = F(3e18)
+    yield "one_huge", big
+
+
+@pytest.mark.parametrize("n", [1, 63, 64, 65, 100, 1000, 2048, 4097, 8192, 8193, 20000])
+def test_exact_parallel_sums_adversarial(K, orc, n):
+    """rmsnorm's sum of squares and softmax's denominator are evaluated by a
+    whole CTA (seqsum.cuh) yet must equal the reference's sequential chain
+    bit for bit, on inputs chosen to stress binade crossings, half-way
+    roundings, subnormals and a single dominating term."""
+    w = (np.random.default_rng(n).standard_normal(n) + 1).astype(F)
+    for name, x in _sum_cases(n, n + 7):
+        out = torch.empty(n, dtype=torch.float32, device="cuda")
+        K.rmsnorm(out, dev(x), dev(w), 1e-5)
+        assert host_bytes(out) == orc.rmsnorm(x, w, 1e-5).tobytes(), f"rmsnorm {name} n={n}"
+        logits = (x / F(4)).astype(F)
+        st = dev(logits)
+        K.softmax(st)
+        ref = orc.softmax(logits)
+        got = st.cpu().numpy()
+        assert got.tobytes() == ref.tobytes(), f"softmax {name} n={n}"
+
+
 def test_argmax_first_max_and_edges(K):
     assert K.argmax(dev(np.array([0.1, 4.0, -2.0, 4.0], np.float32))) == 1  # kernels.rs:228-231
     assert K.argmax(dev(np.array([np.nan, -np.inf, 3.0, 3.0], np.float32))) == 2
