@@ -137,6 +137,33 @@ NRC_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 20000
   }
   return true;
 }
+// Shared-memory flags with acquire / release ordering at CTA scope: a
+// cheaper hand-off than an mbarrier when one warp publishes data to another.
+NRC_DEV uint32_t ld_acquire_smem(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+NRC_DEV void st_release_smem(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+// Bounded wait until the flag reaches `target` (flags only grow): gives up
+// after `limit_ns` of global time (the clock is read every 1024 polls).
+NRC_DEV bool flag_wait_geq(const uint32_t* p, uint32_t target, uint64_t limit_ns = 2000000000ull) {
+  if (ld_acquire_smem(p) >= target) return true;
+  uint64_t t0 = 0;
+  for (uint32_t k = 1;; k++) {
+    if (ld_acquire_smem(p) >= target) return true;
+    if ((k & 1023u) == 0) {
+      const uint64_t t = globaltimer();
+      if (t0 == 0)
+        t0 = t;
+      else if (t - t0 > limit_ns)
+        return false;
+    }
+  }
+}
+
 // 1-D TMA bulk copy global -> shared, completion counted on `bar` (tx bytes).
 // dst, src 16-byte aligned; bytes a multiple of 16. No cluster multicast.
 NRC_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {

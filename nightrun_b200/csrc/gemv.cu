@@ -25,10 +25,13 @@
 //    (row, token) adds the row's terms in block order, the reference's
 //    summation order, and applies the fused epilogue.
 #include <algorithm>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 
 #include "common.cuh"
@@ -141,7 +144,8 @@ NRC_DEV void oct_load(const uint8_t* src, uint32_t* w) {
     w[4 * i + 3] = v.w;
   }
 }
-template <int NT>
+// Terms of block j for token tok go to t[tok * tstride + j * JS].
+template <int NT, int JS = 1>
 NRC_DEV void oct_compute(const uint32_t* w, const uint32_t* xq, int xtok, const float* xd, int nt, int bpr, float* t,
                          int tstride) {
 #pragma unroll
@@ -173,7 +177,7 @@ NRC_DEV void oct_compute(const uint32_t* w, const uint32_t* xq, int xtok, const 
         acc = __dp4a((int)q[5], (int)b.y, acc);
         acc = __dp4a((int)q[6], (int)b.z, acc);
         acc = __dp4a((int)q[7], (int)b.w, acc);
-        t[tok * tstride + j] = __fmul_rn(__fmul_rn(i2f(acc), dw), xd[tok * bpr + j]);
+        t[tok * tstride + j * JS] = __fmul_rn(__fmul_rn(i2f(acc), dw), xd[tok * bpr + j]);
       }
     }
   }
@@ -318,7 +322,7 @@ NRC_DEV int xq_index(int fmt, const Params& p, int tok, int b) {
 // Each row is first copied to shared memory (`xs`, aliasing the term buffer)
 // with one coalesced pass; the norm's sum of squares uses one fixed order, so
 // every CTA and every launch derive identical activations.
-template <int FMT>
+template <int FMT, int NCT = NC>
 NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
   uint32_t* xq = reinterpret_cast<uint32_t*>(smem + p.off_x);
   float* xd = reinterpret_cast<float*>(smem + p.off_xd);
@@ -330,23 +334,23 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
   for (int tok = 0; tok < p.nt; tok++) {
     const float* src = p.xf + (size_t)tok * p.xf_ld;
     if ((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (K & 3) == 0) {
-      for (int i = tid; i < K / 4; i += NC) reinterpret_cast<float4*>(xs)[i] = reinterpret_cast<const float4*>(src)[i];
+      for (int i = tid; i < K / 4; i += NCT) reinterpret_cast<float4*>(xs)[i] = reinterpret_cast<const float4*>(src)[i];
     } else {
-      for (int i = tid; i < K; i += NC) xs[i] = src[i];
+      for (int i = tid; i < K; i += NCT) xs[i] = src[i];
     }
-    named_sync(1, NC);
+    named_sync(1, NCT);
     float sc = 1.0f;
     if (p.norm_w) {
       // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain,
       // seqsum.cuh), then scale = 1 / sqrtf(ss / n + eps).
-      const float ss = seq_sum_group<NC>(
-          K, [&](int i) { return __fmul_rn(xs[i], xs[i]); }, ssh, tid, [] { named_sync(1, NC); });
+      const float ss = seq_sum_group<NCT>(
+          K, [&](int i) { return __fmul_rn(xs[i], xs[i]); }, ssh, tid, [] { named_sync(1, NCT); });
       sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), p.eps)));
     }
     if (FMT == FMT_Q8_0) {
       // q8::quantize (q8.rs:27-44), one thread per 32-value block: all blocks
       // of the row at once.
-      for (int b = tid; b < p.bpr; b += NC) {
+      for (int b = tid; b < p.bpr; b += NCT) {
         const float4* x4 = reinterpret_cast<const float4*>(xs + b * 32);
         float v[32];
 #pragma unroll
@@ -388,7 +392,7 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
         xd[tok * p.bpr + b] = d;
       }
     } else {
-      for (int b = warp; b < p.bpr; b += NCW) {
+      for (int b = warp; b < p.bpr; b += NCT / 32) {
         const float4* s4 = reinterpret_cast<const float4*>(xs + b * 256 + lane * 8);
         const float4 va = s4[0], vb = s4[1];
         float v[8] = {va.x, va.y, va.z, va.w, vb.x, vb.y, vb.z, vb.w};
@@ -448,12 +452,12 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
         if (lane == 0) xd[tok * p.bpr + b] = __fdiv_rn(1.0f, iscale);
       }
     }
-    named_sync(1, NC);  // xs is reused by the next token / the term buffer
+    named_sync(1, NCT);  // xs is reused by the next token / the term buffer
   }
 }
 
 // Activations given as blocks in global memory (the kernel-level entry points).
-template <int FMT>
+template <int FMT, int NCT = NC>
 NRC_DEV void build_x_blocks(const Params& p, uint8_t* smem) {
   uint32_t* xq = reinterpret_cast<uint32_t*>(smem + p.off_x);
   float* xd = reinterpret_cast<float*>(smem + p.off_xd);
@@ -461,7 +465,7 @@ NRC_DEV void build_x_blocks(const Params& p, uint8_t* smem) {
   const int tid = threadIdx.x;
   const int nblk = p.nt * p.bpr;
   if (FMT == FMT_Q8_0) {
-    for (int i = tid; i < nblk; i += NC) {
+    for (int i = tid; i < nblk; i += NCT) {
       const int tok = i / p.bpr, b = i % p.bpr;
       const uint8_t* s = p.xq + (size_t)i * 34;
       uint32_t* dst = xq + xq_index(FMT_Q8_0, p, tok, b);
@@ -472,7 +476,7 @@ NRC_DEV void build_x_blocks(const Params& p, uint8_t* smem) {
       xd[tok * p.bpr + b] = f16_to_f32((uint32_t)s[0] | ((uint32_t)s[1] << 8));
     }
   } else {
-    for (int i = tid; i < nblk; i += NC) {
+    for (int i = tid; i < nblk; i += NCT) {
       const int tok = i / p.bpr, b = i % p.bpr;
       const uint32_t* s = reinterpret_cast<const uint32_t*>(p.xq + (size_t)i * 292);
       uint32_t* dst = xq + xq_index(FMT, p, tok, b);
@@ -541,11 +545,12 @@ NRC_DEV SegRange seg_range(const Span& sp, int row_bytes) {
 
 template <int FMT, int NT, int XMODE, int ALIGNED>
 __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant__ Params p) {
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* stages = smem;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)p.nstage * p.stage_bytes);
   uint64_t* empty = full + MAX_STAGES;
   __shared__ volatile int abort_flag;
+  __shared__ uint64_t pf_go;  // completes once: the ring's first stages are issued
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int NS = p.nstage;
   const int nspan = p.pair ? 2 : 1;
@@ -555,6 +560,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    mbar_init(&pf_go, NS % 4 == 0 ? 4 : (NS % 2 == 0 ? 2 : 1));  // one arrival per issuing lane
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -571,9 +577,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
       const uint64_t pol = l2_evict_first();
       int last = -1;
       int it = lane;
+      bool go = false;
       Span sp0, sp1;
       for (int tile = blockIdx.x + lane * gridDim.x; tile < p.ntiles; tile += nprod * gridDim.x, it += nprod) {
         const int s = it % NS;
+        if (!go && it >= NS) {
+          mbar_arrive(&pf_go);
+          go = true;
+        }
         if (it >= NS && (abort_flag || !mbar_wait(&empty[s], ((it / NS) - 1) & 1))) {
           abort_flag = 1;
           atomicOr(p.err, ERR_WAIT_EMPTY);
@@ -606,14 +617,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
         }
         last = it;
       }
+      if (!go) mbar_arrive(&pf_go);
       // Drain: wait (bounded) for this lane's copies still in flight, so the
       // CTA never exits with a bulk copy pending.
       for (int k = last; k >= 0 && k > last - NS; k -= nprod)
         if (!mbar_wait(&full[k % NS], (k / NS) & 1)) atomicOr(p.err, ERR_DRAIN);
     } else if (p.pf != nullptr && p.pf_bytes >= 16 && blockIdx.x < p.ntiles) {
-      // Once this CTA's first tile has landed, prefetch its share of the next
-      // kernel's weights into L2 (a hint; nothing waits for it).
-      if (mbar_wait(&full[0], 0)) {
+      // Once the issuing lanes have filled the ring, prefetch this CTA's share
+      // of the next kernel's weights into L2 (a hint; nothing waits for it).
+      if (mbar_wait(&pf_go, 0)) {
         const int nl = 32 - nprod, l = lane - nprod;
         const size_t share = ((p.pf_bytes / gridDim.x) + (size_t)nl * 16 - 1) / ((size_t)nl * 16) * ((size_t)nl * 16);
         const size_t lo = (size_t)blockIdx.x * share + (size_t)l * (share / nl);
@@ -758,6 +770,278 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
   }
 }
 
+// ============================================================ lane-per-row GEMV
+// Q8_0 weights whose rows are whole 16-byte aligned octets (K a multiple of
+// 256, 16-byte aligned matrices): the common case of every model here.
+//
+//  * a group is 32 consecutive rows, one per lane; a stage is one octet column
+//    of the group (32 rows x 272 bytes), fetched by one 2-D TMA tensor copy
+//    (no swizzle, no multicast). In shared memory a stage is 32 rows of 272
+//    bytes: 17 x 16 bytes, an odd number of 16-byte words, so the 32 lanes'
+//    16-byte loads of their own rows never share a bank;
+//  * stage i of the CTA goes to consumer warp i mod 16, which owns ring slot
+//    and term slot i mod 16: its lanes load their rows' octets to registers,
+//    hand the slot straight back (so every slot is in flight while its warp
+//    computes), form the 8 block terms per token exactly as the reference
+//    rounds them (kernels.rs:79) and park them in the term slot;
+//  * one chain warp takes the term slots in stage order and adds each row's
+//    terms to its running sum (lane = row), block by block, the reference's
+//    summation order (kernels.rs:72-82); after a group's last octet it runs
+//    the fused epilogue. Gate and up (SwiGLU pair) alternate stage by stage
+//    with one running sum each.
+constexpr int LR_CW = 16;                     // consumer warps (one ring slot each)
+constexpr int LR_THREADS = (LR_CW + 2) * 32;  // + chain warp + producer warp
+constexpr int LR_ROWS = 32;                   // rows per group, one per lane
+constexpr int LR_STAGE = LR_ROWS * 8 * Q8_0_BYTES;  // 8704 bytes, a multiple of 128
+
+struct LrParams {
+  CUtensorMap tmap[3];  // one per weight matrix: dims {row_bytes / 4, rows}, box {68, 32}
+  Params p;             // activations, prologue layout, epilogue (shared with gemv_kernel)
+  int group_start[4];   // first group of each matrix (pair: gate and up share groups)
+  int ngroups;
+  int spg;       // stages per group: n_oct (x 2 in pair mode)
+  int off_tr;    // term ring: LR_CW slots of NT x 8 x 32 floats (bytes from the dynamic base)
+  int off_bar;   // full / empty barriers of the ring
+  int rg;        // rows per group (32, or 16 when 32-row groups would leave SMs idle)
+};
+
+// 2-D tiled TMA load of one box into shared memory, completion counted on
+// `bar`. dst 128-byte aligned; x * 4 bytes a multiple of 16. No multicast.
+NRC_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// The group's matrix and first row.
+NRC_DEV void lr_group(const LrParams& lp, int g, int& seg, int& row0) {
+  seg = 0;
+  if (!lp.p.pair)
+    while (seg + 1 < lp.p.nseg && g >= lp.group_start[seg + 1]) seg++;
+  row0 = (g - lp.group_start[seg]) * lp.rg;
+}
+
+template <int NT, int XMODE>
+__global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_constant__ LrParams lp) {
+  const Params& p = lp.p;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* stages = smem;
+  constexpr int NS = LR_CW;  // ring slots = term slots = consumer warps
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + lp.off_bar);
+  uint64_t* empty = full + NS;
+  float* tring = reinterpret_cast<float*>(smem + lp.off_tr);
+  constexpr int TSF = NT * 8 * 32;  // floats per term slot
+  __shared__ volatile int abort_flag;
+  __shared__ uint64_t pf_go;     // completes once: the ring's first stages are issued
+  __shared__ uint32_t tflag[NS];  // stage i's terms are in slot i mod NS: tflag = i + 1
+  __shared__ uint32_t tcons;      // the chain warp has read stages < tcons
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int spg = lp.spg;
+  // This CTA's groups: blockIdx.x, + gridDim.x, ...; its stages: group-major.
+  const int my_groups = lp.ngroups > (int)blockIdx.x ? (lp.ngroups - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int nstages = my_groups * spg;
+  // Tensor copies need a 128-byte aligned destination: refuse to run otherwise.
+  if (smem_u32(smem) & 127u) {
+    if (tid == 0) atomicOr(p.err, ERR_DRAIN);
+    return;
+  }
+
+  if (tid == 0) {
+    for (int s = 0; s < NS; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      tflag[s] = 0;
+    }
+    tcons = 0;
+    mbar_init(&pf_go, 4);  // one arrival per issuing lane
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  if (warp == LR_CW + 1) {
+    // ----------------------------------------------------------- producer
+    // Lanes 0..3 issue (stage i by lane i mod 4, which therefore owns the ring
+    // slots i mod NS): a tensor copy takes a while to issue, so several
+    // issuing threads keep more copies in flight. The other lanes prefetch
+    // the next kernel's weights into L2 once the ring is filled.
+    constexpr int NPROD = 4;
+    if (lane < NPROD) {
+      const uint64_t pol = l2_evict_first();
+      int last = -1;
+      bool go = false;
+      for (int i = lane; i < nstages; i += NPROD) {
+        const int s = i % NS;
+        if (!go && i >= NS) {
+          mbar_arrive(&pf_go);
+          go = true;
+        }
+        if (i >= NS && (abort_flag || !mbar_wait(&empty[s], ((i / NS) - 1) & 1))) {
+          abort_flag = 1;
+          atomicOr(p.err, ERR_WAIT_EMPTY);
+          break;
+        }
+        const int gl = i / spg, q = i - gl * spg;
+        int seg, row0;
+        lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
+        const int o = p.pair ? q >> 1 : q;
+        const int m = p.pair ? (q & 1) : seg;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(lp.rg * 8 * Q8_0_BYTES));
+        tma_load_2d(stages + (size_t)s * LR_STAGE, &lp.tmap[m], o * (8 * Q8_0_BYTES / 4), row0, &full[s], pol);
+        last = i;
+      }
+      if (!go) mbar_arrive(&pf_go);
+      // Drain: wait (bounded) for this lane's copies still in flight.
+      for (int k = last; k >= 0 && k > last - NS; k -= NPROD)
+        if (!mbar_wait(&full[k % NS], (k / NS) & 1)) atomicOr(p.err, ERR_DRAIN);
+    } else if (p.pf != nullptr && p.pf_bytes >= 16) {
+      if (mbar_wait(&pf_go, 0)) {
+        const int nl = 32 - NPROD, l = lane - NPROD;
+        const size_t share = ((p.pf_bytes / gridDim.x) + (size_t)nl * 16 - 1) / ((size_t)nl * 16) * ((size_t)nl * 16);
+        const size_t lo = (size_t)blockIdx.x * share + (size_t)l * (share / nl);
+        const size_t end = p.pf_bytes & ~(size_t)15;
+        const size_t hi = lo + share / nl < end ? lo + share / nl : end;
+        for (size_t a = lo; a < hi; a += 65536) {
+          const size_t n = hi - a < 65536 ? hi - a : 65536;
+          bulk_prefetch_l2(p.pf + a, (uint32_t)n);
+        }
+      }
+    }
+    return;
+  }
+
+  if (warp == LR_CW) {
+    // -------------------------------------------------------- chain warp
+    // Hand-offs are plain shared-memory flags (acquire / release): this warp
+    // is the one serial stage of the pipeline, so its loop is kept short.
+    float acc[NT], accu[NT];
+#pragma unroll
+    for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
+    unsigned long long best = 0ull;
+    int q = 0, gl = 0;
+    for (int i = 0; i < nstages; i++) {
+      const int ts = i & (NS - 1);
+      const bool ok = __all_sync(0xffffffffu, flag_wait_geq(&tflag[ts], (uint32_t)i + 1));
+      if (!ok || abort_flag) {
+        if (lane == 0 && !abort_flag) {
+          abort_flag = 1;
+          atomicOr(p.err, ERR_WAIT_FULL);
+        }
+        break;
+      }
+      const float* tp = tring + ts * TSF + lane;
+      float v[NT][8];
+#pragma unroll
+      for (int t = 0; t < NT; t++)
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[t][j] = tp[(t * 8 + j) * 32];
+      __syncwarp();
+      if (lane == 0) st_release_smem(&tcons, (uint32_t)i + 1);
+      if (p.pair && (q & 1)) {
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+#pragma unroll
+          for (int j = 0; j < 8; j++) accu[t] = __fadd_rn(accu[t], v[t][j]);
+      } else {
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+#pragma unroll
+          for (int j = 0; j < 8; j++) acc[t] = __fadd_rn(acc[t], v[t][j]);
+      }
+      if (++q == spg) {
+        int seg, row0;
+        lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
+        const int row = row0 + lane;
+        if (lane < lp.rg && row < p.rows[seg]) {
+#pragma unroll
+          for (int t = 0; t < NT; t++) {
+            if (NT > 1 && t >= p.nt) break;
+            if (p.epi == EPI_SWIGLU) {
+              // vec::swiglu: silu = x / (1 + expf(-x)); gate = silu * up
+              const float silu = __fdiv_rn(acc[t], __fadd_rn(1.0f, expf_cr(-acc[t])));
+              p.y[0][(size_t)t * p.ld[0] + row] = __fmul_rn(silu, accu[t]);
+            } else if (p.epi == EPI_RESID) {
+              float* dst = p.resid + (size_t)t * p.resid_ld + row;
+              *dst = __fadd_rn(*dst, __fmul_rn(p.rs, acc[t]));
+            } else {
+              float sv = acc[t];
+              if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
+              p.y[seg][(size_t)t * p.ld[seg] + row] = sv;
+              if (p.epi == EPI_ARGMAX && t == 0 && argmax_candidate(sv)) {
+                const unsigned long long key = argmax_key(sv, (uint32_t)row);
+                best = key > best ? key : best;
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
+        q = 0;
+        gl++;
+      }
+    }
+    if (p.epi == EPI_ARGMAX) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        best = v > best ? v : best;
+      }
+      if (lane == 0 && best) atomicMax(p.argmax_key, best);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------- consumers
+  pdl_wait();
+  if (XMODE == 1)
+    build_x_f32<FMT_Q8_0, LR_CW * 32>(p, smem);
+  else
+    build_x_blocks<FMT_Q8_0, LR_CW * 32>(p, smem);
+  named_sync(1, LR_CW * 32);
+
+  const uint32_t* xq = reinterpret_cast<const uint32_t*>(smem + p.off_x);
+  const float* xd = reinterpret_cast<const float*>(smem + p.off_xd);
+  const int xtok = p.n_oct * XW;
+  const bool has = lane < lp.rg;
+  // Stage i = warp + k * NS: ring slot and term slot `warp`, parity k & 1.
+  int q = warp % spg;
+  const int qstep = NS % spg;
+  for (int i = warp, k = 0; i < nstages; i += NS, k++) {
+    const bool ok = __all_sync(0xffffffffu, !abort_flag && mbar_wait(&full[warp], k & 1));
+    if (!ok) {
+      if (lane == 0 && !abort_flag) {
+        abort_flag = 1;
+        atomicOr(p.err, ERR_WAIT_FULL);
+      }
+      break;
+    }
+    uint32_t w[68];
+    if (has) oct_load<NT>(stages + (size_t)warp * LR_STAGE + (size_t)lane * (8 * Q8_0_BYTES), w);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[warp]);
+    // The term slot is free once the chain warp has read its previous stage.
+    if (k > 0) {
+      const bool ok2 = __all_sync(0xffffffffu, !abort_flag && flag_wait_geq(&tcons, (uint32_t)(i - NS + 1)));
+      if (!ok2) {
+        if (lane == 0 && !abort_flag) {
+          abort_flag = 1;
+          atomicOr(p.err, ERR_WAIT_EMPTY);
+        }
+        break;
+      }
+    }
+    const int o = p.pair ? q >> 1 : q;
+    if (has) oct_compute<NT, 32>(w, xq + o * XW, xtok, xd + 8 * o, p.nt, p.bpr, tring + warp * TSF + lane, 8 * 32);
+    __syncwarp();
+    if (lane == 0) st_release_smem(&tflag[warp], (uint32_t)i + 1);
+    q += qstep;
+    if (q >= spg) q -= spg;
+  }
+}
+
 // ------------------------------------------------------------------ host side
 using KernelFn = void (*)(Params);
 
@@ -823,6 +1107,135 @@ int occupancy(KernelFn fn, int smem, int smem_optin) {
   return n;
 }
 
+// ------------------------------------------------------------- lane-per-row host
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// rows x (row_bytes / 4) u32 view of a Q8_0 matrix; box = one octet column of rg rows.
+bool encode_rows_map(CUtensorMap* m, const void* w, int rows, int row_bytes, int rg) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {8 * Q8_0_BYTES / 4, (cuuint32_t)rg};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(w), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+using LrFn = void (*)(LrParams);
+LrFn pick_lr(int NTc, int xmode) {
+  switch (NTc) {
+    case 1: return xmode ? gemv_lr_kernel<1, 1> : gemv_lr_kernel<1, 0>;
+    case 2: return xmode ? gemv_lr_kernel<2, 1> : gemv_lr_kernel<2, 0>;
+    default: return xmode ? gemv_lr_kernel<4, 1> : gemv_lr_kernel<4, 0>;
+  }
+}
+
+// Launch the lane-per-row kernel if the shape allows it. Returns false (and
+// launches nothing) when it does not; `*err` holds a launch error otherwise.
+bool gemv_lr_try(const GemvArgs& a, const Params& base, int NTc, int xmode, cudaStream_t stream, bool pdl,
+                 cudaError_t* err) {
+  *err = cudaSuccess;
+  if (a.fmt != FMT_Q8_0 || base.bpr % 8 != 0 || NTc > 4) return false;
+  for (int s = 0; s < a.nseg; s++)
+    if ((reinterpret_cast<uintptr_t>(a.seg[s].w) & 15) != 0) return false;
+  const DevInfo di = dev_info();
+  LrParams lp;
+  memset(&lp, 0, sizeof(lp));
+  lp.p = base;
+  Params& p = lp.p;
+  const int n_oct = p.bpr / 8;
+  const int nspan = a.pair ? 2 : 1;
+  lp.spg = n_oct * nspan;
+  const size_t ts_floats = (size_t)NTc * 8 * 32;
+  // Shared memory: ring | barriers | activations | term ring (doubles as the
+  // prologue's f32 staging row).
+  const size_t opt_limit = (size_t)di.smem_optin - SMEM_RESERVE;
+  const size_t x_bytes = (size_t)NTc * n_oct * XW * 4, xd_bytes = (size_t)NTc * p.bpr * 4;
+  // Every ring slot and term slot belongs to one consumer warp (LR_CW of each).
+  const size_t off_bar = (size_t)LR_CW * LR_STAGE;
+  const size_t off_x = off_bar + 2 * LR_CW * 8;
+  const size_t off_xd = off_x + x_bytes;
+  const size_t off_tr = (off_xd + xd_bytes + 127) & ~(size_t)127;
+  size_t tr = (size_t)LR_CW * ts_floats * 4;
+  if (xmode && (size_t)a.K * 4 > tr) tr = (size_t)a.K * 4;
+  const size_t total = off_tr + tr;
+  if (total > opt_limit) return false;
+  // Rows per group: 32, or 16 when that still gives every SM at most one
+  // group (small matrices: twice the SMs stream, half the lanes idle).
+  auto groups_for = [&](int rg) {
+    int n = 0;
+    if (a.pair) return (a.seg[0].rows + rg - 1) / rg;
+    for (int s = 0; s < a.nseg; s++) n += (a.seg[s].rows + rg - 1) / rg;
+    return n;
+  };
+  lp.rg = groups_for(16) <= di.sms ? 16 : LR_ROWS;
+  int ng = 0;
+  if (a.pair) {
+    ng = groups_for(lp.rg);
+    lp.group_start[0] = 0;
+    lp.group_start[1] = ng;
+  } else {
+    for (int s = 0; s < a.nseg; s++) {
+      lp.group_start[s] = ng;
+      ng += (a.seg[s].rows + lp.rg - 1) / lp.rg;
+    }
+    lp.group_start[a.nseg] = ng;
+  }
+  if (ng == 0) return true;
+  for (int s = 0; s < a.nseg; s++)
+    if (!encode_rows_map(&lp.tmap[s], a.seg[s].w, a.seg[s].rows, p.row_bytes, lp.rg)) {
+      *err = cudaErrorNotSupported;
+      return true;
+    }
+  lp.ngroups = ng;
+  lp.off_tr = (int)off_tr;
+  lp.off_bar = (int)off_bar;
+  p.nstage = LR_CW;
+  p.n_oct = n_oct;
+  p.off_x = (int)off_x;
+  p.off_xd = (int)off_xd;
+  p.off_xb = (int)off_xd;
+  p.off_t = (int)off_tr;
+  p.xs_floats = (int)((total - off_tr) / 4);
+  LrFn fn = pick_lr(NTc, xmode);
+  {
+    static std::mutex mu;
+    static std::map<std::pair<int, void*>, bool> attr_set;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    if (!attr_set[std::make_pair(dev, (void*)fn)]) {
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)opt_limit);
+      attr_set[std::make_pair(dev, (void*)fn)] = true;
+    }
+  }
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(std::min(ng, di.sms));
+  cfg.blockDim = dim3(LR_THREADS);
+  cfg.dynamicSmemBytes = total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  *err = cudaLaunchKernelEx(&cfg, fn, lp);
+  return true;
+}
+
 }  // namespace
 
 cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
@@ -864,6 +1277,10 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     p.pf_bytes = a.pf_bytes & ~(size_t)15;
   }
   const int xmode = a.xq ? 0 : 1;
+  {
+    cudaError_t lr_err;
+    if (gemv_lr_try(a, p, NTc, xmode, stream, pdl, &lr_err)) return lr_err;
+  }
   const int nspan = a.pair ? 2 : 1;
   const DevInfo di = dev_info();
   // Units: aligned octets of Q8_0 blocks when every row starts 16-byte aligned.

@@ -167,6 +167,21 @@ def test_matmul_bit_exact_and_equals_matvec(K, orc, fmt, batch):
         assert one.tobytes() == got[b].tobytes()
 
 
+@pytest.mark.parametrize("batch", [1, 2, 3, 4])
+@pytest.mark.parametrize("shape", [(100, 512), (33, 2048), (64, 8192), (1, 256), (2500, 512), (4099, 256)])
+def test_matvec_q8_whole_octet_rows(K, orc, shape, batch):
+    """Q8_0 rows of whole 16-byte aligned octets (cols % 256 == 0), 1-4 tokens:
+    the lane-per-row kernel (16- or 32-row groups, one row per lane, 2-D
+    tensor copies, block terms chained in order by one warp). Partial last
+    groups read zero-filled rows that are never stored."""
+    rows, cols = shape
+    w = make_weights(orc, "q8_0", rows, cols, 60 + rows + batch, adversarial=(batch % 2 == 0))
+    xs = make_acts(orc, "q8_0", cols, 61 + batch, batch)
+    ref = orc.matmul("q8_0", w, xs, rows, cols, batch)
+    got = gpu_matmul(K, "q8_0", w, xs, rows, cols, batch)
+    assert got.tobytes() == ref.tobytes(), f"{rows}x{cols} b{batch}: max diff {np.nanmax(np.abs(got - ref))}"
+
+
 @pytest.mark.parametrize("shape", [(300, 2048), (130, 512), (2048, 2048), (64, 8192), (128, 256), (1, 768)])
 @pytest.mark.parametrize("batch", [9, 16, 17, 33, 64, 100])
 def test_matmul_q8_tensor_core_bit_exact(K, orc, shape, batch):
