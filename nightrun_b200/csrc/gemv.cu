@@ -317,6 +317,47 @@ NRC_DEV int xq_index(int fmt, const Params& p, int tok, int b) {
   return fmt == FMT_Q8_0 ? (tok * p.n_oct + b / 8) * XW + (b % 8) * 8 : (tok * p.bpr + b) * XW;
 }
 
+// q8::quantize (q8.rs:27-44) of the row's 32-value blocks after the optional
+// RMSNorm scaling, G lanes per block (lane g of a group holds values
+// [g * 32 / G, (g + 1) * 32 / G)). The block maximum |v| is a max-reduction
+// (order-free); a NaN value counts as 0, as in the reference's running fmax
+// from 0. Every lane of a warp runs the same rounds (the shuffles are
+// warp-wide).
+template <int G, int NCT>
+NRC_DEV void quant_q8_groups(const Params& p, const float* xs, float sc, uint32_t* xq, float* xd, int tok) {
+  constexpr int P = 32 / G;
+  const int tid = threadIdx.x, gid = tid / G, gl = tid % G;
+  for (int base = 0; base < p.bpr; base += NCT / G) {
+    const int b = base + gid;
+    const bool on = b < p.bpr;
+    float v[P];
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < P; k++) {
+      const int idx = b * 32 + gl * P + k;
+      v[k] = on ? xs[idx] : 0.0f;
+      if (on && p.norm_w) v[k] = __fmul_rn(__fmul_rn(v[k], sc), __ldg(p.norm_w + idx));
+      amax = fmaxf(amax, fabsf(v[k]));
+    }
+#pragma unroll
+    for (int o = G / 2; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (!on) continue;
+    const uint16_t dbits = f32_to_f16(__fdiv_rn(amax, 127.0f));
+    const float d = f16_to_f32(dbits);
+    const float inv = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+    int8_t* dst = reinterpret_cast<int8_t*>(xq + xq_index(FMT_Q8_0, p, tok, b)) + gl * P;
+#pragma unroll
+    for (int k = 0; k < P; k++) {
+      const float xsv = __fmul_rn(v[k], inv);
+      const float r = xsv >= 0.0f ? __fadd_rn(xsv, 0.5f) : __fsub_rn(xsv, 0.5f);
+      int q = rust_f2i(r);
+      q = q < -127 ? -127 : (q > 127 ? 127 : q);
+      dst[k] = (int8_t)q;
+    }
+    if (gl == 0) xd[tok * p.bpr + b] = d;
+  }
+}
+
 // Quantize nt f32 rows (optionally RMS-normalised) into the activation buffers,
 // exactly as q8::quantize (q8.rs:27-44) / quantize_q8k (kquant.rs:157-187).
 // Each row is first copied to shared memory (`xs`, aliasing the term buffer)
@@ -343,54 +384,21 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
     if (p.norm_w) {
       // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain,
       // seqsum.cuh), then scale = 1 / sqrtf(ss / n + eps).
-      const float ss = seq_sum_group<NCT>(
+      const float ss = seq_sum_nonneg_group<NCT>(
           K, [&](int i) { return __fmul_rn(xs[i], xs[i]); }, ssh, tid, [] { named_sync(1, NCT); });
       sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), p.eps)));
     }
     if (FMT == FMT_Q8_0) {
-      // q8::quantize (q8.rs:27-44), one thread per 32-value block: all blocks
-      // of the row at once.
-      for (int b = tid; b < p.bpr; b += NCT) {
-        const float4* x4 = reinterpret_cast<const float4*>(xs + b * 32);
-        float v[32];
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          const float4 f = x4[c];
-          v[4 * c] = f.x;
-          v[4 * c + 1] = f.y;
-          v[4 * c + 2] = f.z;
-          v[4 * c + 3] = f.w;
-        }
-        if (p.norm_w) {
-          const float* wn = p.norm_w + b * 32;
-#pragma unroll
-          for (int k = 0; k < 32; k++) v[k] = __fmul_rn(__fmul_rn(v[k], sc), __ldg(wn + k));
-        }
-        float amax = 0.0f;
-#pragma unroll
-        for (int k = 0; k < 32; k++) amax = fmaxf(amax, fabsf(v[k]));
-        const uint16_t dbits = f32_to_f16(__fdiv_rn(amax, 127.0f));
-        const float d = f16_to_f32(dbits);
-        const float inv = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-        uint32_t pk[8];
-#pragma unroll
-        for (int c = 0; c < 8; c++) {
-          uint32_t wv = 0;
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const float xsv = __fmul_rn(v[4 * c + k], inv);
-            const float r = xsv >= 0.0f ? __fadd_rn(xsv, 0.5f) : __fsub_rn(xsv, 0.5f);
-            int q = rust_f2i(r);
-            q = q < -127 ? -127 : (q > 127 ? 127 : q);
-            wv |= (uint32_t)(uint8_t)(int8_t)q << (8 * k);
-          }
-          pk[c] = wv;
-        }
-        uint4* dst = reinterpret_cast<uint4*>(xq + xq_index(FMT_Q8_0, p, tok, b));
-        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-        xd[tok * p.bpr + b] = d;
-      }
+      // q8::quantize (q8.rs:27-44): G lanes per 32-value block, as many as
+      // lets every block of the row go in one round.
+      if (p.bpr <= NCT / 8)
+        quant_q8_groups<8, NCT>(p, xs, sc, xq, xd, tok);
+      else if (p.bpr <= NCT / 4)
+        quant_q8_groups<4, NCT>(p, xs, sc, xq, xd, tok);
+      else if (p.bpr <= NCT / 2)
+        quant_q8_groups<2, NCT>(p, xs, sc, xq, xd, tok);
+      else
+        quant_q8_groups<1, NCT>(p, xs, sc, xq, xd, tok);
     } else {
       for (int b = warp; b < p.bpr; b += NCT / 32) {
         const float4* s4 = reinterpret_cast<const float4*>(xs + b * 256 + lane * 8);
@@ -917,14 +925,18 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
     // -------------------------------------------------------- chain warp
     // Hand-offs are plain shared-memory flags (acquire / release): this warp
     // is the one serial stage of the pipeline, so its loop is kept short.
+    // Stages are taken CB at a time: one flag round and one release per batch.
+    constexpr int CB = NT >= 4 ? 1 : 4 / NT;
     float acc[NT], accu[NT];
 #pragma unroll
     for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
     unsigned long long best = 0ull;
     int q = 0, gl = 0;
-    for (int i = 0; i < nstages; i++) {
-      const int ts = i & (NS - 1);
-      const bool ok = __all_sync(0xffffffffu, flag_wait_geq(&tflag[ts], (uint32_t)i + 1));
+    for (int i0 = 0; i0 < nstages; i0 += CB) {
+      const int nb = nstages - i0 < CB ? nstages - i0 : CB;
+      // Lane l < nb waits for stage i0 + l.
+      const bool ok = __all_sync(0xffffffffu, lane >= nb || flag_wait_geq(&tflag[(i0 + lane) & (NS - 1)],
+                                                                             (uint32_t)(i0 + lane) + 1));
       if (!ok || abort_flag) {
         if (lane == 0 && !abort_flag) {
           abort_flag = 1;
@@ -932,55 +944,62 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
         }
         break;
       }
-      const float* tp = tring + ts * TSF + lane;
-      float v[NT][8];
+      float v[CB][NT][8];
 #pragma unroll
-      for (int t = 0; t < NT; t++)
-#pragma unroll
-        for (int j = 0; j < 8; j++) v[t][j] = tp[(t * 8 + j) * 32];
-      __syncwarp();
-      if (lane == 0) st_release_smem(&tcons, (uint32_t)i + 1);
-      if (p.pair && (q & 1)) {
+      for (int b = 0; b < CB; b++) {
+        const float* tp = tring + ((i0 + b) & (NS - 1)) * TSF + lane;
 #pragma unroll
         for (int t = 0; t < NT; t++)
 #pragma unroll
-          for (int j = 0; j < 8; j++) accu[t] = __fadd_rn(accu[t], v[t][j]);
-      } else {
-#pragma unroll
-        for (int t = 0; t < NT; t++)
-#pragma unroll
-          for (int j = 0; j < 8; j++) acc[t] = __fadd_rn(acc[t], v[t][j]);
+          for (int j = 0; j < 8; j++) v[b][t][j] = b < nb ? tp[(t * 8 + j) * 32] : 0.0f;
       }
-      if (++q == spg) {
-        int seg, row0;
-        lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
-        const int row = row0 + lane;
-        if (lane < lp.rg && row < p.rows[seg]) {
+      __syncwarp();
+      if (lane == 0) st_release_smem(&tcons, (uint32_t)(i0 + nb));
 #pragma unroll
-          for (int t = 0; t < NT; t++) {
-            if (NT > 1 && t >= p.nt) break;
-            if (p.epi == EPI_SWIGLU) {
-              // vec::swiglu: silu = x / (1 + expf(-x)); gate = silu * up
-              const float silu = __fdiv_rn(acc[t], __fadd_rn(1.0f, expf_cr(-acc[t])));
-              p.y[0][(size_t)t * p.ld[0] + row] = __fmul_rn(silu, accu[t]);
-            } else if (p.epi == EPI_RESID) {
-              float* dst = p.resid + (size_t)t * p.resid_ld + row;
-              *dst = __fadd_rn(*dst, __fmul_rn(p.rs, acc[t]));
-            } else {
-              float sv = acc[t];
-              if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
-              p.y[seg][(size_t)t * p.ld[seg] + row] = sv;
-              if (p.epi == EPI_ARGMAX && t == 0 && argmax_candidate(sv)) {
-                const unsigned long long key = argmax_key(sv, (uint32_t)row);
-                best = key > best ? key : best;
+      for (int b = 0; b < CB; b++) {
+        if (b >= nb) break;
+        if (p.pair && (q & 1)) {
+#pragma unroll
+          for (int t = 0; t < NT; t++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) accu[t] = __fadd_rn(accu[t], v[b][t][j]);
+        } else {
+#pragma unroll
+          for (int t = 0; t < NT; t++)
+#pragma unroll
+            for (int j = 0; j < 8; j++) acc[t] = __fadd_rn(acc[t], v[b][t][j]);
+        }
+        if (++q == spg) {
+          int seg, row0;
+          lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
+          const int row = row0 + lane;
+          if (lane < lp.rg && row < p.rows[seg]) {
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+              if (NT > 1 && t >= p.nt) break;
+              if (p.epi == EPI_SWIGLU) {
+                // vec::swiglu: silu = x / (1 + expf(-x)); gate = silu * up
+                const float silu = __fdiv_rn(acc[t], __fadd_rn(1.0f, expf_cr(-acc[t])));
+                p.y[0][(size_t)t * p.ld[0] + row] = __fmul_rn(silu, accu[t]);
+              } else if (p.epi == EPI_RESID) {
+                float* dst = p.resid + (size_t)t * p.resid_ld + row;
+                *dst = __fadd_rn(*dst, __fmul_rn(p.rs, acc[t]));
+              } else {
+                float sv = acc[t];
+                if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
+                p.y[seg][(size_t)t * p.ld[seg] + row] = sv;
+                if (p.epi == EPI_ARGMAX && t == 0 && argmax_candidate(sv)) {
+                  const unsigned long long key = argmax_key(sv, (uint32_t)row);
+                  best = key > best ? key : best;
+                }
               }
             }
           }
-        }
 #pragma unroll
-        for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
-        q = 0;
-        gl++;
+          for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
+          q = 0;
+          gl++;
+        }
       }
     }
     if (p.epi == EPI_ARGMAX) {
