@@ -191,6 +191,12 @@ NRC_DEV void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Arrive at named barrier `id` without waiting (the waiting side uses
+// named_sync with the same total thread count).
+NRC_DEV void named_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // ------------------------------------------------------------ reductions
 NRC_DEV float warp_sum(float v) {
 #pragma unroll

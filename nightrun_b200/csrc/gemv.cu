@@ -382,10 +382,9 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
     named_sync(1, NCT);
     float sc = 1.0f;
     if (p.norm_w) {
-      // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain,
-      // seqsum.cuh), then scale = 1 / sqrtf(ss / n + eps).
-      const float ss = seq_sum_nonneg_group<NCT>(
-          K, [&](int i) { return __fmul_rn(xs[i], xs[i]); }, ssh, tid, [] { named_sync(1, NCT); });
+      // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (the exact
+      // warp-parallel chain of seqsum.cuh), then scale = 1 / sqrtf(ss / n + eps).
+      const float ss = seq_sum_nonneg_group<true, NCT>(xs, K, ssh, tid, [] { named_sync(1, NCT); });
       sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), p.eps)));
     }
     if (FMT == FMT_Q8_0) {
@@ -809,7 +808,7 @@ struct LrParams {
   int ngroups;
   int spg;       // stages per group: n_oct (x 2 in pair mode)
   int off_tr;    // term ring: LR_CW slots of NT x 8 x 32 floats (bytes from the dynamic base)
-  int off_bar;   // full / empty barriers of the ring
+  int off_bar;   // full / empty barriers of the ring, term-slot free barriers
   int rg;        // rows per group (32, or 16 when 32-row groups would leave SMs idle)
 };
 
@@ -839,12 +838,12 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
   constexpr int NS = LR_CW;  // ring slots = term slots = consumer warps
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + lp.off_bar);
   uint64_t* empty = full + NS;
+  uint64_t* tfree = empty + NS;  // term slot s read by the chain warp (consumers sleep on it)
   float* tring = reinterpret_cast<float*>(smem + lp.off_tr);
   constexpr int TSF = NT * 8 * 32;  // floats per term slot
   __shared__ volatile int abort_flag;
   __shared__ uint64_t pf_go;     // completes once: the ring's first stages are issued
   __shared__ uint32_t tflag[NS];  // stage i's terms are in slot i mod NS: tflag = i + 1
-  __shared__ uint32_t tcons;      // the chain warp has read stages < tcons
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int spg = lp.spg;
   // This CTA's groups: blockIdx.x, + gridDim.x, ...; its stages: group-major.
@@ -860,9 +859,9 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
     for (int s = 0; s < NS; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&tfree[s], 1);
       tflag[s] = 0;
     }
-    tcons = 0;
     mbar_init(&pf_go, 4);  // one arrival per issuing lane
     abort_flag = 0;
     fence_barrier_init();
@@ -927,6 +926,8 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
     // is the one serial stage of the pipeline, so its loop is kept short.
     // Stages are taken CB at a time: one flag round and one release per batch.
     constexpr int CB = NT >= 4 ? 1 : 4 / NT;
+    // Sleep through the consumers' prologue (no polling beside its chain).
+    named_sync(2, LR_CW * 32 + 32);
     float acc[NT], accu[NT];
 #pragma unroll
     for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
@@ -954,7 +955,7 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
           for (int j = 0; j < 8; j++) v[b][t][j] = b < nb ? tp[(t * 8 + j) * 32] : 0.0f;
       }
       __syncwarp();
-      if (lane == 0) st_release_smem(&tcons, (uint32_t)(i0 + nb));
+      if (lane < nb) mbar_arrive(&tfree[(i0 + lane) & (NS - 1)]);
 #pragma unroll
       for (int b = 0; b < CB; b++) {
         if (b >= nb) break;
@@ -1020,6 +1021,7 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
   else
     build_x_blocks<FMT_Q8_0, LR_CW * 32>(p, smem);
   named_sync(1, LR_CW * 32);
+  named_arrive(2, LR_CW * 32 + 32);  // wakes the chain warp
 
   const uint32_t* xq = reinterpret_cast<const uint32_t*>(smem + p.off_x);
   const float* xd = reinterpret_cast<const float*>(smem + p.off_xd);
@@ -1041,9 +1043,10 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
     if (has) oct_load<NT>(stages + (size_t)warp * LR_STAGE + (size_t)lane * (8 * Q8_0_BYTES), w);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[warp]);
-    // The term slot is free once the chain warp has read its previous stage.
+    // The term slot is free once the chain warp has read its previous stage
+    // (an mbarrier: waiting warps sleep instead of polling).
     if (k > 0) {
-      const bool ok2 = __all_sync(0xffffffffu, !abort_flag && flag_wait_geq(&tcons, (uint32_t)(i - NS + 1)));
+      const bool ok2 = __all_sync(0xffffffffu, !abort_flag && mbar_wait(&tfree[warp], (k - 1) & 1));
       if (!ok2) {
         if (lane == 0 && !abort_flag) {
           abort_flag = 1;
@@ -1185,7 +1188,7 @@ bool gemv_lr_try(const GemvArgs& a, const Params& base, int NTc, int xmode, cuda
   const size_t x_bytes = (size_t)NTc * n_oct * XW * 4, xd_bytes = (size_t)NTc * p.bpr * 4;
   // Every ring slot and term slot belongs to one consumer warp (LR_CW of each).
   const size_t off_bar = (size_t)LR_CW * LR_STAGE;
-  const size_t off_x = off_bar + 2 * LR_CW * 8;
+  const size_t off_x = off_bar + 3 * LR_CW * 8;
   const size_t off_xd = off_x + x_bytes;
   const size_t off_tr = (off_xd + xd_bytes + 127) & ~(size_t)127;
   size_t tr = (size_t)LR_CW * ts_floats * 4;

@@ -95,20 +95,27 @@ NRC_DEV float seq_sum_group(int n, const Term& term, SeqSumShared& sh, int tid, 
   return r;
 }
 
-// The same left-to-right sum for terms that are all >= 0 (sums of squares,
-// softmax denominators), evaluated by one warp, bit-identical to the chain.
+// The same left-to-right sum of a[0..n) (each a[j] squared when SQ), for
+// terms that are >= 0, evaluated by one warp and bit-identical to the chain.
 // While the running sum s = S * 2^(E-23) (S in [2^23, 2^24)) stays in one
-// binade, adding t rounds to (S + rne(t / 2^(E-23))) * 2^(E-23): every term
-// rounds on its own, so a chunk of 256 terms adds as one integer sum. The
-// exceptions are a tie (t / ulp ends in exactly .5: the result's parity
-// decides), the sum reaching the next binade, and negative or non-finite
-// terms; the first such term in order is added as a plain f32 step and the
-// next chunk starts after it. The first 32 terms (where the sum still
-// changes binade often) and any non-normal running sum go one at a time.
-template <class Term>
-NRC_DEV float seq_sum_nonneg_warp(int n, const Term& term, int lane, float init = 0.0f) {
-  constexpr int ROWS = 8;  // chunk = ROWS x 32 terms; term i + k * 32 + lane in lane `lane`
+// binade, adding t gives (S + rne(t / ulp)) * ulp exactly, except that a tie
+// (t / ulp ending in exactly .5) rounds to the even neighbour, so it depends
+// on the parity of the running sum. A chunk of 256 terms (8 consecutive per
+// lane) is therefore summed as integers: each lane folds its terms into two
+// sums, one per incoming parity, a warp scan composes those functions, and
+// each lane re-walks its terms from its exact prefix to find the first term
+// that takes the sum to 2^24 (the next binade) or is negative / non-finite.
+// That term is added as a plain f32 step and the next chunk starts after it.
+// The first 32 terms (where the sum changes binade often) and any non-normal
+// running sum go one at a time.
+template <bool SQ>
+NRC_DEV float seq_sum_nonneg_warp(const float* a, int n, int lane, float init = 0.0f) {
+  constexpr int PER = 8;
   constexpr uint32_t TOP = 16777216u;  // 2^24
+  auto term = [&](int j) {
+    const float v = a[j];
+    return SQ ? __fmul_rn(v, v) : v;
+  };
   int i = n < 32 ? n : 32;
   float s = seq_sum_serial(i, term, init);
   while (i < n) {
@@ -121,53 +128,90 @@ NRC_DEV float seq_sum_nonneg_warp(int n, const Term& term, int lane, float init 
     }
     const uint32_t S = (b & 0x7fffffu) | 0x800000u;
     const float scale = __uint_as_float((277u - be) << 23);  // 2^(23 - E): exact scaling to ulps
-    uint32_t r[ROWS];
-    uint32_t fl = 0, tot = 0;
+    const int j0 = i + lane * PER;
+    uint32_t v[PER];  // rne(t / ulp), or floor(t / ulp) for a tie
+    uint32_t tie = 0, bad = 0;
 #pragma unroll
-    for (int k = 0; k < ROWS; k++) {
-      const int j = i + k * 32 + lane;
-      uint32_t rk = 0;
+    for (int k = 0; k < PER; k++) {
+      v[k] = 0;
+      const int j = j0 + k;
       if (j < n) {
         const float t = term(j);
         const float T = __fmul_rn(t, scale);
         if (T < 16777216.0f && !(t < 0.0f)) {
-          rk = __float2uint_rn(T);
-          if (__fsub_rn(T, __uint2float_rz(__float2uint_rz(T))) == 0.5f) fl |= 1u << k;
+          const uint32_t fl = __float2uint_rz(T);
+          if (__fsub_rn(T, __uint2float_rz(fl)) == 0.5f) {
+            tie |= 1u << k;
+            v[k] = fl;
+          } else {
+            v[k] = __float2uint_rn(T);
+          }
         } else {
-          fl |= 1u << k;
+          bad |= 1u << k;
         }
       }
-      r[k] = rk;
-      tot += rk;
     }
-    const uint32_t wtot = __reduce_add_sync(0xffffffffu, tot);
-    if (!__any_sync(0xffffffffu, fl != 0) && wtot < TOP - S) {
-      s = __uint_as_float((be << 23) | ((S + wtot) & 0x7fffffu));
-      i += ROWS * 32;
+    // This lane's increment for an incoming running sum of parity 0 / 1
+    // (terms before its first bad one).
+    uint32_t a0 = 0, a1 = 0, q0 = 0, q1 = 1;
+    bool stop = false;
+#pragma unroll
+    for (int k = 0; k < PER; k++) {
+      stop = stop || ((bad >> k) & 1u);
+      if (!stop) {
+        const bool tk = (tie >> k) & 1u;
+        const uint32_t d0 = tk ? v[k] + ((q0 + v[k]) & 1u) : v[k];
+        const uint32_t d1 = tk ? v[k] + ((q1 + v[k]) & 1u) : v[k];
+        a0 += d0;
+        a1 += d1;
+        q0 += d0;
+        q1 += d1;
+      }
+    }
+    // Inclusive scan of the composed functions: F(p) = L(p) + C((p + L(p)) & 1).
+    uint32_t c0 = a0, c1 = a1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t l0 = __shfl_up_sync(0xffffffffu, c0, o);
+      const uint32_t l1 = __shfl_up_sync(0xffffffffu, c1, o);
+      if (lane >= o) {
+        const uint32_t n0 = l0 + ((l0 & 1u) ? c1 : c0);
+        const uint32_t n1 = l1 + (((1u + l1) & 1u) ? c1 : c0);
+        c0 = n0;
+        c1 = n1;
+      }
+    }
+    uint32_t e0 = __shfl_up_sync(0xffffffffu, c0, 1), e1 = __shfl_up_sync(0xffffffffu, c1, 1);
+    if (lane == 0) e0 = e1 = 0;
+    const bool p0 = S & 1u;
+    // Exact walk from this lane's prefix: the first crossing or bad term.
+    uint32_t run = S + (p0 ? e1 : e0);
+    int kev = PER;
+    uint32_t before = 0;
+#pragma unroll
+    for (int k = 0; k < PER; k++) {
+      if (kev == PER && j0 + k < n) {
+        const bool tk = (tie >> k) & 1u;
+        const uint32_t d = tk ? v[k] + ((run + v[k]) & 1u) : v[k];
+        if (((bad >> k) & 1u) || d >= TOP - run) {
+          kev = k;
+          before = run;
+        } else {
+          run += d;
+        }
+      }
+    }
+    const unsigned evl = __ballot_sync(0xffffffffu, kev < PER);
+    if (evl == 0) {
+      const uint32_t tot = __shfl_sync(0xffffffffu, p0 ? c1 : c0, 31);
+      s = __uint_as_float((be << 23) | ((S + tot) & 0x7fffffu));
+      i += 32 * PER;
       continue;
     }
-    // The first term, in order, that is flagged or takes the sum to 2^24.
-    uint32_t run = S;
-    int jev = i;
-    uint32_t before = S;
-#pragma unroll
-    for (int k = 0; k < ROWS; k++) {
-      uint32_t inc = r[k];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t v = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += v;
-      }
-      const unsigned m = __ballot_sync(0xffffffffu, ((fl >> k) & 1u) || inc >= TOP - run);
-      if (m) {
-        const int L = __ffs(m) - 1;
-        before = run + __shfl_sync(0xffffffffu, inc - r[k], L);
-        jev = i + k * 32 + L;
-        break;
-      }
-      run += __shfl_sync(0xffffffffu, inc, 31);
-    }
-    s = __fadd_rn(__uint_as_float((be << 23) | (before & 0x7fffffu)), term(jev));
+    const int L = __ffs(evl) - 1;
+    const uint32_t sb = __shfl_sync(0xffffffffu, before, L);
+    const int jev = i + L * PER + __shfl_sync(0xffffffffu, kev, L);
+    s = __fadd_rn(__uint_as_float((be << 23) | (sb & 0x7fffffu)), term(jev));
     i = jev + 1;
   }
   return s;
@@ -175,12 +219,12 @@ NRC_DEV float seq_sum_nonneg_warp(int n, const Term& term, int lane, float init 
 
 // seq_sum_nonneg_warp for a group of NTH threads: warp 0 sums, every thread
 // returns the result (`sync` is the group's barrier).
-template <int NTH, class Term, class Sync>
-NRC_DEV float seq_sum_nonneg_group(int n, const Term& term, SeqSumShared& sh, int tid, const Sync& sync) {
+template <bool SQ, int NTH, class Sync>
+NRC_DEV float seq_sum_nonneg_group(const float* a, int n, SeqSumShared& sh, int tid, const Sync& sync) {
   static_assert(NTH % 32 == 0, "group of whole warps");
   if (tid < 32) {
-    const float v = seq_sum_nonneg_warp(n, term, tid);
-    if (tid == 0) sh.s = v;
+    const float r = seq_sum_nonneg_warp<SQ>(a, n, tid);
+    if (tid == 0) sh.s = r;
   }
   sync();
   const float r = sh.s;
