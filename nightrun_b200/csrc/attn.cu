@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   for (int t = tid; t < npos; t += ATT_THREADS) sc[t] = expf_cr(__fsub_rn(sc[t], mx));
   __syncthreads();
   // The sum in position order (vec.rs:35-36), one chain (seqsum.cuh).
-  const float sum = seq_sum_nonneg_group<false, ATT_THREADS>(sc, npos, ssh, tid, [] { __syncthreads(); });
+  const float sum = seq_sum_group<ATT_THREADS>(npos, [&](int t) { return sc[t]; }, ssh, tid, [] { __syncthreads(); });
   const float inv = __fdiv_rn(1.0f, sum);
   for (int t = tid; t < npos; t += ATT_THREADS) sc[t] = __fmul_rn(sc[t], inv);
 

@@ -382,9 +382,10 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
     named_sync(1, NCT);
     float sc = 1.0f;
     if (p.norm_w) {
-      // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (the exact
-      // warp-parallel chain of seqsum.cuh), then scale = 1 / sqrtf(ss / n + eps).
-      const float ss = seq_sum_nonneg_group<true, NCT>(xs, K, ssh, tid, [] { named_sync(1, NCT); });
+      // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain,
+      // seqsum.cuh), then scale = 1 / sqrtf(ss / n + eps).
+      const float ss = seq_sum_group<NCT>(
+          K, [&](int i) { return __fmul_rn(xs[i], xs[i]); }, ssh, tid, [] { named_sync(1, NCT); });
       sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), p.eps)));
     }
     if (FMT == FMT_Q8_0) {

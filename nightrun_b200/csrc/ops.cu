@@ -179,7 +179,8 @@ __global__ void k_rmsnorm(float* __restrict__ out, const float* __restrict__ x, 
     __syncthreads();
     src = row;
   }
-  const float ss = seq_sum_nonneg_group<true, 256>(src, n, sh, (int)threadIdx.x, [] { __syncthreads(); });
+  const float ss = seq_sum_group<256>(
+      n, [&](int i) { return __fmul_rn(src[i], src[i]); }, sh, (int)threadIdx.x, [] { __syncthreads(); });
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
   for (int i = threadIdx.x; i < n; i += blockDim.x) orow[i] = __fmul_rn(__fmul_rn(src[i], scale), w[i]);
 }
@@ -197,7 +198,7 @@ __global__ void k_softmax(float* __restrict__ x, int n, int staged) {
   m = block_max(m, red);
   for (int i = threadIdx.x; i < n; i += blockDim.x) e[i] = expf_cr(__fsub_rn(xr[i], m));
   __syncthreads();
-  const float sum = seq_sum_nonneg_group<false, 256>(e, n, sh, (int)threadIdx.x, [] { __syncthreads(); });
+  const float sum = seq_sum_group<256>(n, [&](int i) { return e[i]; }, sh, (int)threadIdx.x, [] { __syncthreads(); });
   const float inv = __fdiv_rn(1.0f, sum);
   for (int i = threadIdx.x; i < n; i += blockDim.x) xr[i] = __fmul_rn(e[i], inv);
 }
