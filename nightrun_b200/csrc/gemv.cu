@@ -84,6 +84,7 @@ struct Params {
   int tb_warp;                       // floats of one warp's term buffer
   int xs_floats;                     // f32 staging floats at off_t (prologue)
   int n_oct;
+  int off_nw;                        // norm weights staged in shared memory (bytes), or -1
 };
 
 NRC_DEV int imin(int a, int b) { return a < b ? a : b; }
@@ -324,7 +325,8 @@ NRC_DEV int xq_index(int fmt, const Params& p, int tok, int b) {
 // from 0. Every lane of a warp runs the same rounds (the shuffles are
 // warp-wide).
 template <int G, int NCT>
-NRC_DEV void quant_q8_groups(const Params& p, const float* xs, float sc, uint32_t* xq, float* xd, int tok) {
+NRC_DEV void quant_q8_groups(const Params& p, const float* xs, const float* nw, float sc, uint32_t* xq, float* xd,
+                             int tok) {
   constexpr int P = 32 / G;
   const int tid = threadIdx.x, gid = tid / G, gl = tid % G;
   for (int base = 0; base < p.bpr; base += NCT / G) {
@@ -336,7 +338,7 @@ NRC_DEV void quant_q8_groups(const Params& p, const float* xs, float sc, uint32_
     for (int k = 0; k < P; k++) {
       const int idx = b * 32 + gl * P + k;
       v[k] = on ? xs[idx] : 0.0f;
-      if (on && p.norm_w) v[k] = __fmul_rn(__fmul_rn(v[k], sc), __ldg(p.norm_w + idx));
+      if (on && p.norm_w) v[k] = __fmul_rn(__fmul_rn(v[k], sc), nw[idx]);
       amax = fmaxf(amax, fabsf(v[k]));
     }
 #pragma unroll
@@ -384,21 +386,23 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
     if (p.norm_w) {
       // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain,
       // seqsum.cuh), then scale = 1 / sqrtf(ss / n + eps).
-      const float ss = seq_sum_group<NCT>(
-          K, [&](int i) { return __fmul_rn(xs[i], xs[i]); }, ssh, tid, [] { named_sync(1, NCT); });
+      const float ss = seq_sum_squares_group<NCT>(xs, K, ssh, tid, [] { named_sync(1, NCT); });
       sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), p.eps)));
     }
     if (FMT == FMT_Q8_0) {
       // q8::quantize (q8.rs:27-44): G lanes per 32-value block, as many as
       // lets every block of the row go in one round.
+      // Norm weights: staged in shared memory before the dependency wait when
+      // the launch reserved room for them, else read through the cache.
+      const float* nw = p.off_nw >= 0 ? reinterpret_cast<const float*>(smem + p.off_nw) : p.norm_w;
       if (p.bpr <= NCT / 8)
-        quant_q8_groups<8, NCT>(p, xs, sc, xq, xd, tok);
+        quant_q8_groups<8, NCT>(p, xs, nw, sc, xq, xd, tok);
       else if (p.bpr <= NCT / 4)
-        quant_q8_groups<4, NCT>(p, xs, sc, xq, xd, tok);
+        quant_q8_groups<4, NCT>(p, xs, nw, sc, xq, xd, tok);
       else if (p.bpr <= NCT / 2)
-        quant_q8_groups<2, NCT>(p, xs, sc, xq, xd, tok);
+        quant_q8_groups<2, NCT>(p, xs, nw, sc, xq, xd, tok);
       else
-        quant_q8_groups<1, NCT>(p, xs, sc, xq, xd, tok);
+        quant_q8_groups<1, NCT>(p, xs, nw, sc, xq, xd, tok);
     } else {
       for (int b = warp; b < p.bpr; b += NCT / 32) {
         const float4* s4 = reinterpret_cast<const float4*>(xs + b * 256 + lane * 8);
@@ -1016,6 +1020,12 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
   }
 
   // ------------------------------------------------------------- consumers
+  if (XMODE == 1 && p.off_nw >= 0) {
+    // The norm weights do not depend on the previous kernel: stage them now.
+    float4* dst = reinterpret_cast<float4*>(smem + p.off_nw);
+    const float4* src = reinterpret_cast<const float4*>(p.norm_w);
+    for (int i = tid; i < p.K / 4; i += LR_CW * 32) dst[i] = src[i];
+  }
   pdl_wait();
   if (XMODE == 1)
     build_x_f32<FMT_Q8_0, LR_CW * 32>(p, smem);
@@ -1194,8 +1204,14 @@ bool gemv_lr_try(const GemvArgs& a, const Params& base, int NTc, int xmode, cuda
   const size_t off_tr = (off_xd + xd_bytes + 127) & ~(size_t)127;
   size_t tr = (size_t)LR_CW * ts_floats * 4;
   if (xmode && (size_t)a.K * 4 > tr) tr = (size_t)a.K * 4;
-  const size_t total = off_tr + tr;
+  size_t total = off_tr + tr;
   if (total > opt_limit) return false;
+  // Norm weights staged in shared memory when they are 16-byte aligned and fit.
+  p.off_nw = -1;
+  if (xmode && a.norm_w && (reinterpret_cast<uintptr_t>(a.norm_w) & 15) == 0 && total + (size_t)a.K * 4 <= opt_limit) {
+    p.off_nw = (int)total;
+    total += (size_t)a.K * 4;
+  }
   // Rows per group: 32, or 16 when that still gives every SM at most one
   // group (small matrices: twice the SMs stream, half the lanes idle).
   auto groups_for = [&](int rg) {
@@ -1283,6 +1299,7 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
     p.rows[s] = a.seg[s].rows;
     p.ld[s] = a.seg[s].ld;
   }
+  p.off_nw = -1;
   p.xq = static_cast<const uint8_t*>(a.xq);
   p.xf = a.xf;
   p.xf_ld = a.xf_ld;

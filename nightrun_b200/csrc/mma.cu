@@ -389,8 +389,7 @@ __global__ void __launch_bounds__(256) k_mma_quant_act(const MmaActArgs a) {
   float sc = 1.0f;
   if (a.norm_w) {
     // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain, seqsum.cuh).
-    const float ss = seq_sum_group<256>(
-        a.K, [&](int i) { return __fmul_rn(xrow[i], xrow[i]); }, ssh, tid, [] { __syncthreads(); });
+    const float ss = seq_sum_squares_group<256>(xrow, a.K, ssh, tid, [] { __syncthreads(); });
     sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps)));
   }
   // q8::quantize (q8.rs:27-44), one thread per 32-value block.

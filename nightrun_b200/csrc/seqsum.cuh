@@ -39,6 +39,43 @@ NRC_DEV float seq_sum_serial(int n, const Term& term, float init = 0.0f) {
   return s;
 }
 
+// ((init + a0*a0) + a1*a1) + ... for a 16-byte aligned array: the squares of
+// whole 16-term blocks are loaded with 16-byte loads two blocks ahead of their
+// adds, so shared-memory latency stays off the chain (rmsnorm's `ss`).
+NRC_DEV float seq_sum_squares_serial(const float* a, int n, float init = 0.0f) {
+  constexpr int W = 16;
+  float s = init;
+  const int nfull = n - n % W;
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+  if (nfull > 0) {
+    float4 c0[4], c1[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) c0[j] = a4[j];
+#pragma unroll
+    for (int j = 0; j < 4; j++) c1[j] = W < nfull ? a4[4 + j] : c0[j];
+    for (int i = 0; i < nfull; i += W) {
+      const int nb = i + 2 * W < nfull ? i + 2 * W : i;  // two blocks ahead (any block at the end)
+      float4 c2[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) c2[j] = a4[nb / 4 + j];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        s = __fadd_rn(s, __fmul_rn(c0[j].x, c0[j].x));
+        s = __fadd_rn(s, __fmul_rn(c0[j].y, c0[j].y));
+        s = __fadd_rn(s, __fmul_rn(c0[j].z, c0[j].z));
+        s = __fadd_rn(s, __fmul_rn(c0[j].w, c0[j].w));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        c0[j] = c1[j];
+        c1[j] = c2[j];
+      }
+    }
+  }
+  for (int i = nfull; i < n; i++) s = __fadd_rn(s, __fmul_rn(a[i], a[i]));
+  return s;
+}
+
 // Two independent chains over the same index range (their adds interleave).
 template <class TermA, class TermB>
 NRC_DEV void seq_sum_serial2(int n, const TermA& ta, const TermB& tb, float& sa, float& sb) {
@@ -82,6 +119,17 @@ NRC_DEV void seq_sum_serial2(int n, const TermA& ta, const TermB& tb, float& sa,
 struct SeqSumShared {
   float s;
 };
+
+// seq_sum_squares_serial for a group of NTH threads (thread 0 runs it).
+template <int NTH, class Sync>
+NRC_DEV float seq_sum_squares_group(const float* a, int n, SeqSumShared& sh, int tid, const Sync& sync) {
+  static_assert(NTH % 32 == 0, "group of whole warps");
+  if (tid == 0) sh.s = seq_sum_squares_serial(a, n);
+  sync();
+  const float r = sh.s;
+  sync();
+  return r;
+}
 
 // The same sum for a group of NTH threads: thread 0 runs the chain, `sync`
 // is the group's barrier, every thread returns the result.
