@@ -152,6 +152,11 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+# DRAM bytes (read + write) of one classifier-shape launch, from the ncu capture
+# in profiles/gemv_lr_q8_0_classifier_128256x2048_n1.md (same command shape).
+CLASSIFIER_TRAFFIC = 282_699_520
+
+
 def gemv_roofline(torch, K, rows, cols, reps, stream):
     """Standalone Q8_0 GEMV on the classifier shape (the largest decode launch)."""
     from nightrun_b200 import kernels
@@ -274,8 +279,10 @@ def run_ours(args, rank, world, local_rank):
                     "d2h_bytes_per_step": vocab * 4 + 8},
             "gpu_launches": launches_per_step(cfg) * Kst,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None,
-                         "kernel": f"gemv_kernel<Q8_0> {vocab}x{cfg['dim']} (classifier), {gms * 1000:.1f} us/launch",
+                         "frac": achieved / hbm, "traffic": CLASSIFIER_TRAFFIC,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of the same "
+                                           "shape (profiles/gemv_lr_q8_0_classifier_128256x2048_n1.md)",
+                         "kernel": f"gemv_lr_kernel<1> Q8_0 {vocab}x{cfg['dim']} (classifier), {gms * 1000:.1f} us/launch",
                          "peak_kind": hbm_kind,
                          "algorithmic_bytes_per_launch": gbytes},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / hbm},

@@ -802,9 +802,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
 //    the fused epilogue. Gate and up (SwiGLU pair) alternate stage by stage
 //    with one running sum each.
 constexpr int LR_CW = 16;                     // consumer warps (one ring slot each)
-constexpr int LR_THREADS = (LR_CW + 2) * 32;  // + chain warp + producer warp
-constexpr int LR_ROWS = 32;                   // rows per group, one per lane
-constexpr int LR_STAGE = LR_ROWS * 8 * Q8_0_BYTES;  // 8704 bytes, a multiple of 128
+constexpr int LR_NCH = 2;                     // chain warps (alternate row groups)
+constexpr int LR_THREADS = (LR_CW + LR_NCH + 1) * 32;  // + chain warps + producer warp
+constexpr int LR_STAGE = 32 * 8 * Q8_0_BYTES;  // 32 octets = 8704 bytes, a multiple of 128
 
 struct LrParams {
   CUtensorMap tmap[3];  // one per weight matrix: dims {row_bytes / 4, rows}, box {68, 32}
@@ -814,7 +814,7 @@ struct LrParams {
   int spg;       // stages per group: n_oct (x 2 in pair mode)
   int off_tr;    // term ring: LR_CW slots of NT x 8 x 32 floats (bytes from the dynamic base)
   int off_bar;   // full / empty barriers of the ring, term-slot free barriers
-  int rg;        // rows per group (32, or 16 when 32-row groups would leave SMs idle)
+  int rg;        // rows per group: 32 / OPS
 };
 
 // 2-D tiled TMA load of one box into shared memory, completion counted on
@@ -835,7 +835,7 @@ NRC_DEV void lr_group(const LrParams& lp, int g, int& seg, int& row0) {
   row0 = (g - lp.group_start[seg]) * lp.rg;
 }
 
-template <int NT, int XMODE>
+template <int NT, int XMODE, int OPS>
 __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_constant__ LrParams lp) {
   const Params& p = lp.p;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -874,7 +874,7 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
   __syncthreads();
   pdl_trigger();
 
-  if (warp == LR_CW + 1) {
+  if (warp == LR_CW + LR_NCH) {
     // ----------------------------------------------------------- producer
     // Lanes 0..3 issue (stage i by lane i mod 4, which therefore owns the ring
     // slots i mod NS): a tensor copy takes a while to issue, so several
@@ -899,10 +899,10 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
         const int gl = i / spg, q = i - gl * spg;
         int seg, row0;
         lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
-        const int o = p.pair ? q >> 1 : q;
+        const int og = p.pair ? q >> 1 : q;  // octet column group of this stage
         const int m = p.pair ? (q & 1) : seg;
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(lp.rg * 8 * Q8_0_BYTES));
-        tma_load_2d(stages + (size_t)s * LR_STAGE, &lp.tmap[m], o * (8 * Q8_0_BYTES / 4), row0, &full[s], pol);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)LR_STAGE);
+        tma_load_2d(stages + (size_t)s * LR_STAGE, &lp.tmap[m], og * OPS * (8 * Q8_0_BYTES / 8), row0, &full[s], pol);
         last = i;
       }
       if (!go) mbar_arrive(&pf_go);
@@ -925,86 +925,90 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
     return;
   }
 
-  if (warp == LR_CW) {
-    // -------------------------------------------------------- chain warp
-    // Hand-offs are plain shared-memory flags (acquire / release): this warp
-    // is the one serial stage of the pipeline, so its loop is kept short.
-    // Stages are taken CB at a time: one flag round and one release per batch.
-    constexpr int CB = NT >= 4 ? 1 : 4 / NT;
+  if (warp >= LR_CW) {
+    // ------------------------------------------------------- chain warps
+    // Chain warp c takes the CTA's row groups c, c + LR_NCH, ...: each group's
+    // stages in order (so every row's terms are added in block order), CB
+    // stages per flag round. Hand-offs: acquire flags in, mbarriers out.
+    const int c = warp - LR_CW;
+    constexpr int CB = NT * OPS >= 4 ? 1 : 4 / (NT * OPS);
     // Sleep through the consumers' prologue (no polling beside its chain).
-    named_sync(2, LR_CW * 32 + 32);
-    float acc[NT], accu[NT];
-#pragma unroll
-    for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
+    named_sync(2, (LR_CW + LR_NCH) * 32);
     unsigned long long best = 0ull;
-    int q = 0, gl = 0;
-    for (int i0 = 0; i0 < nstages; i0 += CB) {
-      const int nb = nstages - i0 < CB ? nstages - i0 : CB;
-      // Lane l < nb waits for stage i0 + l.
-      const bool ok = __all_sync(0xffffffffu, lane >= nb || flag_wait_geq(&tflag[(i0 + lane) & (NS - 1)],
-                                                                             (uint32_t)(i0 + lane) + 1));
-      if (!ok || abort_flag) {
-        if (lane == 0 && !abort_flag) {
-          abort_flag = 1;
-          atomicOr(p.err, ERR_WAIT_FULL);
+    bool stop = false;
+    for (int gl = c; gl < my_groups && !stop; gl += LR_NCH) {
+      float acc[NT], accu[NT];
+#pragma unroll
+      for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
+      for (int q0 = 0; q0 < spg; q0 += CB) {
+        const int i0 = gl * spg + q0;
+        const int nb = spg - q0 < CB ? spg - q0 : CB;
+        // Lane l < nb waits for stage i0 + l.
+        const bool ok = __all_sync(0xffffffffu, lane >= nb || flag_wait_geq(&tflag[(i0 + lane) & (NS - 1)],
+                                                                               (uint32_t)(i0 + lane) + 1));
+        if (!ok || abort_flag) {
+          if (lane == 0 && !abort_flag) {
+            abort_flag = 1;
+            atomicOr(p.err, ERR_WAIT_FULL);
+          }
+          stop = true;
+          break;
         }
-        break;
-      }
-      float v[CB][NT][8];
+        // Row `lane` (< 32 / OPS): octets lane * OPS .. + OPS - 1 of the stage, in order.
+        float v[CB][NT][8 * OPS];
 #pragma unroll
-      for (int b = 0; b < CB; b++) {
-        const float* tp = tring + ((i0 + b) & (NS - 1)) * TSF + lane;
-#pragma unroll
-        for (int t = 0; t < NT; t++)
-#pragma unroll
-          for (int j = 0; j < 8; j++) v[b][t][j] = b < nb ? tp[(t * 8 + j) * 32] : 0.0f;
-      }
-      __syncwarp();
-      if (lane < nb) mbar_arrive(&tfree[(i0 + lane) & (NS - 1)]);
-#pragma unroll
-      for (int b = 0; b < CB; b++) {
-        if (b >= nb) break;
-        if (p.pair && (q & 1)) {
+        for (int b = 0; b < CB; b++) {
+          const float* tp = tring + ((i0 + b) & (NS - 1)) * TSF + lane * OPS;
 #pragma unroll
           for (int t = 0; t < NT; t++)
 #pragma unroll
-            for (int j = 0; j < 8; j++) accu[t] = __fadd_rn(accu[t], v[b][t][j]);
-        } else {
+            for (int o = 0; o < OPS; o++)
 #pragma unroll
-          for (int t = 0; t < NT; t++)
-#pragma unroll
-            for (int j = 0; j < 8; j++) acc[t] = __fadd_rn(acc[t], v[b][t][j]);
+              for (int j = 0; j < 8; j++)
+                v[b][t][o * 8 + j] = b < nb && lane * OPS < 32 ? tp[(t * 8 + j) * 32 + o] : 0.0f;
         }
-        if (++q == spg) {
-          int seg, row0;
-          lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
-          const int row = row0 + lane;
-          if (lane < lp.rg && row < p.rows[seg]) {
+        __syncwarp();
+        if (lane < nb) mbar_arrive(&tfree[(i0 + lane) & (NS - 1)]);
 #pragma unroll
-            for (int t = 0; t < NT; t++) {
-              if (NT > 1 && t >= p.nt) break;
-              if (p.epi == EPI_SWIGLU) {
-                // vec::swiglu: silu = x / (1 + expf(-x)); gate = silu * up
-                const float silu = __fdiv_rn(acc[t], __fadd_rn(1.0f, expf_cr(-acc[t])));
-                p.y[0][(size_t)t * p.ld[0] + row] = __fmul_rn(silu, accu[t]);
-              } else if (p.epi == EPI_RESID) {
-                float* dst = p.resid + (size_t)t * p.resid_ld + row;
-                *dst = __fadd_rn(*dst, __fmul_rn(p.rs, acc[t]));
-              } else {
-                float sv = acc[t];
-                if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
-                p.y[seg][(size_t)t * p.ld[seg] + row] = sv;
-                if (p.epi == EPI_ARGMAX && t == 0 && argmax_candidate(sv)) {
-                  const unsigned long long key = argmax_key(sv, (uint32_t)row);
-                  best = key > best ? key : best;
-                }
-              }
+        for (int b = 0; b < CB; b++) {
+          if (b >= nb) break;
+          if (p.pair && ((q0 + b) & 1)) {
+#pragma unroll
+            for (int t = 0; t < NT; t++)
+#pragma unroll
+              for (int j = 0; j < 8 * OPS; j++) accu[t] = __fadd_rn(accu[t], v[b][t][j]);
+          } else {
+#pragma unroll
+            for (int t = 0; t < NT; t++)
+#pragma unroll
+              for (int j = 0; j < 8 * OPS; j++) acc[t] = __fadd_rn(acc[t], v[b][t][j]);
+          }
+        }
+      }
+      if (stop) break;
+      int seg, row0;
+      lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
+      const int row = row0 + lane;
+      if (lane < lp.rg && row < p.rows[seg]) {
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+          if (NT > 1 && t >= p.nt) break;
+          if (p.epi == EPI_SWIGLU) {
+            // vec::swiglu: silu = x / (1 + expf(-x)); gate = silu * up
+            const float silu = __fdiv_rn(acc[t], __fadd_rn(1.0f, expf_cr(-acc[t])));
+            p.y[0][(size_t)t * p.ld[0] + row] = __fmul_rn(silu, accu[t]);
+          } else if (p.epi == EPI_RESID) {
+            float* dst = p.resid + (size_t)t * p.resid_ld + row;
+            *dst = __fadd_rn(*dst, __fmul_rn(p.rs, acc[t]));
+          } else {
+            float sv = acc[t];
+            if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
+            p.y[seg][(size_t)t * p.ld[seg] + row] = sv;
+            if (p.epi == EPI_ARGMAX && t == 0 && argmax_candidate(sv)) {
+              const unsigned long long key = argmax_key(sv, (uint32_t)row);
+              best = key > best ? key : best;
             }
           }
-#pragma unroll
-          for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
-          q = 0;
-          gl++;
         }
       }
     }
@@ -1032,12 +1036,13 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
   else
     build_x_blocks<FMT_Q8_0, LR_CW * 32>(p, smem);
   named_sync(1, LR_CW * 32);
-  named_arrive(2, LR_CW * 32 + 32);  // wakes the chain warp
+  named_arrive(2, (LR_CW + LR_NCH) * 32);  // wakes the chain warps
 
   const uint32_t* xq = reinterpret_cast<const uint32_t*>(smem + p.off_x);
   const float* xd = reinterpret_cast<const float*>(smem + p.off_xd);
   const int xtok = p.n_oct * XW;
-  const bool has = lane < lp.rg;
+  // Lane = (row lane / OPS, octet lane % OPS) of the stage's box.
+  const int lo = lane % OPS;
   // Stage i = warp + k * NS: ring slot and term slot `warp`, parity k & 1.
   int q = warp % spg;
   const int qstep = NS % spg;
@@ -1051,7 +1056,7 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
       break;
     }
     uint32_t w[68];
-    if (has) oct_load<NT>(stages + (size_t)warp * LR_STAGE + (size_t)lane * (8 * Q8_0_BYTES), w);
+    oct_load<NT>(stages + (size_t)warp * LR_STAGE + (size_t)lane * (8 * Q8_0_BYTES), w);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[warp]);
     // The term slot is free once the chain warp has read its previous stage
@@ -1066,8 +1071,8 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
         break;
       }
     }
-    const int o = p.pair ? q >> 1 : q;
-    if (has) oct_compute<NT, 32>(w, xq + o * XW, xtok, xd + 8 * o, p.nt, p.bpr, tring + warp * TSF + lane, 8 * 32);
+    const int o = (p.pair ? q >> 1 : q) * OPS + lo;
+    oct_compute<NT, 32>(w, xq + o * XW, xtok, xd + 8 * o, p.nt, p.bpr, tring + warp * TSF + lane, 8 * 32);
     __syncwarp();
     if (lane == 0) st_release_smem(&tflag[warp], (uint32_t)i + 1);
     q += qstep;
@@ -1154,26 +1159,30 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// rows x (row_bytes / 4) u32 view of a Q8_0 matrix; box = one octet column of rg rows.
-bool encode_rows_map(CUtensorMap* m, const void* w, int rows, int row_bytes, int rg) {
+// rows x (row_bytes / 8) u64 view of a Q8_0 matrix; box = `ops` octet columns
+// of 32 / ops rows (8704 bytes, the rows' octets back to back).
+bool encode_rows_map(CUtensorMap* m, const void* w, int rows, int row_bytes, int ops) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 4), (cuuint64_t)rows};
+  const cuuint64_t dims[2] = {(cuuint64_t)(row_bytes / 8), (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-  const cuuint32_t box[2] = {8 * Q8_0_BYTES / 4, (cuuint32_t)rg};
+  const cuuint32_t box[2] = {(cuuint32_t)(ops * 8 * Q8_0_BYTES / 8), (cuuint32_t)(32 / ops)};
   const cuuint32_t estr[2] = {1, 1};
-  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(w), dims, strides, box, estr,
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(w), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 using LrFn = void (*)(LrParams);
-LrFn pick_lr(int NTc, int xmode) {
-  switch (NTc) {
-    case 1: return xmode ? gemv_lr_kernel<1, 1> : gemv_lr_kernel<1, 0>;
-    case 2: return xmode ? gemv_lr_kernel<2, 1> : gemv_lr_kernel<2, 0>;
-    default: return xmode ? gemv_lr_kernel<4, 1> : gemv_lr_kernel<4, 0>;
-  }
+// Instances with NT x OPS <= 4 (the chain warp keeps NT x 8 x OPS terms in registers).
+template <int NT, int OPS>
+LrFn pick_lr_x(int xmode) {
+  return xmode ? gemv_lr_kernel<NT, 1, OPS> : gemv_lr_kernel<NT, 0, OPS>;
+}
+LrFn pick_lr(int NTc, int xmode, int ops) {
+  if (NTc == 1) return ops == 4 ? pick_lr_x<1, 4>(xmode) : (ops == 2 ? pick_lr_x<1, 2>(xmode) : pick_lr_x<1, 1>(xmode));
+  if (NTc == 2) return ops == 2 ? pick_lr_x<2, 2>(xmode) : pick_lr_x<2, 1>(xmode);
+  return pick_lr_x<4, 1>(xmode);
 }
 
 // Launch the lane-per-row kernel if the shape allows it. Returns false (and
@@ -1191,7 +1200,20 @@ bool gemv_lr_try(const GemvArgs& a, const Params& base, int NTc, int xmode, cuda
   Params& p = lp.p;
   const int n_oct = p.bpr / 8;
   const int nspan = a.pair ? 2 : 1;
-  lp.spg = n_oct * nspan;
+  // A stage is 32 octets: OPS octet columns of 32 / OPS rows. One column of
+  // 32 rows keeps the chain warps' per-stage work short; matrices whose
+  // 32-row groups would leave SMs idle take up to 4 columns of 8 rows instead
+  // (more, smaller groups), as far as the row length and NT allow.
+  int groups32 = 0;
+  if (a.pair)
+    groups32 = (a.seg[0].rows + 31) / 32;
+  else
+    for (int s = 0; s < a.nseg; s++) groups32 += (a.seg[s].rows + 31) / 32;
+  int ops = 1;
+  if (groups32 < di.sms)
+    while (ops < 4 && n_oct % (2 * ops) == 0 && NTc * 2 * ops <= 4) ops *= 2;
+  lp.rg = 32 / ops;
+  lp.spg = n_oct / ops * nspan;
   const size_t ts_floats = (size_t)NTc * 8 * 32;
   // Shared memory: ring | barriers | activations | term ring (doubles as the
   // prologue's f32 staging row).
@@ -1212,18 +1234,9 @@ bool gemv_lr_try(const GemvArgs& a, const Params& base, int NTc, int xmode, cuda
     p.off_nw = (int)total;
     total += (size_t)a.K * 4;
   }
-  // Rows per group: 32, or 16 when that still gives every SM at most one
-  // group (small matrices: twice the SMs stream, half the lanes idle).
-  auto groups_for = [&](int rg) {
-    int n = 0;
-    if (a.pair) return (a.seg[0].rows + rg - 1) / rg;
-    for (int s = 0; s < a.nseg; s++) n += (a.seg[s].rows + rg - 1) / rg;
-    return n;
-  };
-  lp.rg = groups_for(16) <= di.sms ? 16 : LR_ROWS;
   int ng = 0;
   if (a.pair) {
-    ng = groups_for(lp.rg);
+    ng = (a.seg[0].rows + lp.rg - 1) / lp.rg;
     lp.group_start[0] = 0;
     lp.group_start[1] = ng;
   } else {
@@ -1235,7 +1248,7 @@ bool gemv_lr_try(const GemvArgs& a, const Params& base, int NTc, int xmode, cuda
   }
   if (ng == 0) return true;
   for (int s = 0; s < a.nseg; s++)
-    if (!encode_rows_map(&lp.tmap[s], a.seg[s].w, a.seg[s].rows, p.row_bytes, lp.rg)) {
+    if (!encode_rows_map(&lp.tmap[s], a.seg[s].w, a.seg[s].rows, p.row_bytes, ops)) {
       *err = cudaErrorNotSupported;
       return true;
     }
@@ -1249,7 +1262,7 @@ bool gemv_lr_try(const GemvArgs& a, const Params& base, int NTc, int xmode, cuda
   p.off_xb = (int)off_xd;
   p.off_t = (int)off_tr;
   p.xs_floats = (int)((total - off_tr) / 4);
-  LrFn fn = pick_lr(NTc, xmode);
+  LrFn fn = pick_lr(NTc, xmode, ops);
   {
     static std::mutex mu;
     static std::map<std::pair<int, void*>, bool> attr_set;

@@ -168,12 +168,15 @@ def test_matmul_bit_exact_and_equals_matvec(K, orc, fmt, batch):
 
 
 @pytest.mark.parametrize("batch", [1, 2, 3, 4])
-@pytest.mark.parametrize("shape", [(100, 512), (33, 2048), (64, 8192), (1, 256), (2500, 512), (4099, 256)])
+@pytest.mark.parametrize("shape", [(100, 512), (33, 2048), (64, 8192), (1, 256), (2500, 512), (4099, 256),
+                                   (4801, 2048)])
 def test_matvec_q8_whole_octet_rows(K, orc, shape, batch):
     """Q8_0 rows of whole 16-byte aligned octets (cols % 256 == 0), 1-4 tokens:
-    the lane-per-row kernel (16- or 32-row groups, one row per lane, 2-D
-    tensor copies, block terms chained in order by one warp). Partial last
-    groups read zero-filled rows that are never stored."""
+    the streaming kernel with 32-octet stages (1, 2 or 4 octet columns of
+    32, 16 or 8 rows: 4801 rows x 2048 fill every SM with 32-row groups, the
+    small shapes take narrower groups), block terms chained in order by two
+    chain warps. Partial last groups read zero-filled rows that are never
+    stored."""
     rows, cols = shape
     w = make_weights(orc, "q8_0", rows, cols, 60 + rows + batch, adversarial=(batch % 2 == 0))
     xs = make_acts(orc, "q8_0", cols, 61 + batch, batch)
