@@ -183,6 +183,15 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
     cp_async_commit();
   };
   stage_v(0, 0);
+  // The K row of this thread's first position, loaded now so its latency
+  // overlaps the RoPE work below.
+  uint4 k0[16];
+  if (tid < cached) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kbase + (size_t)tid * kv_dim);
+#pragma unroll
+    for (int c = 0; c < 16; c++)
+      if (c < cpr) k0[c] = kr[c];
+  }
   if (fused) {
     const float* ct = a.cos_tab + (size_t)pos * half;
     const float* st = a.sin_tab + (size_t)pos * half;
@@ -219,7 +228,20 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   float mloc = -INFINITY;
   for (int t = tid; t < npos; t += ATT_THREADS) {
     float s = 0.0f;
-    if (t < cached) {
+    if (t == tid && t < cached) {
+#pragma unroll
+      for (int c = 0; c < 16; c++) {
+        if (c < cpr) {
+          const uint32_t w[4] = {k0[c].x, k0[c].y, k0[c].z, k0[c].w};
+          const float* qd = qs + c * 8;
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            s = __fadd_rn(s, __fmul_rn(h2f(w[j] & 0xffffu), qd[2 * j]));
+            s = __fadd_rn(s, __fmul_rn(h2f(w[j] >> 16), qd[2 * j + 1]));
+          }
+        }
+      }
+    } else if (t < cached) {
       const uint4* kr = reinterpret_cast<const uint4*>(kbase + (size_t)t * kv_dim);
       for (int c0 = 0; c0 < cpr; c0 += 8) {
         uint4 k8[8];
