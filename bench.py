@@ -187,6 +187,24 @@ def gemv_roofline(torch, K, rows, cols, reps, stream):
     return nbytes, ms
 
 
+def max_over_ranks_of(v, world, device):
+    """The slowest rank's time: every timed region is reported as the max over
+    ranks (an all-reduce MAX on `device`; the process group must be up)."""
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_tokens_per_s(ms_max, steps, world):
+    """Whole-job throughput of `world` independent replicas that each decoded
+    `steps` tokens, timed by the slowest rank."""
+    return world * steps / (ms_max / 1000.0)
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -209,11 +227,7 @@ def run_ours(args, rank, world, local_rank):
             dist.barrier()
 
     def max_over_ranks(v):
-        if world == 1:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return max_over_ranks_of(v, world, "cuda")
 
     sampler.start()
     # ---- device-resident decode (graph replay per token)
@@ -230,7 +244,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
-    value = world * Kst / (ms / 1000.0)
+    value = job_tokens_per_s(ms, Kst, world)
 
     # ---- end to end through the public API: host token in, host logits out, every step
     ctx.reset()
@@ -255,7 +269,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    e2e_value = world * Kst / (e2e_ms / 1000.0)
+    e2e_value = job_tokens_per_s(e2e_ms, Kst, world)
 
     # ---- dominant kernel: Q8_0 GEMV on the classifier shape (vocab x dim)
     gstream = torch.cuda.Stream()
