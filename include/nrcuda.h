@@ -67,7 +67,9 @@ int nrc_dequant_q6k(const void* blocks, float* out, size_t nblocks, void* stream
  * y[r] = dot(w[r,:], x), w = rows x cols Q8_0, x = cols/32 Q8_0 blocks.
  * Bit-identical to the reference's scalar dot (kernels.rs:72-82). */
 int nrc_matvec_q8_0(float* y, const void* w, const void* x, size_t rows, size_t cols, void* stream);
-/* kernels::matmul_q8 (kernels.rs:91-143): y is [batch][rows], xs is [batch][cols/32]. */
+/* kernels::matmul_q8 (kernels.rs:91-143): y is [batch][rows], xs is [batch][cols/32].
+ * Like every kernel-level entry point it is asynchronous: an expired bounded wait inside its
+ * kernels is reported by a later nrc_sync_check on the same stream. */
 int nrc_matmul_q8_0(float* y, const void* w, const void* xs, size_t rows, size_t cols, size_t batch,
                     void* stream);
 /* nrc_matmul_q8_0 that allocates nothing. No counterpart in the reference:
@@ -80,11 +82,12 @@ int nrc_matmul_q8_0(float* y, const void* w, const void* xs, size_t rows, size_t
  *  - cols > NRC_NOALLOC_MAX_COLS is rejected with NRC_ERR_INVALID.
  *  - Only the error word must start at zero; every call clears it itself.
  *  - The first call on a device resolves the array's address
- *    (cudaGetSymbolAddress) and sets kernel attributes: make it outside any
- *    stream capture.
+ *    (cudaGetSymbolAddress) and sets kernel attributes.
+ *  - Every call blocks the host until its kernels have finished (it reads the
+ *    error word back and synchronizes `stream`), so it must never be made while
+ *    `stream` is being captured into a CUDA graph.
  *  - Calls overlapping in time on one device (several streams or threads)
- *    race on the array: serialize them.
- *  - Returns after its kernels finished (it reads the error word back). */
+ *    race on the array: serialize them. */
 #define NRC_NOALLOC_MAX_COLS 16384
 #define NRC_NOALLOC_SCRATCH_BYTES (256 + 64 * NRC_NOALLOC_MAX_COLS + 64 * (NRC_NOALLOC_MAX_COLS / 32) * 4)
 int nrc_matmul_q8_0_noalloc(float* y, const void* w, const void* xs, size_t rows, size_t cols, size_t batch,

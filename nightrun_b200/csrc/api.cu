@@ -80,9 +80,12 @@ int matvec_common(int fmt, float* y, const void* w, const void* x, size_t rows, 
       const size_t bpr = cols / 32;
       uint8_t* xq = nullptr;
       float* xd = nullptr;
-      if (cudaMallocAsync((void**)&xq, (size_t)ntg * NS * cols, S(stream)) != cudaSuccess ||
-          cudaMallocAsync((void**)&xd, (size_t)ntg * NS * bpr * 4, S(stream)) != cudaSuccess)
+      if (cudaMallocAsync((void**)&xq, (size_t)ntg * NS * cols, S(stream)) != cudaSuccess)
         return nrc_fail_api(NRC_ERR_ALLOC, "activation tile allocation failed");
+      if (cudaMallocAsync((void**)&xd, (size_t)ntg * NS * bpr * 4, S(stream)) != cudaSuccess) {
+        cudaFreeAsync(xq, S(stream));
+        return nrc_fail_api(NRC_ERR_ALLOC, "activation scale allocation failed");
+      }
       rc = cuda_rc(mma_pack_q8_run(static_cast<const uint8_t*>(x) + t0 * bpr * 34, nt, (int)cols, NS, ntg, xq, xd,
                                    S(stream)),
                    "mma pack");

@@ -408,13 +408,7 @@ cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl) {
     return cudaErrorInvalidValue;
   const size_t smem = attention_smem_bytes(a.n_heads, a.n_kv_heads, a.head_dim, a.ctx);
   if (smem > ATTN_MAX_SMEM) return cudaErrorInvalidValue;
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute((const void*)k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, ATTN_MAX_SMEM);
-    attr_done[dev] = true;
-  }
+  if (cudaError_t e = ensure_smem_attr((const void*)k_attention, ATTN_MAX_SMEM)) return e;
   AttnArgs aa = a;
   void* args[] = {&aa};
   return launch((const void*)k_attention, dim3(a.n_heads, a.nt), dim3(ATT_THREADS), smem, s, pdl, args);

@@ -3,10 +3,32 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <set>
+#include <tuple>
+
 #define NRC_HD __host__ __device__ __forceinline__
 #define NRC_DEV __device__ __forceinline__
 
 namespace nrc {
+
+// Raise kernel `fn`'s dynamic shared-memory limit to `bytes` once per
+// (device, kernel, size). The setting is recorded only when the call
+// succeeds, so a failed first attempt is retried by the next launch; the
+// record is guarded for callers on several host threads.
+inline cudaError_t ensure_smem_attr(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<int, const void*, int>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> g(mu);
+  const auto key = std::make_tuple(dev, fn, bytes);
+  if (done.count(key)) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done.insert(key);
+  return e;
+}
 
 // ---------------------------------------------------------------- constants
 constexpr int QK8_0 = 32;

@@ -1012,7 +1012,7 @@ int ensure_graph(nrc_ctx* c) {
 
 extern "C" int nrc_ctx_forward(nrc_ctx* c, uint32_t token, float* logits_host, uint32_t* next_host) {
   if (!c) return fail(NRC_ERR_INVALID, "null context");
-  if (c->pos >= c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  if (c->pos + c->pending >= c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   if (token >= (uint32_t)c->vocab) return fail(NRC_ERR_BAD_TOKEN, "token %u >= vocab %d", token, c->vocab);
   CU(cudaSetDevice(c->device));
   if (!c->gexec) {
@@ -1034,7 +1034,7 @@ extern "C" int nrc_ctx_prefill_chunk(nrc_ctx* c, const uint32_t* tokens, size_t 
                                      uint32_t* next_host) {
   if (!c || !tokens) return fail(NRC_ERR_INVALID, "null argument");
   if (n < 1 || n > NRC_MAX_BATCH) return fail(NRC_ERR_BAD_BATCH, "prefill chunk of %zu tokens", n);
-  if (c->pos + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  if (c->pos + c->pending + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   for (size_t i = 0; i < n; i++)
     if (tokens[i] >= (uint32_t)c->vocab) return fail(NRC_ERR_BAD_TOKEN, "token %u >= vocab %d", tokens[i], c->vocab);
   CU(cudaSetDevice(c->device));
@@ -1049,7 +1049,7 @@ extern "C" int nrc_ctx_prefill_chunk(nrc_ctx* c, const uint32_t* tokens, size_t 
 extern "C" int nrc_ctx_prefill(nrc_ctx* c, const uint32_t* tokens, size_t n, float* logits_host, uint32_t* next_host) {
   if (!c || !tokens) return fail(NRC_ERR_INVALID, "null argument");
   if (n == 0) return fail(NRC_ERR_BAD_BATCH, "empty prompt");
-  if (c->pos + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  if (c->pos + c->pending + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   for (size_t i = 0; i < n; i += NRC_MAX_BATCH) {
     const size_t b = n - i < (size_t)NRC_MAX_BATCH ? n - i : (size_t)NRC_MAX_BATCH;
     const bool last = i + b == n;
@@ -1062,7 +1062,7 @@ extern "C" int nrc_ctx_prefill(nrc_ctx* c, const uint32_t* tokens, size_t n, flo
 extern "C" int nrc_ctx_generate(nrc_ctx* c, uint32_t first, size_t n, uint32_t* out_host) {
   if (!c || (!out_host && n)) return fail(NRC_ERR_INVALID, "null argument");
   if (n == 0) return NRC_OK;
-  if (c->pos + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  if (c->pos + c->pending + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   if (first >= (uint32_t)c->vocab) return fail(NRC_ERR_BAD_TOKEN, "token %u >= vocab %d", first, c->vocab);
   CU(cudaSetDevice(c->device));
   const size_t p0 = c->pos;
@@ -1077,7 +1077,7 @@ extern "C" int nrc_ctx_generate(nrc_ctx* c, uint32_t first, size_t n, uint32_t* 
 
 extern "C" int nrc_ctx_decode_async(nrc_ctx* c, size_t n) {
   if (!c) return fail(NRC_ERR_INVALID, "null context");
-  if (c->pos + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
+  if (c->pos + c->pending + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   if (!c->gexec) return fail(NRC_ERR_INVALID, "no decode step yet: call nrc_ctx_forward or nrc_ctx_prefill first");
   CU(cudaSetDevice(c->device));
   for (size_t i = 0; i < n; i++) CU(cudaGraphLaunch(c->gexec, c->stream));
@@ -1104,7 +1104,7 @@ extern "C" int nrc_ctx_reset(nrc_ctx* c) {
   return NRC_OK;
 }
 extern "C" size_t nrc_ctx_pos(const nrc_ctx* c) { return c ? c->pos : 0; }
-extern "C" size_t nrc_ctx_remaining(const nrc_ctx* c) { return c ? c->ctx - c->pos : 0; }
+extern "C" size_t nrc_ctx_remaining(const nrc_ctx* c) { return c ? c->ctx - c->pos - c->pending : 0; }
 extern "C" int nrc_ctx_logits_device(const nrc_ctx* c, const float** out) {
   if (!c || !out) return fail(NRC_ERR_INVALID, "null argument");
   *out = c->logits;

@@ -1127,18 +1127,14 @@ DevInfo dev_info() {
 int occupancy(KernelFn fn, int smem, int smem_optin) {
   static std::mutex mu;
   static std::map<std::tuple<int, void*, int>, int> cache;
-  static std::map<std::pair<int, void*>, bool> attr_set;
   int dev = 0;
   cudaGetDevice(&dev);
+  // The attribute is an upper bound: set it once to the largest dynamic size any launch may use.
+  if (ensure_smem_attr((const void*)fn, smem_optin - SMEM_RESERVE) != cudaSuccess) return 0;
   std::lock_guard<std::mutex> g(mu);
   auto key = std::make_tuple(dev, (void*)fn, smem);
   auto itc = cache.find(key);
   if (itc != cache.end()) return itc->second;
-  // The attribute is an upper bound: set it once to the largest dynamic size any launch may use.
-  if (!attr_set[std::make_pair(dev, (void*)fn)]) {
-    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin - SMEM_RESERVE);
-    attr_set[std::make_pair(dev, (void*)fn)] = true;
-  }
   int n = 0;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, NTHREADS, smem) != cudaSuccess) n = 0;
   cache[key] = n;
@@ -1263,17 +1259,7 @@ bool gemv_lr_try(const GemvArgs& a, const Params& base, int NTc, int xmode, cuda
   p.off_t = (int)off_tr;
   p.xs_floats = (int)((total - off_tr) / 4);
   LrFn fn = pick_lr(NTc, xmode, ops);
-  {
-    static std::mutex mu;
-    static std::map<std::pair<int, void*>, bool> attr_set;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    std::lock_guard<std::mutex> g(mu);
-    if (!attr_set[std::make_pair(dev, (void*)fn)]) {
-      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)opt_limit);
-      attr_set[std::make_pair(dev, (void*)fn)] = true;
-    }
-  }
+  if ((*err = ensure_smem_attr((const void*)fn, (int)opt_limit)) != cudaSuccess) return true;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(std::min(ng, di.sms));
   cfg.blockDim = dim3(LR_THREADS);

@@ -471,13 +471,7 @@ cudaError_t mma_quant_act_run(const MmaActArgs& a, cudaStream_t s, bool pdl) {
   MmaActArgs aa = a;
   void* args[] = {&aa};
   const size_t smem = (size_t)a.K * 4;
-  static bool attr_done[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute((const void*)k_mma_quant_act, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-    attr_done[dev] = true;
-  }
+  if (cudaError_t e = ensure_smem_attr((const void*)k_mma_quant_act, 64 * 1024)) return e;
   if (smem > 64 * 1024) return cudaErrorInvalidValue;
   return launch((const void*)k_mma_quant_act, dim3(a.NS * a.ntg), dim3(256), smem, s, pdl, args);
 }
@@ -540,14 +534,7 @@ cudaError_t mma_q8_run(const MmaArgs& a, cudaStream_t s, bool pdl) {
   while (cols < (uint32_t)(NSLOT * a.NS)) cols <<= 1;
   p.tmem_cols = cols;
   const void* fn = a.NS == 16 ? (const void*)k_mma_q8<16> : (a.NS == 32 ? (const void*)k_mma_q8<32> : (const void*)k_mma_q8<64>);
-  static bool attr_done[64][3] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int ki = a.NS == 16 ? 0 : (a.NS == 32 ? 1 : 2);
-  if (dev < 64 && !attr_done[dev][ki]) {
-    cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024);
-    attr_done[dev][ki] = true;
-  }
+  if (cudaError_t e = ensure_smem_attr(fn, 225 * 1024)) return e;
   if (smem > 225 * 1024) return cudaErrorInvalidValue;
   if (tiles == 0) return cudaSuccess;
   void* args[] = {&p};

@@ -12,12 +12,12 @@
 // by every pass before they are read.
 //
 // The device address of the array is resolved once per device with
-// cudaGetSymbolAddress; that first call, and the first launch of each kernel
-// (which sets its shared-memory attribute), must happen outside any stream
-// capture. Calls that overlap in time on one device (different streams or
-// host threads) share the array and race; the caller serializes them. The
-// call returns after its kernels finished: it reads the error word back, so
-// an expired bounded wait is reported by the same call.
+// cudaGetSymbolAddress. Calls that overlap in time on one device (different
+// streams or host threads) share the array and race; the caller serializes
+// them. Every call blocks the host until its kernels have finished (it reads
+// the error word back and synchronizes the stream, so an expired bounded wait
+// is reported by the same call); it therefore cannot be made inside a stream
+// capture.
 #include <mutex>
 
 #include "common.cuh"

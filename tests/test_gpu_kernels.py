@@ -318,10 +318,11 @@ def _sum_cases(n, seed):
 
 @pytest.mark.parametrize("n", [1, 63, 64, 65, 100, 1000, 2048, 4097, 8192, 8193, 20000])
 def test_exact_parallel_sums_adversarial(K, orc, n):
-    """rmsnorm's sum of squares and softmax's denominator are evaluated by a
-    whole CTA (seqsum.cuh) yet must equal the reference's sequential chain
-    bit for bit, on inputs chosen to stress binade crossings, half-way
-    roundings, subnormals and a single dominating term."""
+    """rmsnorm's sum of squares and softmax's denominator (one pipelined
+    serial chain on the device, 16-term blocks fetched ahead of their adds)
+    must equal the reference's sequential chain bit for bit, on inputs chosen
+    to stress binade crossings, half-way roundings, subnormals and a single
+    dominating term."""
     w = (np.random.default_rng(n).standard_normal(n) + 1).astype(F)
     for name, x in _sum_cases(n, n + 7):
         out = torch.empty(n, dtype=torch.float32, device="cuda")

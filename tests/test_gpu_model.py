@@ -109,12 +109,12 @@ def test_prefill_matches_oracle_prefill(NB, orc, name):
 
 
 @pytest.mark.parametrize("name", TINY)
-def test_prefill_bit_identical_to_sequential(NB, name):  # prefill.rs:91-133 lengths (<= 129)
+def test_prefill_bit_identical_to_sequential(NB, name):  # all 16 lengths of prefill.rs:91-133
     cfg = CONFIGS[name]
     m = NB.Model.synth(cfg, MODEL_SEED)
-    seq, bat = m.ctx(320), m.ctx(320)
-    ids = prompt_ids(140, cfg["vocab"])
-    for n in (1, 7, 15, 17, 31, 33, 63, 65, 127, 128, 129):
+    seq, bat = m.ctx(520), m.ctx(520)
+    ids = prompt_ids(520, cfg["vocab"])
+    for n in (1, 7, 15, 17, 31, 33, 63, 65, 127, 128, 129, 255, 257, 511, 512, 513):
         seq.reset()
         bat.reset()
         ls = None
@@ -174,6 +174,39 @@ def test_context_limits_and_errors(NB):
     assert e.value.name == "CTX_FULL"
     c.reset()
     assert c.pos == 0 and c.remaining() == 8
+
+
+def test_context_limit_counts_enqueued_steps(NB):
+    """Decode steps enqueued with decode_async but not yet synced count against
+    the context window: every entry point rejects on the host (CTX_FULL) before
+    any kernel could append a KV row past the end (infer.rs:513, 605)."""
+    cfg = CONFIGS["tiny_llama_q8"]
+    m = NB.Model.synth(cfg, MODEL_SEED)
+    c = m.ctx(12)
+    c.prefill(list(range(4)))
+    c.decode_async(5)  # device position reaches 9 once these run
+    assert c.remaining() == 3
+    for call in (lambda: c.decode_async(4), lambda: c.prefill_chunk([1, 2, 3, 4]),
+                 lambda: c.prefill([1, 2, 3, 4]), lambda: c.generate(1, 4)):
+        with pytest.raises(NB.NrcError) as e:
+            call()
+        assert e.value.name == "CTX_FULL"
+    c.decode_async(3)
+    with pytest.raises(NB.NrcError) as e:
+        c.forward(1)
+    assert e.value.name == "CTX_FULL"
+    c.sync()
+    assert c.pos == 12 and c.remaining() == 0
+    # The same steps synced one call at a time give the same tokens.
+    c2 = m.ctx(12)
+    c2.prefill(list(range(4)))
+    toks = [c2.next_token]
+    for _ in range(8):
+        toks.append(c2.forward_greedy(toks[-1]))
+    c.reset()
+    c.prefill(list(range(4)))
+    c.decode_async(8)
+    assert c.sync() == toks[-1]
 
 
 @pytest.mark.slow

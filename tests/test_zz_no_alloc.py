@@ -38,6 +38,10 @@ def test_noalloc_matches_matmul_q8_over_two_calls(K, orc, rows, cols, batch):
         ref = run(K.matmul_q8, w, xs, rows, cols, batch)
         got = run(K.matmul_q8_noalloc, w, xs, rows, cols, batch)
         assert got.tobytes() == ref.tobytes(), f"call {call}: {rows}x{cols} b{batch}"
+        if rows * cols * batch <= 2048 * 8192 * 33:
+            # and directly against the reference's scalar matmul (kernels.rs:91-143)
+            want = orc.matmul("q8_0", w, xs, rows, cols, batch).reshape(batch, rows)
+            assert got.tobytes() == want.tobytes(), f"call {call}: {rows}x{cols} b{batch} vs oracle"
 
 
 def test_noalloc_rejects_cols_beyond_scratch(K):
