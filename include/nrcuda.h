@@ -119,6 +119,15 @@ int nrc_expf(const float* x, float* y, size_t n, void* stream);
 int nrc_expf_hash(uint64_t* out_dev, int chunk0, int nchunks, void* stream);
 /* vec::argmax (vec.rs:80-90): first maximum; writes the index to *out_dev (uint32, device). */
 int nrc_argmax(const float* x, size_t n, uint32_t* out_dev, void* stream);
+/* Sampler::sample (crates/nr-model/src/sample.rs:32-96) over n device logits (n <= 262144):
+ * temperature <= 0 is vec::argmax; otherwise the top-64 prefilter (the reference's min-heap,
+ * replayed exactly when logits tie at its boundary), softmax with temperature in descending
+ * order, the top_p nucleus cut and one xorshift64 draw from *rng_dev (device uint64, the
+ * Sampler's state: seed | 1 at Sampler::new, advanced once per draw). Candidates with equal
+ * logits are ordered by ascending index (the reference's sort_unstable_by leaves that order
+ * unspecified). Writes the token id to *out_dev (uint32, device). */
+int nrc_sample(const float* logits, size_t n, float temperature, float top_p, uint64_t* rng_dev, uint32_t* out_dev,
+               void* stream);
 /* rope::rope_freqs (crates/nr-tensor/src/rope.rs:14-34), computed on the host into out_host
  * (head_dim/2 values); factor <= 0 disables the Llama-3 scaling. */
 int nrc_rope_freqs(float* out_host, size_t head_dim, float theta, float factor, float low_freq_factor,
@@ -194,6 +203,21 @@ int nrc_ctx_generate(nrc_ctx* c, uint32_t first, size_t n, uint32_t* out_host);
  * nrc_ctx_sync, which waits, advances pos and returns the last chosen token. */
 int nrc_ctx_decode_async(nrc_ctx* c, size_t n);
 int nrc_ctx_sync(nrc_ctx* c, uint32_t* next_host);
+/* Decode arithmetic of a context. NRC_MODE_EXACT (default): every sum in the reference's order,
+ * logits and KV cache bit-identical to its scalar path. NRC_MODE_FAST: single-token decode steps
+ * add block terms, the RMSNorm sum of squares and the attention softmax / V sums as trees (the
+ * per-block integer dots and roundings, and the activation quantization, are unchanged); results
+ * then differ from the reference in the last bits, within the north star's tolerance (1e-5
+ * relative L2 per matvec, 1e-3 max-abs on the logits). Prefill chunks stay exact. No counterpart in
+ * the reference, whose one CPU path is the exact one. */
+#define NRC_MODE_EXACT 0
+#define NRC_MODE_FAST 1
+int nrc_ctx_set_mode(nrc_ctx* c, int mode);
+/* Sampler::new(temperature, top_p, seed) (sample.rs:15-21) attached to the context: from now on
+ * every step that chooses a next token draws once with it (each forward, each prefill_chunk, the
+ * last chunk of a prefill, every generated / decode_async step), on the device. temperature <= 0
+ * restores greedy argmax. The logits the steps return are unchanged. */
+int nrc_ctx_set_sampler(nrc_ctx* c, float temperature, float top_p, uint64_t seed);
 int nrc_ctx_reset(nrc_ctx* c);              /* infer.rs:494-496 */
 size_t nrc_ctx_pos(const nrc_ctx* c);       /* InferCtx::pos */
 size_t nrc_ctx_remaining(const nrc_ctx* c); /* infer.rs:504-506 */

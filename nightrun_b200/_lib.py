@@ -84,6 +84,7 @@ SIGNATURES = [
     ("nrc_argmax", I, [P, S, P, P]),
     ("nrc_expf", I, [P, P, S, P]),
     ("nrc_expf_hash", I, [P, I, I, P]),
+    ("nrc_sample", I, [P, S, F, F, P, P, P]),
     ("nrc_rope_freqs", I, [P, S, F, F, F, F, F]),
     ("nrc_rope_apply", I, [P, S, S, P, S, I, P]),
     ("nrc_model_load", I, [P, S, I, I, C.POINTER(P)]),
@@ -102,6 +103,8 @@ SIGNATURES = [
     ("nrc_ctx_generate", I, [P, U32, S, P]),
     ("nrc_ctx_decode_async", I, [P, S]),
     ("nrc_ctx_sync", I, [P, P]),
+    ("nrc_ctx_set_sampler", I, [P, F, F, U64]),
+    ("nrc_ctx_set_mode", I, [P, I]),
     ("nrc_ctx_reset", I, [P]),
     ("nrc_ctx_pos", S, [P]),
     ("nrc_ctx_remaining", S, [P]),

@@ -13,6 +13,7 @@
 #include "mma.cuh"
 #include "nrcuda.h"
 #include "ops.cuh"
+#include "sample.cuh"
 
 using namespace nrc;
 
@@ -24,6 +25,7 @@ namespace {
 struct DevScratch {
   unsigned* err = nullptr;
   unsigned long long* key = nullptr;
+  unsigned long long* cand = nullptr;  // sampler candidates (SAMPLE_MAX_N logits)
 };
 
 int dev_scratch(DevScratch* out) {
@@ -39,10 +41,12 @@ int dev_scratch(DevScratch* out) {
   }
   DevScratch s;
   void* p = nullptr;
-  if (cudaMalloc(&p, 256) != cudaSuccess) return nrc_fail_api(NRC_ERR_ALLOC, "scratch allocation failed");
+  const size_t bytes = 256 + sample_scratch_bytes(SAMPLE_MAX_N);
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return nrc_fail_api(NRC_ERR_ALLOC, "scratch allocation failed");
   cudaMemset(p, 0, 256);
   s.err = static_cast<unsigned*>(p);
   s.key = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(p) + 64);
+  s.cand = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(p) + 256);
   cache[dev] = s;
   *out = s;
   return NRC_OK;
@@ -213,6 +217,20 @@ int nrc_argmax(const float* x, size_t n, uint32_t* out_dev, void* stream) {
   int rc = dev_scratch(&sc);
   if (rc) return rc;
   return cuda_rc(op_argmax(x, n, sc.key, out_dev, S(stream)), "argmax");
+}
+
+int nrc_sample(const float* logits, size_t n, float temperature, float top_p, uint64_t* rng_dev, uint32_t* out_dev,
+               void* stream) {
+  if (!out_dev || !rng_dev || (n && !logits)) return nrc_fail_api(NRC_ERR_INVALID, "null pointer");
+  if (n == 0 || n > (size_t)SAMPLE_MAX_N)
+    return nrc_fail_api(NRC_ERR_INVALID, "sampler over %zu logits (1..%d supported)", n, SAMPLE_MAX_N);
+  DevScratch sc;
+  int rc = dev_scratch(&sc);
+  if (rc) return rc;
+  if (temperature <= 0.0f) return cuda_rc(op_argmax(logits, n, sc.key, out_dev, S(stream)), "argmax");
+  SampleArgs a{logits, (int)n, temperature, top_p, reinterpret_cast<unsigned long long*>(rng_dev), sc.cand, out_dev,
+               nullptr};
+  return cuda_rc(sample_run(a, S(stream), false), "sample");
 }
 
 int nrc_rope_freqs(float* out, size_t head_dim, float theta, float factor, float low, float high, float orig) {

@@ -306,6 +306,177 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   if (d < hd) a.out[(size_t)tok * att_dim + (size_t)h * hd + d] = acc;
 }
 
+// Decode attention of the tolerance mode (infer.rs:553-572 up to summation
+// order): grid (query head, position split). The fused per-head norms, RoPE
+// and KV append are those of k_attention. Scores: one thread per position
+// (fused multiply-adds); softmax max and sum as CTA trees; V: hd/8 threads
+// per cached row, 16-byte loads, 8 accumulators each, the position groups
+// combined in a fixed order. With several splits each CTA writes (max, sum,
+// unnormalised output) and the last CTA of the head (an arrival counter, no
+// waiting) merges the splits in split order and resets the counter.
+constexpr int AF_THREADS = 128;
+
+__global__ void __launch_bounds__(AF_THREADS) k_attention_fast(const AttnArgs a, float* part, unsigned* count,
+                                                               int nsplit, int max_per) {
+  pdl_wait();
+  pdl_trigger();
+  const int h = blockIdx.x, sp = blockIdx.y;
+  const int hd = a.head_dim, half = hd / 2;
+  const int gqa = a.n_heads / a.n_kv_heads;
+  const int g = h / gqa;
+  const int kv_dim = a.n_kv_heads * hd;
+  const uint32_t pos = a.pos_dev[0];
+  const int npos = (int)pos + 1;
+  const int per = (npos + nsplit - 1) / nsplit;
+  const int t0 = min(npos, sp * per), t1 = min(npos, t0 + per);
+  const bool mine = (int)pos >= t0 && (int)pos < t1;  // this split holds the new position
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                                               // [hd]
+  float* hbuf = qs + hd;                                        // [3][hd]
+  uint16_t* knew = reinterpret_cast<uint16_t*>(hbuf + 3 * hd);  // [hd]
+  uint16_t* vnew = knew + hd;                                   // [hd]
+  float* sc = reinterpret_cast<float*>(vnew + hd);              // [max_per]
+  float* vpart = sc + ((max_per + 3) & ~3);                     // [16][hd]
+  __shared__ float red[AF_THREADS / 32];
+  __shared__ unsigned last;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint16_t* kbase = a.kcache + (size_t)g * hd;
+  const uint16_t* vbase = a.vcache + (size_t)g * hd;
+  {
+    const float* ct = a.cos_tab + (size_t)pos * half;
+    const float* st = a.sin_tab + (size_t)pos * half;
+    const int pr = hd / 32;
+    float outv[4];
+    if (warp == 0) {
+      warp_rope_head(a.q + (size_t)h * hd, a.q_norm, a.eps, ct, st, a.style, hd, hbuf, lane, outv);
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        if (i < pr) qs[lane + 32 * i] = outv[i];
+    } else if (warp == 1 && mine) {
+      warp_rope_head(a.k + (size_t)g * hd, a.k_norm, a.eps, ct, st, a.style, hd, hbuf + hd, lane, outv);
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        if (i < pr) {
+          const uint16_t kb = f32_to_f16(outv[i]);
+          knew[lane + 32 * i] = kb;
+          if (h % gqa == 0) a.kcache[(size_t)pos * kv_dim + (size_t)g * hd + lane + 32 * i] = kb;
+        }
+    } else if (warp == 2 && mine) {
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        if (i < pr) {
+          const uint16_t vb = f32_to_f16(a.v[(size_t)g * hd + lane + 32 * i]);
+          vnew[lane + 32 * i] = vb;
+          if (h % gqa == 0) a.vcache[(size_t)pos * kv_dim + (size_t)g * hd + lane + 32 * i] = vb;
+        }
+    }
+  }
+  __syncthreads();
+  // Scores.
+  const int cpr = hd / 8;
+  float mloc = -INFINITY;
+  for (int t = t0 + tid; t < t1; t += AF_THREADS) {
+    float s = 0.0f;
+    if (t == (int)pos) {
+      for (int d = 0; d < hd; d++) s = fmaf(h2f(knew[d]), qs[d], s);
+    } else {
+      const uint4* kr = reinterpret_cast<const uint4*>(kbase + (size_t)t * kv_dim);
+      for (int c0 = 0; c0 < cpr; c0 += 8) {
+        uint4 k8[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+          if (c0 + c < cpr) k8[c] = kr[c0 + c];
+#pragma unroll
+        for (int c = 0; c < 8; c++)
+          if (c0 + c < cpr) {
+            const uint32_t w[4] = {k8[c].x, k8[c].y, k8[c].z, k8[c].w};
+            const float* qd = qs + (c0 + c) * 8;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              s = fmaf(h2f(w[j] & 0xffffu), qd[2 * j], s);
+              s = fmaf(h2f(w[j] >> 16), qd[2 * j + 1], s);
+            }
+          }
+      }
+    }
+    s = s * a.scale;
+    sc[t - t0] = s;
+    mloc = fmaxf(mloc, s);
+  }
+  mloc = warp_max(mloc);
+  if (lane == 0) red[warp] = mloc;
+  __syncthreads();
+  float mx = red[0];
+#pragma unroll
+  for (int w = 1; w < AF_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
+  __syncthreads();  // red is reused below
+  float lsum = 0.0f;
+  for (int t = t0 + tid; t < t1; t += AF_THREADS) {
+    const float e = expf_cr(sc[t - t0] - mx);
+    sc[t - t0] = e;
+    lsum += e;
+  }
+  lsum = warp_sum(lsum);
+  if (lane == 0) red[warp] = lsum;
+  __syncthreads();
+  float l = 0.0f;
+#pragma unroll
+  for (int w = 0; w < AF_THREADS / 32; w++) l += red[w];
+  // V: thread (c, grp) accumulates dims c*8 .. c*8+7 over positions t0 + grp, + P, ...
+  const int P = AF_THREADS / cpr;
+  const int c = tid % cpr, grp = tid / cpr;
+  float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+  for (int t = t0 + grp; t < t1; t += P) {
+    const float e = sc[t - t0];
+    uint4 vv;
+    if (t == (int)pos)
+      vv = reinterpret_cast<const uint4*>(vnew)[c];
+    else
+      vv = reinterpret_cast<const uint4*>(vbase + (size_t)t * kv_dim)[c];
+    const uint32_t w[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      acc[2 * j] = fmaf(e, h2f(w[j] & 0xffffu), acc[2 * j]);
+      acc[2 * j + 1] = fmaf(e, h2f(w[j] >> 16), acc[2 * j + 1]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; j++) vpart[grp * hd + c * 8 + j] = acc[j];
+  __syncthreads();
+  float o = 0.0f;
+  if (tid < hd)
+    for (int q = 0; q < P; q++) o += vpart[q * hd + tid];
+  float* out = a.out + (size_t)h * hd;
+  if (nsplit == 1) {
+    if (tid < hd) out[tid] = o / l;
+    return;
+  }
+  float* pp = part + ((size_t)h * nsplit + sp) * (hd + 2);
+  if (tid < hd) pp[2 + tid] = o;
+  if (tid == 0) {
+    pp[0] = mx;
+    pp[1] = l;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(&count[h], 1u);
+  __syncthreads();
+  if (last != (unsigned)nsplit - 1) return;
+  __threadfence();
+  const float* ph = part + (size_t)h * nsplit * (hd + 2);
+  float M = -INFINITY;
+  for (int k = 0; k < nsplit; k++) M = fmaxf(M, ph[k * (hd + 2)]);
+  float L = 0.0f, O = 0.0f;
+  for (int k = 0; k < nsplit; k++) {
+    const float* q = ph + k * (hd + 2);
+    const float f = q[1] > 0.0f ? expf_cr(q[0] - M) : 0.0f;
+    L += q[1] * f;
+    if (tid < hd) O += q[2 + tid] * f;
+  }
+  if (tid < hd) out[tid] = O / L;
+  if (tid == 0) count[h] = 0u;
+}
+
 __global__ void k_embed(const EmbedArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -412,6 +583,33 @@ cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl) {
   AttnArgs aa = a;
   void* args[] = {&aa};
   return launch((const void*)k_attention, dim3(a.n_heads, a.nt), dim3(ATT_THREADS), smem, s, pdl, args);
+}
+
+int attention_fast_splits(int ctx) {
+  const int n = (ctx + 255) / 256;
+  return n < 1 ? 1 : (n > 32 ? 32 : n);
+}
+size_t attention_fast_scratch_floats(int n_heads, int head_dim, int nsplit) {
+  return (size_t)n_heads * nsplit * (head_dim + 2);
+}
+size_t attention_fast_smem_bytes(int head_dim, int ctx, int nsplit) {
+  const int max_per = (ctx + nsplit - 1) / nsplit;
+  return (size_t)head_dim * 4 * 4 + (size_t)head_dim * 2 * 2 + (size_t)((max_per + 3) & ~3) * 4 +
+         (size_t)16 * head_dim * 4;
+}
+
+cudaError_t attention_fast_run(const AttnArgs& a, float* part, unsigned* count, int nsplit, cudaStream_t s,
+                               bool pdl) {
+  if (a.n_kv_heads < 1 || a.n_heads % a.n_kv_heads || a.head_dim % 32 || a.head_dim < 64 || a.head_dim > 128 ||
+      a.nt != 1 || nsplit < 1 || (nsplit > 1 && (!part || !count)))
+    return cudaErrorInvalidValue;
+  const int max_per = (a.ctx + nsplit - 1) / nsplit;
+  const size_t smem = attention_fast_smem_bytes(a.head_dim, a.ctx, nsplit);
+  if (smem > ATTN_MAX_SMEM) return cudaErrorInvalidValue;
+  if (cudaError_t e = ensure_smem_attr((const void*)k_attention_fast, (int)ATTN_MAX_SMEM)) return e;
+  AttnArgs aa = a;
+  void* args[] = {&aa, &part, &count, &nsplit, (void*)&max_per};
+  return launch((const void*)k_attention_fast, dim3(a.n_heads, nsplit), dim3(AF_THREADS), smem, s, pdl, args);
 }
 
 cudaError_t embed_run(const EmbedArgs& a, cudaStream_t s, bool pdl) {

@@ -233,9 +233,10 @@ NRC_DEV float warp_max(float v) {
 
 // Orderable key for a float (NaN and -inf excluded by the caller): larger key =
 // larger value; ties broken toward the lower index (vec::argmax keeps the
-// first maximum, crates/nr-tensor/src/vec.rs:80-90).
+// first maximum, crates/nr-tensor/src/vec.rs:80-90). -0.0 and +0.0 compare
+// equal there, so both map to the key of +0.0.
 NRC_DEV unsigned long long argmax_key(float v, uint32_t idx) {
-  uint32_t b = __float_as_uint(v);
+  uint32_t b = __float_as_uint(v == 0.0f ? 0.0f : v);
   uint32_t o = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
   return ((unsigned long long)o << 32) | (unsigned long long)(0xffffffffu - idx);
 }

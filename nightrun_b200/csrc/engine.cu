@@ -12,10 +12,12 @@
 #include <vector>
 
 #include "common.cuh"
+#include "fast.cuh"
 #include "gemv.cuh"
 #include "mma.cuh"
 #include "nrcuda.h"
 #include "ops.cuh"
+#include "sample.cuh"
 #include "synth.cuh"
 
 using namespace nrc;
@@ -460,11 +462,12 @@ struct Status {
   uint32_t err;
   uint32_t pad;
   unsigned long long key;
+  unsigned long long rng;  // Sampler::rng (sample.rs:9), advanced once per draw
   uint32_t tok[NRC_MAX_BATCH];
 };
 
 struct Layout {
-  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, status, hist, total;
+  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, status, hist, samp, afp, afc, total;
 };
 
 size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -497,6 +500,10 @@ Layout layout_for(const nrc_meta& mt, size_t ctx) {
   L.mxd = take(B * (maxk / 32) * 4);  // and their block scales
   L.status = take(sizeof(Status));
   L.hist = take((ctx + 1) * 4);
+  L.samp = take(sample_scratch_bytes((int)mt.vocab));  // sampler candidates
+  // Split-position partials and per-head arrival counters of the tolerance-mode attention.
+  L.afp = take(attention_fast_scratch_floats(mt.n_heads, mt.head_dim, attention_fast_splits((int)ctx)) * 4);
+  L.afc = take((size_t)mt.n_heads * 4);
   L.total = o;
   return L;
 }
@@ -555,6 +562,15 @@ struct nrc_ctx {
   size_t pending = 0;  // decode steps enqueued by nrc_ctx_decode_async, not yet synced
   cudaGraphExec_t gexec = nullptr;
   bool pdl = true;
+  // Sampler attached by nrc_ctx_set_sampler (greedy when temperature <= 0).
+  float temperature = 0.0f, top_p = 1.0f;
+  bool sampling = false;
+  unsigned long long* samp = nullptr;
+  // Tolerance mode (nrc_ctx_set_mode): decode steps use the tree-reduced kernels.
+  bool fast = false;
+  float* af_part = nullptr;
+  unsigned* af_count = nullptr;
+  int af_nsplit = 1;
 };
 
 extern "C" int nrc_ctx_required_bytes(const nrc_model* m, size_t ctx, size_t* out) {
@@ -663,6 +679,10 @@ extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
   c->mxd = reinterpret_cast<float*>(A + c->lay.mxd);
   c->st = reinterpret_cast<Status*>(A + c->lay.status);
   c->hist = reinterpret_cast<uint32_t*>(A + c->lay.hist);
+  c->samp = reinterpret_cast<unsigned long long*>(A + c->lay.samp);
+  c->af_part = reinterpret_cast<float*>(A + c->lay.afp);
+  c->af_count = reinterpret_cast<unsigned*>(A + c->lay.afc);
+  c->af_nsplit = attention_fast_splits((int)ctx);
 
   // RoPE tables (infer.rs:427-445; rope.rs:49-65): cos/sin of pos * freq.
   const size_t half = mt.head_dim / 2;
@@ -816,12 +836,16 @@ cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
   }
   a.pf = L.pf;
   a.pf_bytes = L.pf_bytes;
+  if (c->fast && nt == 1) {
+    a.nt = 1;
+    return fast_gemv_run(a, s, pdl);
+  }
   return gemv_tokens(a, nt, L.K, s, pdl);
 }
 
 // Enqueue one forward step over nt tokens at positions st->pos .. +nt-1
 // (infer.rs:510-595 for nt == 1, infer.rs:601-750 otherwise).
-cudaError_t enqueue_step(nrc_ctx* c, int nt) {
+cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw) {
   cudaStream_t s = c->stream;
   const bool pdl = c->pdl;
   cudaError_t e;
@@ -903,7 +927,11 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
                   nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
       if ((e = rope_append_run(ra, s, pdl))) return e;
     }
-    if ((e = attention_run(aa, s, pdl))) return e;
+    if (c->fast && nt == 1 && c->hd >= 64)
+      e = attention_fast_run(aa, c->af_part, c->af_count, c->af_nsplit, s, pdl);
+    else
+      e = attention_run(aa, s, pdl);
+    if (e) return e;
     {  // output projection + residual (infer.rs:574-575)
       Lin L{};
       L.fmt = w.fo;
@@ -972,7 +1000,12 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt) {
     a.scale = c->logit_recip;
     a.argmax_key = &c->st->key;
     a.nt = 1;
-    if ((e = gemv_run(a, s, pdl))) return e;
+    if ((e = (c->fast && nt == 1) ? fast_gemv_run(a, s, pdl) : gemv_run(a, s, pdl))) return e;
+  }
+  if (c->sampling && draw) {
+    // Sampler::sample (sample.rs:32-96) replaces the greedy key with its draw.
+    SampleArgs sa{c->logits, c->vocab, c->temperature, c->top_p, &c->st->rng, c->samp, nullptr, &c->st->key};
+    if ((e = sample_run(sa, s, pdl))) return e;
   }
   return step_finish_run(&c->st->pos, (uint32_t)nt, &c->st->key, &c->st->next, c->st->tok, c->hist, s, pdl);
 }
@@ -993,7 +1026,7 @@ int ensure_graph(nrc_ctx* c) {
   if (c->gexec) return NRC_OK;
   cudaGraph_t g = nullptr;
   CU(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-  cudaError_t e = enqueue_step(c, 1);
+  cudaError_t e = enqueue_step(c, 1, true);
   cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
   if (e != cudaSuccess || e2 != cudaSuccess) {
     if (g) cudaGraphDestroy(g);
@@ -1019,7 +1052,7 @@ extern "C" int nrc_ctx_forward(nrc_ctx* c, uint32_t token, float* logits_host, u
     // First step runs eagerly (warms per-kernel caches), later ones replay the graph.
     c->h_stage[16] = token;
     CU(cudaMemcpyAsync(c->st->tok, &c->h_stage[16], 4, cudaMemcpyHostToDevice, c->stream));
-    CU(enqueue_step(c, 1));
+    CU(enqueue_step(c, 1, true));
     int rc = finish_sync(c, logits_host, next_host, 1);
     if (rc) return rc;
     return ensure_graph(c);
@@ -1030,8 +1063,8 @@ extern "C" int nrc_ctx_forward(nrc_ctx* c, uint32_t token, float* logits_host, u
   return finish_sync(c, logits_host, next_host, 1);
 }
 
-extern "C" int nrc_ctx_prefill_chunk(nrc_ctx* c, const uint32_t* tokens, size_t n, float* logits_host,
-                                     uint32_t* next_host) {
+static int prefill_chunk_impl(nrc_ctx* c, const uint32_t* tokens, size_t n, float* logits_host, uint32_t* next_host,
+                              bool draw) {
   if (!c || !tokens) return fail(NRC_ERR_INVALID, "null argument");
   if (n < 1 || n > NRC_MAX_BATCH) return fail(NRC_ERR_BAD_BATCH, "prefill chunk of %zu tokens", n);
   if (c->pos + c->pending + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
@@ -1040,10 +1073,15 @@ extern "C" int nrc_ctx_prefill_chunk(nrc_ctx* c, const uint32_t* tokens, size_t 
   CU(cudaSetDevice(c->device));
   memcpy(&c->h_stage[16], tokens, n * 4);
   CU(cudaMemcpyAsync(c->st->tok, &c->h_stage[16], n * 4, cudaMemcpyHostToDevice, c->stream));
-  CU(enqueue_step(c, (int)n));
+  CU(enqueue_step(c, (int)n, draw));
   int rc = finish_sync(c, logits_host, next_host, n);
   if (rc) return rc;
   return ensure_graph(c);
+}
+
+extern "C" int nrc_ctx_prefill_chunk(nrc_ctx* c, const uint32_t* tokens, size_t n, float* logits_host,
+                                     uint32_t* next_host) {
+  return prefill_chunk_impl(c, tokens, n, logits_host, next_host, true);
 }
 
 extern "C" int nrc_ctx_prefill(nrc_ctx* c, const uint32_t* tokens, size_t n, float* logits_host, uint32_t* next_host) {
@@ -1053,7 +1091,7 @@ extern "C" int nrc_ctx_prefill(nrc_ctx* c, const uint32_t* tokens, size_t n, flo
   for (size_t i = 0; i < n; i += NRC_MAX_BATCH) {
     const size_t b = n - i < (size_t)NRC_MAX_BATCH ? n - i : (size_t)NRC_MAX_BATCH;
     const bool last = i + b == n;
-    int rc = nrc_ctx_prefill_chunk(c, tokens + i, b, last ? logits_host : nullptr, last ? next_host : nullptr);
+    int rc = prefill_chunk_impl(c, tokens + i, b, last ? logits_host : nullptr, last ? next_host : nullptr, last);
     if (rc) return rc;
   }
   return NRC_OK;
@@ -1091,6 +1129,44 @@ extern "C" int nrc_ctx_sync(nrc_ctx* c, uint32_t* next_host) {
   const size_t adv = c->pending;
   c->pending = 0;
   return finish_sync(c, nullptr, next_host, adv);
+}
+
+// Decode arithmetic: NRC_MODE_EXACT (the reference's summation order, bit for
+// bit) or NRC_MODE_FAST (tree reductions within the north star's tolerance).
+extern "C" int nrc_ctx_set_mode(nrc_ctx* c, int mode) {
+  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  if (mode != NRC_MODE_EXACT && mode != NRC_MODE_FAST) return fail(NRC_ERR_INVALID, "unknown mode %d", mode);
+  CU(cudaSetDevice(c->device));
+  CU(cudaStreamSynchronize(c->stream));
+  const bool fast = mode == NRC_MODE_FAST;
+  if (fast == c->fast) return NRC_OK;
+  c->fast = fast;
+  if (c->gexec) {
+    cudaGraphExecDestroy(c->gexec);
+    c->gexec = nullptr;
+    return ensure_graph(c);
+  }
+  return NRC_OK;
+}
+
+// Sampler::new (sample.rs:15-21) attached to the context: rng = seed | 1.
+extern "C" int nrc_ctx_set_sampler(nrc_ctx* c, float temperature, float top_p, uint64_t seed) {
+  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  if (c->vocab > SAMPLE_MAX_N) return fail(NRC_ERR_INVALID, "vocabulary of %d exceeds the sampler's %d", c->vocab, SAMPLE_MAX_N);
+  CU(cudaSetDevice(c->device));
+  CU(cudaStreamSynchronize(c->stream));
+  c->temperature = temperature;
+  c->top_p = top_p;
+  c->sampling = !(temperature <= 0.0f);
+  const unsigned long long rng = (unsigned long long)(seed | 1ull);
+  CU(cudaMemcpy(&c->st->rng, &rng, 8, cudaMemcpyHostToDevice));
+  // The decode graph is recaptured with (or without) the sampler kernels.
+  if (c->gexec) {
+    cudaGraphExecDestroy(c->gexec);
+    c->gexec = nullptr;
+    return ensure_graph(c);
+  }
+  return NRC_OK;
 }
 
 extern "C" int nrc_ctx_reset(nrc_ctx* c) {

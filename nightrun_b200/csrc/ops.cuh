@@ -65,6 +65,14 @@ struct AttnArgs {
 constexpr size_t ATTN_MAX_SMEM = 200 * 1024;
 size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx);
 cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl);
+// Decode attention of the tolerance mode (tree reductions, positions split
+// over `nsplit` CTAs per head, merged by the last one): scratch of
+// attention_fast_scratch_floats floats and n_heads zeroed counters.
+int attention_fast_splits(int ctx);
+size_t attention_fast_scratch_floats(int n_heads, int head_dim, int nsplit);
+size_t attention_fast_smem_bytes(int head_dim, int ctx, int nsplit);
+cudaError_t attention_fast_run(const AttnArgs& a, float* part, unsigned* count, int nsplit, cudaStream_t s,
+                               bool pdl);
 
 // Embedding rows (QMat::dequant_row, infer.rs:37-56) times embed_scale for nt
 // tokens read from tok_dev; also clears the greedy-argmax key.

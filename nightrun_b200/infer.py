@@ -135,6 +135,18 @@ class InferCtx:
     def logits(self):
         return self._logits.copy()
 
+    EXACT, FAST = 0, 1
+
+    def set_mode(self, mode):
+        """EXACT (default): bit-identical to the reference's scalar path. FAST:
+        decode steps with tree reductions, within the north star's tolerance."""
+        check(lib().nrc_ctx_set_mode(self.h, int(mode)))
+
+    def set_sampler(self, temperature, top_p, seed):
+        """Attach Sampler::new(temperature, top_p, seed) (sample.rs:15-21): every
+        step that returns a next token draws once on the device."""
+        check(lib().nrc_ctx_set_sampler(self.h, float(temperature), float(top_p), int(seed) & 0xFFFFFFFFFFFFFFFF))
+
     def reset(self):
         check(lib().nrc_ctx_reset(self.h))
 

@@ -125,6 +125,26 @@ def expf_hash(out, chunk0, nchunks, stream=None):
     check(lib().nrc_expf_hash(_ptr(out), chunk0, nchunks, _stream(stream)))
 
 
+class Sampler:
+    """nr_model::Sampler (crates/nr-model/src/sample.rs:5-96) drawing on the
+    device: `sample(logits)` takes a float32 CUDA tensor and returns the token id.
+    The xorshift64 state lives in device memory (seed | 1 at construction)."""
+
+    def __init__(self, temperature, top_p, seed, device="cuda"):
+        self.temperature = float(temperature)
+        self.top_p = float(top_p)
+        self.rng = torch.tensor([(seed | 1) & 0xFFFFFFFFFFFFFFFF], dtype=torch.uint64, device=device)
+        self._out = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def sample(self, logits, stream=None):
+        check(lib().nrc_sample(_ptr(logits), logits.numel(), self.temperature, self.top_p, _ptr(self.rng),
+                               _ptr(self._out), _stream(stream)))
+        return int(self._out.item())
+
+    def state(self):
+        return int(self.rng.cpu().item())
+
+
 def argmax(x, stream=None):
     """vec::argmax (vec.rs:80-90): index of the first maximum (host int)."""
     out = torch.zeros(1, dtype=torch.int32, device=x.device)

@@ -524,13 +524,14 @@ uint32_t sampler_sample(Sampler* s, const float* logits, size_t n) {
       }
     }
   }
-  // sort_unstable_by descending: the order among equal logits is unspecified
-  // in the reference; a stable descending insertion sort is used here.
+  // sort_unstable_by descending (sample.rs:66-67): the order among equal
+  // logits is unspecified in the reference; here equal logits are ordered by
+  // ascending token index (the order the device sampler uses).
   for (int i = 1; i < TOP_K; i++) {
     float v = hv[i];
     uint32_t id = hi[i];
     int j = i - 1;
-    while (j >= 0 && hv[j] < v) {
+    while (j >= 0 && (hv[j] < v || (hv[j] == v && hi[j] > id))) {
       hv[j + 1] = hv[j];
       hi[j + 1] = hi[j];
       j--;

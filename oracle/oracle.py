@@ -222,6 +222,14 @@ class Oracle:
         x = np.ascontiguousarray(x, np.float32)
         return self.L.or_argmax(self._p(x), x.size)
 
+    def sample(self, logits, temperature, top_p, state):
+        """Sampler::sample (sample.rs:32-96) with xorshift state `state` (already
+        seed | 1); returns (token, new state)."""
+        x = np.ascontiguousarray(logits, np.float32)
+        st = C.c_uint64(state)
+        tok = self.L.or_sampler_sample(temperature, top_p, C.byref(st), self._p(x), x.size)
+        return int(tok), int(st.value)
+
     def rope_freqs(self, head_dim, theta, scaling=None):
         out = np.empty(head_dim // 2, np.float32)
         f, lo, hi, orig = scaling if scaling else (0.0, 0.0, 0.0, 0.0)
