@@ -428,9 +428,10 @@ cudaError_t fast_gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   p.units = units;
   if (units == 0) return cudaSuccess;
   // Units per stage: the stage holds R rows (x 2 in pair mode) plus the
-  // alignment slack of each copy.
+  // alignment slack of each copy (at most 15 bytes before and 15 after each
+  // of up to FMAXP copies; the row loads read at most 6 bytes past a row).
   const int per_unit = p.row_bytes * (a.pair ? 2 : 1);
-  p.R = (FSTAGE - 16 * FMAXP) / per_unit;
+  p.R = (FSTAGE - 32 * FMAXP - 16) / per_unit;
   if (p.R < 1) return cudaErrorInvalidValue;  // a row larger than a stage
   p.x = a.xf;
   p.norm_w = a.norm_w;
