@@ -205,11 +205,12 @@ int nrc_ctx_decode_async(nrc_ctx* c, size_t n);
 int nrc_ctx_sync(nrc_ctx* c, uint32_t* next_host);
 /* Decode arithmetic of a context. NRC_MODE_EXACT (default): every sum in the reference's order,
  * logits and KV cache bit-identical to its scalar path. NRC_MODE_FAST: single-token decode steps
- * add block terms, the RMSNorm sum of squares and the attention softmax / V sums as trees (the
- * per-block integer dots and roundings, and the activation quantization, are unchanged); results
- * then differ from the reference in the last bits, within the north star's tolerance (1e-5
- * relative L2 per matvec, 1e-3 max-abs on the logits). Prefill chunks stay exact. No counterpart in
- * the reference, whose one CPU path is the exact one. */
+ * add the RMSNorm sum of squares and the attention softmax and V sums as trees (block dots, their
+ * roundings, the activation quantization and the matvec row sums are unchanged). A reordered sum
+ * can move an activation quant by one step, so logits drift from the scalar path about as far as
+ * the reference's own AVX2 path drifts (its x86 kernels reorder sums too). Prefill chunks stay
+ * exact. The reference's counterpart is the choice between its scalar and AVX2 kernels
+ * (crates/nr-tensor/src/kernels.rs:227-286). */
 #define NRC_MODE_EXACT 0
 #define NRC_MODE_FAST 1
 int nrc_ctx_set_mode(nrc_ctx* c, int mode);
@@ -227,6 +228,32 @@ int nrc_ctx_logits_device(const nrc_ctx* c, const float** out);
 void* nrc_ctx_stream(const nrc_ctx* c);
 /* Copy the f16 K and V cache rows of (layer, pos) to the host (kv_dim values each). */
 int nrc_ctx_kv(nrc_ctx* c, size_t layer, size_t pos, uint16_t* k_host, uint16_t* v_host);
+
+/* ---------------------------------------------------- several sequences (batched streams) */
+/* A context of n_seqs independent sequences decoded together: the reference runs one InferCtx
+ * per stream (crates/nr-model/src/infer.rs:319-778); here each sequence has its own KV cache and
+ * position and every linear layer runs once per pass over all sequences' tokens. Per sequence,
+ * logits and tokens are bit-identical to a single-sequence context. Greedy choice only; the
+ * single-sequence entry points (nrc_ctx_forward, ...) reject such a context, nrc_ctx_reset /
+ * nrc_ctx_free / nrc_ctx_stream apply. */
+int nrc_batch_new(const nrc_model* m, size_t ctx, size_t n_seqs, nrc_ctx** out);
+/* InferCtx::prefill (infer.rs:753-759) of every sequence: prompts back to back in tokens_host,
+ * lens_host[s] >= 1 tokens for sequence s; several sequences share each pass of up to
+ * max(64, n_seqs) tokens. next_host (optional, n_seqs ids) receives each greedy choice. */
+int nrc_batch_prefill(nrc_ctx* c, const uint32_t* tokens_host, const uint32_t* lens_host, uint32_t* next_host);
+/* One decode step of every sequence (InferCtx::forward, infer.rs:510-595), each consuming the token
+ * it chose last; logits_host (optional) receives [n_seqs][vocab], next_host (optional) [n_seqs]. */
+int nrc_batch_step(nrc_ctx* c, float* logits_host, uint32_t* next_host);
+/* n decode steps of every sequence on the device (graph replays); out_host[s * n + i] receives
+ * sequence s's choice after step i. */
+int nrc_batch_generate(nrc_ctx* c, size_t n, uint32_t* out_host);
+/* Enqueue n decode steps without waiting; nrc_batch_sync waits and returns the last choices. */
+int nrc_batch_decode_async(nrc_ctx* c, size_t n);
+int nrc_batch_sync(nrc_ctx* c, uint32_t* next_host);
+size_t nrc_batch_size(const nrc_ctx* c);
+size_t nrc_batch_pos(const nrc_ctx* c, size_t seq);
+/* Copy sequence seq's f16 K and V cache rows of (layer, pos) to the host. */
+int nrc_batch_kv(nrc_ctx* c, size_t seq, size_t layer, size_t pos, uint16_t* k_host, uint16_t* v_host);
 
 #ifdef __cplusplus
 }

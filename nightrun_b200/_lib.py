@@ -111,6 +111,15 @@ SIGNATURES = [
     ("nrc_ctx_logits_device", I, [P, C.POINTER(P)]),
     ("nrc_ctx_stream", P, [P]),
     ("nrc_ctx_kv", I, [P, S, S, P, P]),
+    ("nrc_batch_new", I, [P, S, S, C.POINTER(P)]),
+    ("nrc_batch_prefill", I, [P, P, P, P]),
+    ("nrc_batch_step", I, [P, P, P]),
+    ("nrc_batch_generate", I, [P, S, P]),
+    ("nrc_batch_decode_async", I, [P, S]),
+    ("nrc_batch_sync", I, [P, P]),
+    ("nrc_batch_size", S, [P]),
+    ("nrc_batch_pos", S, [P, S]),
+    ("nrc_batch_kv", I, [P, S, S, S, P, P]),
 ]
 
 

@@ -93,7 +93,8 @@ __global__ void k_rope_append(const RopeArgs a) {
   const int item = blockIdx.x * warps + threadIdx.x / 32;  // (token, head)
   if (item >= a.nt * nh) return;
   const int tok = item / nh, h = item % nh;
-  const uint32_t pos = a.pos_dev[0] + (uint32_t)tok;
+  const uint32_t pos = a.pos_tok ? a.pos_tok[tok] : a.pos_dev[0] + (uint32_t)tok;
+  const size_t cache_off = a.pos_tok ? (size_t)a.seq_tok[tok] * a.seq_stride : 0;
   const bool is_q = h < a.n_heads;
   const int kvh = h - a.n_heads;
   __shared__ float buf[8][128];
@@ -108,8 +109,8 @@ __global__ void k_rope_append(const RopeArgs a) {
     for (int i = 0; i < 4; i++)
       if (i < per) dst[lane + 32 * i] = outv[i];
   } else {
-    uint16_t* kd = a.kcache + (size_t)pos * kv_dim + kvh * hd;
-    uint16_t* vd = a.vcache + (size_t)pos * kv_dim + kvh * hd;
+    uint16_t* kd = a.kcache + cache_off + (size_t)pos * kv_dim + kvh * hd;
+    uint16_t* vd = a.vcache + cache_off + (size_t)pos * kv_dim + kvh * hd;
     const float* vs = a.v + (size_t)tok * kv_dim + kvh * hd;
 #pragma unroll
     for (int i = 0; i < 4; i++)
@@ -146,6 +147,10 @@ NRC_DEV void cp_async_wait() {
 //     shared memory by cp.async, double-buffered, the first chunk issued
 //     before the scores so its latency overlaps them.
 // f16 -> f32 uses the hardware conversion, exact for every f16 value.
+// FAST (tolerance mode): the same structure with fused multiply-adds in the
+// dot products, the softmax sum as a CTA tree and the V sums split over
+// ATT_THREADS / head_dim position groups combined in a fixed order.
+template <bool FAST>
 __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -154,21 +159,23 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   const int gqa = a.n_heads / a.n_kv_heads;
   const int g = h / gqa;
   const int att_dim = a.n_heads * hd, kv_dim = a.n_kv_heads * hd;
-  const uint32_t pos = a.pos_dev[0] + (uint32_t)tok;
+  const uint32_t pos = a.pos_tok ? a.pos_tok[tok] : a.pos_dev[0] + (uint32_t)tok;
   const int npos = (int)pos + 1;
   const bool fused = a.fused != 0;
+  const size_t cache_off = a.pos_tok ? (size_t)a.seq_tok[tok] * a.seq_stride : 0;
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                                               // [hd]
   float* hbuf = qs + hd;                                        // [3][hd] rope scratch (fused)
   uint16_t* knew = reinterpret_cast<uint16_t*>(hbuf + 3 * hd);  // [hd] new k (f16, fused)
   uint16_t* vnew = knew + hd;                                   // [hd] new v (f16, fused)
   float* sc = reinterpret_cast<float*>(vnew + hd);              // [ctx] scores, then probabilities
-  uint16_t* vs = reinterpret_cast<uint16_t*>(sc + ((a.ctx + 3) & ~3));  // [2][ATT_VCH][hd]
+  const int sc_len = ((a.ctx + 3) & ~3) > ATT_THREADS ? ((a.ctx + 3) & ~3) : ATT_THREADS;
+  uint16_t* vs = reinterpret_cast<uint16_t*>(sc + sc_len);      // [2][ATT_VCH][hd]
   __shared__ float red[ATT_THREADS / 32];
   __shared__ SeqSumShared ssh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint16_t* kbase = a.kcache + (size_t)g * hd;
-  uint16_t* vbase = a.vcache + (size_t)g * hd;
+  uint16_t* kbase = a.kcache + cache_off + (size_t)g * hd;
+  uint16_t* vbase = a.vcache + cache_off + (size_t)g * hd;
   const int cpr = hd / 8;  // 16-byte chunks per K/V row
   // Rows [0, cached) come from the cache; with the append fused, row `pos`
   // comes from shared memory.
@@ -236,8 +243,13 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
           const float* qd = qs + c * 8;
 #pragma unroll
           for (int j = 0; j < 4; j++) {
-            s = __fadd_rn(s, __fmul_rn(h2f(w[j] & 0xffffu), qd[2 * j]));
-            s = __fadd_rn(s, __fmul_rn(h2f(w[j] >> 16), qd[2 * j + 1]));
+            if (FAST) {
+              s = fmaf(h2f(w[j] & 0xffffu), qd[2 * j], s);
+              s = fmaf(h2f(w[j] >> 16), qd[2 * j + 1], s);
+            } else {
+              s = __fadd_rn(s, __fmul_rn(h2f(w[j] & 0xffffu), qd[2 * j]));
+              s = __fadd_rn(s, __fmul_rn(h2f(w[j] >> 16), qd[2 * j + 1]));
+            }
           }
         }
       }
@@ -255,8 +267,13 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
             const float* qd = qs + (c0 + c) * 8;
 #pragma unroll
             for (int j = 0; j < 4; j++) {
-              s = __fadd_rn(s, __fmul_rn(h2f(w[j] & 0xffffu), qd[2 * j]));
-              s = __fadd_rn(s, __fmul_rn(h2f(w[j] >> 16), qd[2 * j + 1]));
+              if (FAST) {
+                s = fmaf(h2f(w[j] & 0xffffu), qd[2 * j], s);
+                s = fmaf(h2f(w[j] >> 16), qd[2 * j + 1], s);
+              } else {
+                s = __fadd_rn(s, __fmul_rn(h2f(w[j] & 0xffffu), qd[2 * j]));
+                s = __fadd_rn(s, __fmul_rn(h2f(w[j] >> 16), qd[2 * j + 1]));
+              }
             }
           }
         }
@@ -276,13 +293,16 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   for (int w = 1; w < ATT_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
   for (int t = tid; t < npos; t += ATT_THREADS) sc[t] = expf_cr(__fsub_rn(sc[t], mx));
   __syncthreads();
-  // The sum in position order (vec.rs:35-36), one chain (seqsum.cuh).
-  const float sum = seq_sum_group<ATT_THREADS>(npos, [&](int t) { return sc[t]; }, ssh, tid, [] { __syncthreads(); });
+  // The sum in position order (vec.rs:35-36), one chain (seqsum.cuh); a tree in the tolerance mode.
+  const float sum = FAST ? tree_sum_group<ATT_THREADS>(npos, [&](int t) { return sc[t]; }, ssh, tid, [] { __syncthreads(); })
+                         : seq_sum_group<ATT_THREADS>(npos, [&](int t) { return sc[t]; }, ssh, tid, [] { __syncthreads(); });
   const float inv = __fdiv_rn(1.0f, sum);
   for (int t = tid; t < npos; t += ATT_THREADS) sc[t] = __fmul_rn(sc[t], inv);
 
   float acc = 0.0f;
-  const int d = tid;
+  // Exact: thread d chains every position. FAST: H position groups per dim.
+  const int H = FAST ? ATT_THREADS / hd : 1;
+  const int d = FAST ? tid % hd : tid, grp = FAST ? tid / hd : 0;
   int buf = 0;
   for (int t0 = 0; t0 < npos; t0 += ATT_VCH, buf ^= 1) {
     const int tn = min(ATT_VCH, npos - t0);
@@ -296,185 +316,30 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
     if (fused && (int)pos < t0 + tn)
       for (int i = tid; i < hd; i += ATT_THREADS) vb[((int)pos - t0) * hd + i] = vnew[i];
     __syncthreads();
-    if (d < hd) {
+    if (FAST) {
+      const uint16_t* vr = vb + d;
+      const float* p = sc + t0;
+#pragma unroll 4
+      for (int t = grp; t < tn; t += H) acc = fmaf(p[t], h2f(vr[(size_t)t * hd]), acc);
+    } else if (d < hd) {
       const uint16_t* vr = vb + d;
       const float* p = sc + t0;
       acc = seq_sum_serial(tn, [&](int t) { return __fmul_rn(p[t], h2f(vr[(size_t)t * hd])); }, acc);
     }
     __syncthreads();  // the buffer is restaged two chunks later
   }
-  if (d < hd) a.out[(size_t)tok * att_dim + (size_t)h * hd + d] = acc;
-}
-
-// Decode attention of the tolerance mode (infer.rs:553-572 up to summation
-// order): grid (query head, position split). The fused per-head norms, RoPE
-// and KV append are those of k_attention. Scores: one thread per position
-// (fused multiply-adds); softmax max and sum as CTA trees; V: hd/8 threads
-// per cached row, 16-byte loads, 8 accumulators each, the position groups
-// combined in a fixed order. With several splits each CTA writes (max, sum,
-// unnormalised output) and the last CTA of the head (an arrival counter, no
-// waiting) merges the splits in split order and resets the counter.
-constexpr int AF_THREADS = 128;
-
-__global__ void __launch_bounds__(AF_THREADS) k_attention_fast(const AttnArgs a, float* part, unsigned* count,
-                                                               int nsplit, int max_per) {
-  pdl_wait();
-  pdl_trigger();
-  const int h = blockIdx.x, sp = blockIdx.y;
-  const int hd = a.head_dim, half = hd / 2;
-  const int gqa = a.n_heads / a.n_kv_heads;
-  const int g = h / gqa;
-  const int kv_dim = a.n_kv_heads * hd;
-  const uint32_t pos = a.pos_dev[0];
-  const int npos = (int)pos + 1;
-  const int per = (npos + nsplit - 1) / nsplit;
-  const int t0 = min(npos, sp * per), t1 = min(npos, t0 + per);
-  const bool mine = (int)pos >= t0 && (int)pos < t1;  // this split holds the new position
-  extern __shared__ __align__(16) float sm[];
-  float* qs = sm;                                               // [hd]
-  float* hbuf = qs + hd;                                        // [3][hd]
-  uint16_t* knew = reinterpret_cast<uint16_t*>(hbuf + 3 * hd);  // [hd]
-  uint16_t* vnew = knew + hd;                                   // [hd]
-  float* sc = reinterpret_cast<float*>(vnew + hd);              // [max_per]
-  float* vpart = sc + ((max_per + 3) & ~3);                     // [16][hd]
-  __shared__ float red[AF_THREADS / 32];
-  __shared__ unsigned last;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint16_t* kbase = a.kcache + (size_t)g * hd;
-  const uint16_t* vbase = a.vcache + (size_t)g * hd;
-  {
-    const float* ct = a.cos_tab + (size_t)pos * half;
-    const float* st = a.sin_tab + (size_t)pos * half;
-    const int pr = hd / 32;
-    float outv[4];
-    if (warp == 0) {
-      warp_rope_head(a.q + (size_t)h * hd, a.q_norm, a.eps, ct, st, a.style, hd, hbuf, lane, outv);
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-        if (i < pr) qs[lane + 32 * i] = outv[i];
-    } else if (warp == 1 && mine) {
-      warp_rope_head(a.k + (size_t)g * hd, a.k_norm, a.eps, ct, st, a.style, hd, hbuf + hd, lane, outv);
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-        if (i < pr) {
-          const uint16_t kb = f32_to_f16(outv[i]);
-          knew[lane + 32 * i] = kb;
-          if (h % gqa == 0) a.kcache[(size_t)pos * kv_dim + (size_t)g * hd + lane + 32 * i] = kb;
-        }
-    } else if (warp == 2 && mine) {
-#pragma unroll
-      for (int i = 0; i < 4; i++)
-        if (i < pr) {
-          const uint16_t vb = f32_to_f16(a.v[(size_t)g * hd + lane + 32 * i]);
-          vnew[lane + 32 * i] = vb;
-          if (h % gqa == 0) a.vcache[(size_t)pos * kv_dim + (size_t)g * hd + lane + 32 * i] = vb;
-        }
+  if (FAST) {
+    // Combine the position groups in a fixed order (the scores buffer is free now).
+    sc[tid] = acc;
+    __syncthreads();
+    if (tid < hd) {
+      float o = 0.0f;
+      for (int g2 = 0; g2 < H; g2++) o += sc[g2 * hd + tid];
+      a.out[(size_t)tok * att_dim + (size_t)h * hd + tid] = o;
     }
-  }
-  __syncthreads();
-  // Scores.
-  const int cpr = hd / 8;
-  float mloc = -INFINITY;
-  for (int t = t0 + tid; t < t1; t += AF_THREADS) {
-    float s = 0.0f;
-    if (t == (int)pos) {
-      for (int d = 0; d < hd; d++) s = fmaf(h2f(knew[d]), qs[d], s);
-    } else {
-      const uint4* kr = reinterpret_cast<const uint4*>(kbase + (size_t)t * kv_dim);
-      for (int c0 = 0; c0 < cpr; c0 += 8) {
-        uint4 k8[8];
-#pragma unroll
-        for (int c = 0; c < 8; c++)
-          if (c0 + c < cpr) k8[c] = kr[c0 + c];
-#pragma unroll
-        for (int c = 0; c < 8; c++)
-          if (c0 + c < cpr) {
-            const uint32_t w[4] = {k8[c].x, k8[c].y, k8[c].z, k8[c].w};
-            const float* qd = qs + (c0 + c) * 8;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-              s = fmaf(h2f(w[j] & 0xffffu), qd[2 * j], s);
-              s = fmaf(h2f(w[j] >> 16), qd[2 * j + 1], s);
-            }
-          }
-      }
-    }
-    s = s * a.scale;
-    sc[t - t0] = s;
-    mloc = fmaxf(mloc, s);
-  }
-  mloc = warp_max(mloc);
-  if (lane == 0) red[warp] = mloc;
-  __syncthreads();
-  float mx = red[0];
-#pragma unroll
-  for (int w = 1; w < AF_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
-  __syncthreads();  // red is reused below
-  float lsum = 0.0f;
-  for (int t = t0 + tid; t < t1; t += AF_THREADS) {
-    const float e = expf_cr(sc[t - t0] - mx);
-    sc[t - t0] = e;
-    lsum += e;
-  }
-  lsum = warp_sum(lsum);
-  if (lane == 0) red[warp] = lsum;
-  __syncthreads();
-  float l = 0.0f;
-#pragma unroll
-  for (int w = 0; w < AF_THREADS / 32; w++) l += red[w];
-  // V: thread (c, grp) accumulates dims c*8 .. c*8+7 over positions t0 + grp, + P, ...
-  const int P = AF_THREADS / cpr;
-  const int c = tid % cpr, grp = tid / cpr;
-  float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
-  for (int t = t0 + grp; t < t1; t += P) {
-    const float e = sc[t - t0];
-    uint4 vv;
-    if (t == (int)pos)
-      vv = reinterpret_cast<const uint4*>(vnew)[c];
-    else
-      vv = reinterpret_cast<const uint4*>(vbase + (size_t)t * kv_dim)[c];
-    const uint32_t w[4] = {vv.x, vv.y, vv.z, vv.w};
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      acc[2 * j] = fmaf(e, h2f(w[j] & 0xffffu), acc[2 * j]);
-      acc[2 * j + 1] = fmaf(e, h2f(w[j] >> 16), acc[2 * j + 1]);
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 8; j++) vpart[grp * hd + c * 8 + j] = acc[j];
-  __syncthreads();
-  float o = 0.0f;
-  if (tid < hd)
-    for (int q = 0; q < P; q++) o += vpart[q * hd + tid];
-  float* out = a.out + (size_t)h * hd;
-  if (nsplit == 1) {
-    if (tid < hd) out[tid] = o / l;
     return;
   }
-  float* pp = part + ((size_t)h * nsplit + sp) * (hd + 2);
-  if (tid < hd) pp[2 + tid] = o;
-  if (tid == 0) {
-    pp[0] = mx;
-    pp[1] = l;
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) last = atomicAdd(&count[h], 1u);
-  __syncthreads();
-  if (last != (unsigned)nsplit - 1) return;
-  __threadfence();
-  const float* ph = part + (size_t)h * nsplit * (hd + 2);
-  float M = -INFINITY;
-  for (int k = 0; k < nsplit; k++) M = fmaxf(M, ph[k * (hd + 2)]);
-  float L = 0.0f, O = 0.0f;
-  for (int k = 0; k < nsplit; k++) {
-    const float* q = ph + k * (hd + 2);
-    const float f = q[1] > 0.0f ? expf_cr(q[0] - M) : 0.0f;
-    L += q[1] * f;
-    if (tid < hd) O += q[2 + tid] * f;
-  }
-  if (tid < hd) out[tid] = O / L;
-  if (tid == 0) count[h] = 0u;
+  if (d < hd) a.out[(size_t)tok * att_dim + (size_t)h * hd + d] = acc;
 }
 
 __global__ void k_embed(const EmbedArgs a) {
@@ -529,6 +394,52 @@ __global__ void k_embed(const EmbedArgs a) {
   }
 }
 
+// Rows of x selected for the classifier of a multi-sequence pass.
+__global__ void k_gather_rows(const float* __restrict__ x, int dim, const uint32_t* __restrict__ rows,
+                              float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const float* src = x + (size_t)rows[blockIdx.x] * dim;
+  float* dst = out + (size_t)blockIdx.x * dim;
+  for (int i = threadIdx.x; i < dim; i += blockDim.x) dst[i] = src[i];
+}
+
+// Greedy choice of each classifier row (vec::argmax, vec.rs:80-90: first
+// maximum) and the bookkeeping of its sequence: next token, next input,
+// position after the row's token, history.
+__global__ void k_rows_argmax(const float* __restrict__ logits, int vocab, const uint32_t* __restrict__ rows,
+                              const uint32_t* __restrict__ seq, const uint32_t* __restrict__ pos, uint32_t* bpos,
+                              uint32_t* btok, uint32_t* bnext, uint32_t* bhist, int ctx) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  const float* lr = logits + (size_t)r * vocab;
+  unsigned long long best = 0ull;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+    const float v = lr[i];
+    if (argmax_candidate(v)) {
+      const unsigned long long k = argmax_key(v, (uint32_t)i);
+      best = k > best ? k : best;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+    best = v > best ? v : best;
+  }
+  __shared__ unsigned long long wb[32];
+  if ((threadIdx.x & 31) == 0) wb[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) best = wb[w] > best ? wb[w] : best;
+  const uint32_t t = rows[r], sq = seq[t], p = pos[t];
+  const uint32_t nt = argmax_index(best);
+  bnext[sq] = nt;
+  btok[sq] = nt;
+  if ((int)p < ctx) bhist[(size_t)sq * ctx + p] = nt;
+  bpos[sq] = p + 1;
+}
+
 __global__ void k_step_finish(uint32_t* pos, uint32_t n, const unsigned long long* key, uint32_t* next_tok,
                               uint32_t* tok_in, uint32_t* hist) {
   pdl_wait();
@@ -568,48 +479,23 @@ cudaError_t rope_append_run(const RopeArgs& a, cudaStream_t s, bool pdl) {
 size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx) {
   (void)n_heads;
   (void)n_kv_heads;
-  // q + rope scratch (4 hd floats) | new k, v (2 hd f16) | scores | 2 V chunks
-  return (size_t)head_dim * 4 * 4 + (size_t)head_dim * 2 * 2 + (size_t)((ctx + 3) & ~3) * 4 +
-         (size_t)2 * ATT_VCH * head_dim * 2;
+  // q + rope scratch (4 hd floats) | new k, v (2 hd f16) | scores (at least one float per thread: the
+  // tolerance mode combines its V partial sums there) | 2 V chunks
+  const int sc = ((ctx + 3) & ~3) > ATT_THREADS ? ((ctx + 3) & ~3) : ATT_THREADS;
+  return (size_t)head_dim * 4 * 4 + (size_t)head_dim * 2 * 2 + (size_t)sc * 4 + (size_t)2 * ATT_VCH * head_dim * 2;
 }
 
-cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl) {
+cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl, bool fast) {
   if (a.n_kv_heads < 1 || a.n_heads % a.n_kv_heads || a.head_dim % 32 || a.head_dim > ATT_THREADS ||
-      (a.fused && a.nt != 1))
+      (a.fused && (a.nt != 1 || a.pos_tok)))
     return cudaErrorInvalidValue;
   const size_t smem = attention_smem_bytes(a.n_heads, a.n_kv_heads, a.head_dim, a.ctx);
   if (smem > ATTN_MAX_SMEM) return cudaErrorInvalidValue;
-  if (cudaError_t e = ensure_smem_attr((const void*)k_attention, ATTN_MAX_SMEM)) return e;
+  const void* fn = fast ? (const void*)k_attention<true> : (const void*)k_attention<false>;
+  if (cudaError_t e = ensure_smem_attr(fn, ATTN_MAX_SMEM)) return e;
   AttnArgs aa = a;
   void* args[] = {&aa};
-  return launch((const void*)k_attention, dim3(a.n_heads, a.nt), dim3(ATT_THREADS), smem, s, pdl, args);
-}
-
-int attention_fast_splits(int ctx) {
-  const int n = (ctx + 255) / 256;
-  return n < 1 ? 1 : (n > 32 ? 32 : n);
-}
-size_t attention_fast_scratch_floats(int n_heads, int head_dim, int nsplit) {
-  return (size_t)n_heads * nsplit * (head_dim + 2);
-}
-size_t attention_fast_smem_bytes(int head_dim, int ctx, int nsplit) {
-  const int max_per = (ctx + nsplit - 1) / nsplit;
-  return (size_t)head_dim * 4 * 4 + (size_t)head_dim * 2 * 2 + (size_t)((max_per + 3) & ~3) * 4 +
-         (size_t)16 * head_dim * 4;
-}
-
-cudaError_t attention_fast_run(const AttnArgs& a, float* part, unsigned* count, int nsplit, cudaStream_t s,
-                               bool pdl) {
-  if (a.n_kv_heads < 1 || a.n_heads % a.n_kv_heads || a.head_dim % 32 || a.head_dim < 64 || a.head_dim > 128 ||
-      a.nt != 1 || nsplit < 1 || (nsplit > 1 && (!part || !count)))
-    return cudaErrorInvalidValue;
-  const int max_per = (a.ctx + nsplit - 1) / nsplit;
-  const size_t smem = attention_fast_smem_bytes(a.head_dim, a.ctx, nsplit);
-  if (smem > ATTN_MAX_SMEM) return cudaErrorInvalidValue;
-  if (cudaError_t e = ensure_smem_attr((const void*)k_attention_fast, (int)ATTN_MAX_SMEM)) return e;
-  AttnArgs aa = a;
-  void* args[] = {&aa, &part, &count, &nsplit, (void*)&max_per};
-  return launch((const void*)k_attention_fast, dim3(a.n_heads, nsplit), dim3(AF_THREADS), smem, s, pdl, args);
+  return launch(fn, dim3(a.n_heads, a.nt), dim3(ATT_THREADS), smem, s, pdl, args);
 }
 
 cudaError_t embed_run(const EmbedArgs& a, cudaStream_t s, bool pdl) {
@@ -617,6 +503,21 @@ cudaError_t embed_run(const EmbedArgs& a, cudaStream_t s, bool pdl) {
   void* args[] = {&aa};
   const int bx = (a.dim + 255) / 256;
   return launch((const void*)k_embed, dim3(bx < 16 ? bx : 16, a.nt), dim3(256), 0, s, pdl, args);
+}
+
+cudaError_t gather_rows_run(const float* x, int dim, const uint32_t* rows, int nrows, float* out, cudaStream_t s,
+                            bool pdl) {
+  if (nrows <= 0) return cudaSuccess;
+  void* args[] = {&x, &dim, &rows, &out};
+  return launch((const void*)k_gather_rows, dim3(nrows), dim3(256), 0, s, pdl, args);
+}
+
+cudaError_t rows_argmax_run(const float* logits, int vocab, int nrows, const uint32_t* rows, const uint32_t* seq,
+                            const uint32_t* pos, uint32_t* bpos, uint32_t* btok, uint32_t* bnext, uint32_t* bhist,
+                            int ctx, cudaStream_t s, bool pdl) {
+  if (nrows <= 0) return cudaSuccess;
+  void* args[] = {&logits, &vocab, &rows, &seq, &pos, &bpos, &btok, &bnext, &bhist, &ctx};
+  return launch((const void*)k_rows_argmax, dim3(nrows), dim3(512), 0, s, pdl, args);
 }
 
 cudaError_t step_finish_run(uint32_t* pos_dev, uint32_t n, const unsigned long long* key, uint32_t* next_tok,

@@ -6,13 +6,13 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <memory>
 #include <mutex>
 #include <string>
 #include <vector>
 
 #include "common.cuh"
-#include "fast.cuh"
 #include "gemv.cuh"
 #include "mma.cuh"
 #include "nrcuda.h"
@@ -467,15 +467,24 @@ struct Status {
 };
 
 struct Layout {
-  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, status, hist, samp, afp, afc, total;
+  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, status, hist, samp;
+  // Several sequences: per-sequence positions / next input / last choice,
+  // 0..S-1, the pass's per-token ids / positions / sequences, classifier
+  // rows, gathered final rows, their logits, per-sequence token history.
+  size_t bpos, btok, bnext, biota, ctok, cpos, cseq, crow, xl, blogits, bhist;
+  size_t total;
 };
 
 size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
 
-Layout layout_for(const nrc_meta& mt, size_t ctx) {
+// Tokens per forward pass of a context of n_seqs sequences.
+size_t pass_tokens(size_t n_seqs) { return n_seqs > NRC_MAX_BATCH ? n_seqs : NRC_MAX_BATCH; }
+
+Layout layout_for(const nrc_meta& mt, size_t ctx, size_t n_seqs = 1, bool batch = false) {
   Layout L{};
   const size_t dim = mt.dim, att = (size_t)mt.n_heads * mt.head_dim, kv = (size_t)mt.n_kv_heads * mt.head_dim;
-  const size_t B = NRC_MAX_BATCH;
+  const size_t B = pass_tokens(n_seqs);
+  const size_t BM = (B + 63) / 64 * 64;  // tensor-core token groups
   size_t maxk = dim > att ? dim : att;
   if (mt.ffn_dim > maxk) maxk = mt.ffn_dim;
   size_t o = 0;
@@ -484,8 +493,9 @@ Layout layout_for(const nrc_meta& mt, size_t ctx) {
     o = al(o + bytes);
     return r;
   };
-  L.kc = take((size_t)mt.n_layers * ctx * kv * 2);
-  L.vc = take((size_t)mt.n_layers * ctx * kv * 2);
+  // KV caches f16 [layer][sequence][ctx][kv_dim].
+  L.kc = take((size_t)mt.n_layers * n_seqs * ctx * kv * 2);
+  L.vc = take((size_t)mt.n_layers * n_seqs * ctx * kv * 2);
   L.x = take(B * dim * 4);
   L.q = take(B * att * 4);
   L.k = take(B * kv * 4);
@@ -496,14 +506,25 @@ Layout layout_for(const nrc_meta& mt, size_t ctx) {
   L.logits = take((size_t)mt.vocab * 4);
   L.cos_t = take(ctx * (mt.head_dim / 2) * 4);
   L.sin_t = take(ctx * (mt.head_dim / 2) * 4);
-  L.mxq = take(B * maxk);            // tensor-core activation tiles (prefill)
-  L.mxd = take(B * (maxk / 32) * 4);  // and their block scales
+  L.mxq = take(BM * maxk);            // tensor-core activation tiles (prefill)
+  L.mxd = take(BM * (maxk / 32) * 4);  // and their block scales
   L.status = take(sizeof(Status));
   L.hist = take((ctx + 1) * 4);
   L.samp = take(sample_scratch_bytes((int)mt.vocab));  // sampler candidates
-  // Split-position partials and per-head arrival counters of the tolerance-mode attention.
-  L.afp = take(attention_fast_scratch_floats(mt.n_heads, mt.head_dim, attention_fast_splits((int)ctx)) * 4);
-  L.afc = take((size_t)mt.n_heads * 4);
+  if (batch) {
+    const size_t S = n_seqs;
+    L.bpos = take(S * 4);
+    L.btok = take(S * 4);
+    L.bnext = take(S * 4);
+    L.biota = take(S * 4);
+    L.ctok = take(B * 4);
+    L.cpos = take(B * 4);
+    L.cseq = take(B * 4);
+    L.crow = take(S * 4);
+    L.xl = take(S * dim * 4);
+    L.blogits = take(S * (size_t)mt.vocab * 4);
+    L.bhist = take(S * ctx * 4);
+  }
   L.total = o;
   return L;
 }
@@ -566,11 +587,17 @@ struct nrc_ctx {
   float temperature = 0.0f, top_p = 1.0f;
   bool sampling = false;
   unsigned long long* samp = nullptr;
-  // Tolerance mode (nrc_ctx_set_mode): decode steps use the tree-reduced kernels.
+  // Tolerance mode (nrc_ctx_set_mode): decode steps use tree reductions.
   bool fast = false;
-  float* af_part = nullptr;
-  unsigned* af_count = nullptr;
-  int af_nsplit = 1;
+  // Several sequences (nrc_batch_new): each has its own KV cache and position.
+  size_t n_seqs = 1, max_tok = NRC_MAX_BATCH;
+  bool batch = false;  // created by nrc_batch_new: the nrc_batch_* entry points drive it
+  uint32_t *bpos = nullptr, *btok = nullptr, *bnext = nullptr, *biota = nullptr;
+  uint32_t *ctok = nullptr, *cpos = nullptr, *cseq = nullptr, *crow = nullptr;
+  float *xl = nullptr, *blogits = nullptr;
+  uint32_t* bhist = nullptr;
+  std::vector<size_t> hpos;  // host copy of every sequence's position
+  uint32_t* h_big = nullptr;  // pinned staging for pass arrays (4 x max_tok words)
 };
 
 extern "C" int nrc_ctx_required_bytes(const nrc_model* m, size_t ctx, size_t* out) {
@@ -579,10 +606,12 @@ extern "C" int nrc_ctx_required_bytes(const nrc_model* m, size_t ctx, size_t* ou
   return NRC_OK;
 }
 
-// InferCtx::new (infer.rs:352-492): shape-checked binding of every tensor.
-extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
+// InferCtx::new (infer.rs:352-492): shape-checked binding of every tensor;
+// n_seqs independent sequences (each its own KV cache and position).
+static int ctx_create(const nrc_model* m, size_t ctx, size_t n_seqs, bool batch, nrc_ctx** out) {
   if (!m || !out) return fail(NRC_ERR_INVALID, "null argument");
   if (ctx == 0) return fail(NRC_ERR_INVALID, "ctx must be > 0");
+  if (n_seqs == 0 || n_seqs > 4096) return fail(NRC_ERR_INVALID, "n_seqs must be in 1..4096");
   *out = nullptr;
   const nrc_meta& mt = m->meta;
   if (mt.head_dim % 32 || mt.head_dim > 128 || mt.n_kv_heads == 0 || mt.n_heads % mt.n_kv_heads)
@@ -603,7 +632,7 @@ extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
   c->kv_dim = mt.n_kv_heads * mt.head_dim;
   c->ffn = mt.ffn_dim;
   c->vocab = mt.vocab;
-  std::unique_ptr<nrc_ctx> guard(c);
+  std::unique_ptr<nrc_ctx, int (*)(nrc_ctx*)> guard(c, nrc_ctx_free);
   const uint8_t* base = m->d_data;
   auto mat = [&](int kind, int layer, uint32_t rows, uint32_t cols, const uint8_t** p, int* fmt) -> int {
     const Entry* e = m->find(kind, layer);
@@ -658,7 +687,10 @@ extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
   c->logit_recip = 1.0f / mt.logit_scale;
 
   CU(cudaSetDevice(c->device));
-  c->lay = layout_for(mt, ctx);
+  c->n_seqs = n_seqs;
+  c->batch = batch;
+  c->max_tok = pass_tokens(n_seqs);
+  c->lay = layout_for(mt, ctx, n_seqs, batch);
   if (cudaMalloc(&c->arena, c->lay.total) != cudaSuccess)
     return fail(NRC_ERR_ALLOC, "inference arena exhausted (%llu bytes)", (unsigned long long)c->lay.total);
   CU(cudaMemset(c->arena, 0, c->lay.total));
@@ -680,9 +712,24 @@ extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
   c->st = reinterpret_cast<Status*>(A + c->lay.status);
   c->hist = reinterpret_cast<uint32_t*>(A + c->lay.hist);
   c->samp = reinterpret_cast<unsigned long long*>(A + c->lay.samp);
-  c->af_part = reinterpret_cast<float*>(A + c->lay.afp);
-  c->af_count = reinterpret_cast<unsigned*>(A + c->lay.afc);
-  c->af_nsplit = attention_fast_splits((int)ctx);
+  if (batch) {
+    c->bpos = reinterpret_cast<uint32_t*>(A + c->lay.bpos);
+    c->btok = reinterpret_cast<uint32_t*>(A + c->lay.btok);
+    c->bnext = reinterpret_cast<uint32_t*>(A + c->lay.bnext);
+    c->biota = reinterpret_cast<uint32_t*>(A + c->lay.biota);
+    c->ctok = reinterpret_cast<uint32_t*>(A + c->lay.ctok);
+    c->cpos = reinterpret_cast<uint32_t*>(A + c->lay.cpos);
+    c->cseq = reinterpret_cast<uint32_t*>(A + c->lay.cseq);
+    c->crow = reinterpret_cast<uint32_t*>(A + c->lay.crow);
+    c->xl = reinterpret_cast<float*>(A + c->lay.xl);
+    c->blogits = reinterpret_cast<float*>(A + c->lay.blogits);
+    c->bhist = reinterpret_cast<uint32_t*>(A + c->lay.bhist);
+    c->hpos.assign(n_seqs, 0);
+    std::vector<uint32_t> iota(n_seqs);
+    for (size_t i = 0; i < n_seqs; i++) iota[i] = (uint32_t)i;
+    CU(cudaMemcpy(c->biota, iota.data(), n_seqs * 4, cudaMemcpyHostToDevice));
+    CU(cudaMallocHost(&c->h_big, (c->max_tok * 3 + n_seqs) * 4));
+  }
 
   // RoPE tables (infer.rs:427-445; rope.rs:49-65): cos/sin of pos * freq.
   const size_t half = mt.head_dim / 2;
@@ -714,6 +761,8 @@ extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) {
   return NRC_OK;
 }
 
+extern "C" int nrc_ctx_new(const nrc_model* m, size_t ctx, nrc_ctx** out) { return ctx_create(m, ctx, 1, false, out); }
+
 extern "C" int nrc_ctx_free(nrc_ctx* c) {
   if (!c) return NRC_OK;
   cudaSetDevice(c->device);
@@ -721,6 +770,7 @@ extern "C" int nrc_ctx_free(nrc_ctx* c) {
   if (c->gexec) cudaGraphExecDestroy(c->gexec);
   if (c->stream) cudaStreamDestroy(c->stream);
   if (c->h_stage) cudaFreeHost(c->h_stage);
+  if (c->h_big) cudaFreeHost(c->h_big);
   if (c->arena) cudaFree(c->arena);
   delete c;
   return NRC_OK;
@@ -768,6 +818,7 @@ struct Lin {
   int rows[3];
   int nseg;
   int epi;
+  float scale = 1.0f;  // EPI_STORE: y = sum * scale
   // Weights of the next linear layer, prefetched into L2 while this one runs.
   const uint8_t* pf;
   size_t pf_bytes;
@@ -809,7 +860,7 @@ cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
     m.NS = NS;
     m.ntg = ntg;
     m.epi = L.epi == EPI_RESID ? EPI_RESID : EPI_STORE;
-    m.scale = 1.0f;
+    m.scale = L.scale;
     m.resid = c->x;
     m.resid_ld = c->dim;
     m.rs = c->rs;
@@ -819,6 +870,7 @@ cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
     return cudaSuccess;
   }
   GemvArgs a = gemv_base(c, L.fmt, L.K);
+  a.scale = L.scale;
   a.xf = L.x;
   a.xf_ld = L.K;
   a.norm_w = L.norm_w;
@@ -836,20 +888,30 @@ cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
   }
   a.pf = L.pf;
   a.pf_bytes = L.pf_bytes;
-  if (c->fast && nt == 1) {
-    a.nt = 1;
-    return fast_gemv_run(a, s, pdl);
-  }
+  a.fast_norm = c->fast && nt == 1;
   return gemv_tokens(a, nt, L.K, s, pdl);
 }
 
-// Enqueue one forward step over nt tokens at positions st->pos .. +nt-1
-// (infer.rs:510-595 for nt == 1, infer.rs:601-750 otherwise).
-cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw) {
+// The tokens of one pass of a context of several sequences: token t is id
+// ids[t] at position pos[t] of sequence seq[t]; the classifier runs on the
+// nrows tokens rows[0..nrows) (the last token of each sequence that ends in
+// this pass), whose sequences advance to position pos + 1.
+struct Pass {
+  const uint32_t* ids;
+  const uint32_t* pos;
+  const uint32_t* seq;
+  const uint32_t* rows;
+  int nrows;
+};
+
+// Enqueue one forward pass over nt tokens (infer.rs:510-595 for nt == 1,
+// infer.rs:601-750 otherwise): one sequence at positions st->pos .. +nt-1
+// (bp null), or the tokens of `bp` over several sequences.
+cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr) {
   cudaStream_t s = c->stream;
   const bool pdl = c->pdl;
   cudaError_t e;
-  EmbedArgs ea{c->embed, c->f_embed, c->dim, c->embed_scale, c->st->tok, nt, c->x, &c->st->key};
+  EmbedArgs ea{c->embed, c->f_embed, c->dim, c->embed_scale, bp ? bp->ids : c->st->tok, nt, c->x, &c->st->key};
   if ((e = embed_run(ea, s, pdl))) return e;
   // Weight regions of each layer's linear layers, for the L2 prefetch hints.
   auto qkv_region = [&](const LayerW& w, const uint8_t** p, size_t* n) {
@@ -897,8 +959,9 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw) {
         if ((e = linear(c, L, nt))) return e;
       }
     }
-    uint16_t* kc_l = c->kc + (size_t)l * c->ctx * c->kv_dim;
-    uint16_t* vc_l = c->vc + (size_t)l * c->ctx * c->kv_dim;
+    const size_t seq_stride = c->ctx * (size_t)c->kv_dim;
+    uint16_t* kc_l = c->kc + (size_t)l * c->n_seqs * seq_stride;
+    uint16_t* vc_l = c->vc + (size_t)l * c->n_seqs * seq_stride;
     AttnArgs aa{};
     aa.q = c->q;
     aa.out = c->att;
@@ -911,7 +974,12 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw) {
     aa.head_dim = c->hd;
     aa.ctx = (int)c->ctx;
     aa.pos_dev = &c->st->pos;
-    if (nt == 1) {
+    if (bp) {
+      aa.pos_tok = bp->pos;
+      aa.seq_tok = bp->seq;
+      aa.seq_stride = seq_stride;
+    }
+    if (nt == 1 && !bp) {
       // Decode: per-head norms, RoPE and the KV append fused into attention.
       aa.fused = 1;
       aa.k = c->k;
@@ -925,13 +993,14 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw) {
     } else {
       RopeArgs ra{c->q, c->k, c->v, w.q_norm, w.k_norm, c->eps, c->cos_t, c->sin_t, c->style, kc_l, vc_l,
                   nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
+      if (bp) {
+        ra.pos_tok = bp->pos;
+        ra.seq_tok = bp->seq;
+        ra.seq_stride = seq_stride;
+      }
       if ((e = rope_append_run(ra, s, pdl))) return e;
     }
-    if (c->fast && nt == 1 && c->hd >= 64)
-      e = attention_fast_run(aa, c->af_part, c->af_count, c->af_nsplit, s, pdl);
-    else
-      e = attention_run(aa, s, pdl);
-    if (e) return e;
+    if ((e = attention_run(aa, s, pdl, c->fast && nt == 1 && !bp))) return e;
     {  // output projection + residual (infer.rs:574-575)
       Lin L{};
       L.fmt = w.fo;
@@ -988,6 +1057,26 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw) {
       if ((e = linear(c, L, nt))) return e;
     }
   }
+  if (bp && bp->nrows == 0) return cudaSuccess;
+  if (bp) {
+    // Final norm + classifier on every sequence's last token of the pass, then
+    // each row's greedy argmax (infer.rs:586-591, 740-746; sample.rs:33-35).
+    if ((e = gather_rows_run(c->x, c->dim, bp->rows, bp->nrows, c->xl, s, pdl))) return e;
+    Lin L{};
+    L.fmt = c->f_out;
+    L.K = c->dim;
+    L.x = c->xl;
+    L.norm_w = c->out_norm;
+    L.w[0] = c->out_w;
+    L.y[0] = c->blogits;
+    L.rows[0] = c->vocab;
+    L.nseg = 1;
+    L.epi = EPI_STORE;
+    L.scale = c->logit_recip;
+    if ((e = linear(c, L, bp->nrows))) return e;
+    return rows_argmax_run(c->blogits, c->vocab, bp->nrows, bp->rows, bp->seq, bp->pos, c->bpos, c->btok, c->bnext,
+                           c->bhist, (int)c->ctx, s, pdl);
+  }
   // Final norm + classifier on the last token, fused greedy argmax (infer.rs:586-591, 740-746).
   {
     GemvArgs a = gemv_base(c, c->f_out, c->dim);
@@ -1000,7 +1089,8 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw) {
     a.scale = c->logit_recip;
     a.argmax_key = &c->st->key;
     a.nt = 1;
-    if ((e = (c->fast && nt == 1) ? fast_gemv_run(a, s, pdl) : gemv_run(a, s, pdl))) return e;
+    a.fast_norm = c->fast && nt == 1;
+    if ((e = gemv_run(a, s, pdl))) return e;
   }
   if (c->sampling && draw) {
     // Sampler::sample (sample.rs:32-96) replaces the greedy key with its draw.
@@ -1043,8 +1133,14 @@ int ensure_graph(nrc_ctx* c) {
 }
 }  // namespace
 
-extern "C" int nrc_ctx_forward(nrc_ctx* c, uint32_t token, float* logits_host, uint32_t* next_host) {
+static int not_batch(const nrc_ctx* c) {
   if (!c) return fail(NRC_ERR_INVALID, "null context");
+  if (c->batch) return fail(NRC_ERR_INVALID, "multi-sequence context: use the nrc_batch_* entry points");
+  return NRC_OK;
+}
+
+extern "C" int nrc_ctx_forward(nrc_ctx* c, uint32_t token, float* logits_host, uint32_t* next_host) {
+  if (int rc = not_batch(c)) return rc;
   if (c->pos + c->pending >= c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   if (token >= (uint32_t)c->vocab) return fail(NRC_ERR_BAD_TOKEN, "token %u >= vocab %d", token, c->vocab);
   CU(cudaSetDevice(c->device));
@@ -1065,7 +1161,8 @@ extern "C" int nrc_ctx_forward(nrc_ctx* c, uint32_t token, float* logits_host, u
 
 static int prefill_chunk_impl(nrc_ctx* c, const uint32_t* tokens, size_t n, float* logits_host, uint32_t* next_host,
                               bool draw) {
-  if (!c || !tokens) return fail(NRC_ERR_INVALID, "null argument");
+  if (int rc = not_batch(c)) return rc;
+  if (!tokens) return fail(NRC_ERR_INVALID, "null argument");
   if (n < 1 || n > NRC_MAX_BATCH) return fail(NRC_ERR_BAD_BATCH, "prefill chunk of %zu tokens", n);
   if (c->pos + c->pending + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   for (size_t i = 0; i < n; i++)
@@ -1085,7 +1182,8 @@ extern "C" int nrc_ctx_prefill_chunk(nrc_ctx* c, const uint32_t* tokens, size_t 
 }
 
 extern "C" int nrc_ctx_prefill(nrc_ctx* c, const uint32_t* tokens, size_t n, float* logits_host, uint32_t* next_host) {
-  if (!c || !tokens) return fail(NRC_ERR_INVALID, "null argument");
+  if (int rc = not_batch(c)) return rc;
+  if (!tokens) return fail(NRC_ERR_INVALID, "null argument");
   if (n == 0) return fail(NRC_ERR_BAD_BATCH, "empty prompt");
   if (c->pos + c->pending + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   for (size_t i = 0; i < n; i += NRC_MAX_BATCH) {
@@ -1098,7 +1196,8 @@ extern "C" int nrc_ctx_prefill(nrc_ctx* c, const uint32_t* tokens, size_t n, flo
 }
 
 extern "C" int nrc_ctx_generate(nrc_ctx* c, uint32_t first, size_t n, uint32_t* out_host) {
-  if (!c || (!out_host && n)) return fail(NRC_ERR_INVALID, "null argument");
+  if (int rc = not_batch(c)) return rc;
+  if (!out_host && n) return fail(NRC_ERR_INVALID, "null argument");
   if (n == 0) return NRC_OK;
   if (c->pos + c->pending + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   if (first >= (uint32_t)c->vocab) return fail(NRC_ERR_BAD_TOKEN, "token %u >= vocab %d", first, c->vocab);
@@ -1114,7 +1213,7 @@ extern "C" int nrc_ctx_generate(nrc_ctx* c, uint32_t first, size_t n, uint32_t* 
 }
 
 extern "C" int nrc_ctx_decode_async(nrc_ctx* c, size_t n) {
-  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  if (int rc = not_batch(c)) return rc;
   if (c->pos + c->pending + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "context window exhausted");
   if (!c->gexec) return fail(NRC_ERR_INVALID, "no decode step yet: call nrc_ctx_forward or nrc_ctx_prefill first");
   CU(cudaSetDevice(c->device));
@@ -1134,7 +1233,7 @@ extern "C" int nrc_ctx_sync(nrc_ctx* c, uint32_t* next_host) {
 // Decode arithmetic: NRC_MODE_EXACT (the reference's summation order, bit for
 // bit) or NRC_MODE_FAST (tree reductions within the north star's tolerance).
 extern "C" int nrc_ctx_set_mode(nrc_ctx* c, int mode) {
-  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  if (int rc = not_batch(c)) return rc;
   if (mode != NRC_MODE_EXACT && mode != NRC_MODE_FAST) return fail(NRC_ERR_INVALID, "unknown mode %d", mode);
   CU(cudaSetDevice(c->device));
   CU(cudaStreamSynchronize(c->stream));
@@ -1151,7 +1250,7 @@ extern "C" int nrc_ctx_set_mode(nrc_ctx* c, int mode) {
 
 // Sampler::new (sample.rs:15-21) attached to the context: rng = seed | 1.
 extern "C" int nrc_ctx_set_sampler(nrc_ctx* c, float temperature, float top_p, uint64_t seed) {
-  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  if (int rc = not_batch(c)) return rc;
   if (c->vocab > SAMPLE_MAX_N) return fail(NRC_ERR_INVALID, "vocabulary of %d exceeds the sampler's %d", c->vocab, SAMPLE_MAX_N);
   CU(cudaSetDevice(c->device));
   CU(cudaStreamSynchronize(c->stream));
@@ -1176,6 +1275,10 @@ extern "C" int nrc_ctx_reset(nrc_ctx* c) {
   c->pos = 0;
   c->pending = 0;
   CU(cudaMemsetAsync(&c->st->pos, 0, 4, c->stream));
+  if (c->batch) {
+    std::fill(c->hpos.begin(), c->hpos.end(), (size_t)0);
+    CU(cudaMemsetAsync(c->bpos, 0, c->n_seqs * 4, c->stream));
+  }
   CU(cudaStreamSynchronize(c->stream));
   return NRC_OK;
 }
@@ -1192,6 +1295,180 @@ extern "C" int nrc_ctx_kv(nrc_ctx* c, size_t layer, size_t pos, uint16_t* k_host
   if (layer >= (size_t)c->n_layers || pos >= c->ctx) return fail(NRC_ERR_INVALID, "kv index out of range");
   CU(cudaSetDevice(c->device));
   const size_t off = (layer * c->ctx + pos) * c->kv_dim;
+  CU(cudaMemcpyAsync(k_host, c->kc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaMemcpyAsync(v_host, c->vc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  return NRC_OK;
+}
+
+// ------------------------------------------------------------ several sequences
+// Independent sequences decoded together (the batched-stream workload): every
+// linear layer runs once per pass over all the pass's tokens, attention runs
+// per (sequence, head) over that sequence's own KV cache. Results per
+// sequence are bit-identical to a single-sequence context (every per-token
+// reduction keeps the reference's order; nothing mixes tokens).
+extern "C" int nrc_batch_new(const nrc_model* m, size_t ctx, size_t n_seqs, nrc_ctx** out) {
+  return ctx_create(m, ctx, n_seqs, true, out);
+}
+
+static int is_batch(const nrc_ctx* c) {
+  if (!c) return fail(NRC_ERR_INVALID, "null context");
+  if (!c->batch) return fail(NRC_ERR_INVALID, "not a multi-sequence context (nrc_batch_new)");
+  return NRC_OK;
+}
+
+static int batch_sync(nrc_ctx* c) {
+  CU(cudaMemcpyAsync(c->h_stage, &c->st->err, 4, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaStreamSynchronize(c->stream));
+  if (c->h_stage[0]) return fail(NRC_ERR_DEVICE, "kernel wait expired (error bits 0x%x)", c->h_stage[0]);
+  return NRC_OK;
+}
+
+// Prefill of every sequence: prompts back to back in `tokens`, lens[s] >= 1
+// tokens for sequence s (continuing at its current position). Tokens are
+// packed into passes of up to the context's pass size, several sequences per
+// pass (infer.rs:601-750 per sequence). next_host[s] (optional) receives
+// each sequence's greedy choice after its prompt.
+extern "C" int nrc_batch_prefill(nrc_ctx* c, const uint32_t* tokens, const uint32_t* lens, uint32_t* next_host) {
+  if (int rc = is_batch(c)) return rc;
+  if (!tokens || !lens) return fail(NRC_ERR_INVALID, "null argument");
+  const size_t S = c->n_seqs, B = c->max_tok;
+  size_t total = 0;
+  for (size_t q = 0; q < S; q++) {
+    if (lens[q] < 1) return fail(NRC_ERR_BAD_BATCH, "sequence %zu: empty prompt", q);
+    if (c->hpos[q] + lens[q] > c->ctx) return fail(NRC_ERR_CTX_FULL, "sequence %zu: context window exhausted", q);
+    total += lens[q];
+  }
+  for (size_t i = 0; i < total; i++)
+    if (tokens[i] >= (uint32_t)c->vocab) return fail(NRC_ERR_BAD_TOKEN, "token %u >= vocab %d", tokens[i], c->vocab);
+  CU(cudaSetDevice(c->device));
+  uint32_t* hid = c->h_big;
+  uint32_t* hp = hid + B;
+  uint32_t* hs = hp + B;
+  uint32_t* hr = hs + B;
+  size_t q = 0, j = 0, off = 0;  // sequence, token within it, offset in `tokens`
+  while (q < S) {
+    int nt = 0, nrows = 0;
+    while (q < S && (size_t)nt < B) {
+      hid[nt] = tokens[off];
+      hp[nt] = (uint32_t)(c->hpos[q] + j);
+      hs[nt] = (uint32_t)q;
+      nt++;
+      off++;
+      if (++j == lens[q]) {
+        hr[nrows++] = (uint32_t)(nt - 1);
+        c->hpos[q] += lens[q];
+        q++;
+        j = 0;
+      }
+    }
+    CU(cudaMemcpyAsync(c->ctok, hid, nt * 4, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemcpyAsync(c->cpos, hp, nt * 4, cudaMemcpyHostToDevice, c->stream));
+    CU(cudaMemcpyAsync(c->cseq, hs, nt * 4, cudaMemcpyHostToDevice, c->stream));
+    if (nrows) CU(cudaMemcpyAsync(c->crow, hr, nrows * 4, cudaMemcpyHostToDevice, c->stream));
+    const Pass pass{c->ctok, c->cpos, c->cseq, c->crow, nrows};
+    CU(enqueue_step(c, nt, false, &pass));
+    if (int rc = batch_sync(c)) return rc;  // the staging buffer is refilled by the next pass
+  }
+  if (next_host) {
+    CU(cudaMemcpyAsync(next_host, c->bnext, S * 4, cudaMemcpyDeviceToHost, c->stream));
+    CU(cudaStreamSynchronize(c->stream));
+  }
+  return NRC_OK;
+}
+
+static int ensure_batch_graph(nrc_ctx* c) {
+  if (c->gexec) return NRC_OK;
+  const Pass pass{c->btok, c->bpos, c->biota, c->biota, (int)c->n_seqs};
+  cudaGraph_t g = nullptr;
+  CU(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e = enqueue_step(c, (int)c->n_seqs, false, &pass);
+  cudaError_t e2 = cudaStreamEndCapture(c->stream, &g);
+  if (e != cudaSuccess || e2 != cudaSuccess) {
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    return fail(NRC_ERR_CUDA, "graph capture failed: %s", cudaGetErrorString(e != cudaSuccess ? e : e2));
+  }
+  e = cudaGraphInstantiate(&c->gexec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    c->gexec = nullptr;
+    return fail(NRC_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(e));
+  }
+  return NRC_OK;
+}
+
+static int batch_check_step(nrc_ctx* c, size_t n) {
+  for (size_t q = 0; q < c->n_seqs; q++) {
+    if (c->hpos[q] == 0) return fail(NRC_ERR_INVALID, "sequence %zu has no prompt yet: call nrc_batch_prefill", q);
+    if (c->hpos[q] + n > c->ctx) return fail(NRC_ERR_CTX_FULL, "sequence %zu: context window exhausted", q);
+  }
+  return NRC_OK;
+}
+
+// One decode step of every sequence (InferCtx::forward per sequence,
+// infer.rs:510-595): each consumes the token it chose last, on the device.
+// logits_host (optional) receives [n_seqs][vocab], next_host [n_seqs].
+extern "C" int nrc_batch_step(nrc_ctx* c, float* logits_host, uint32_t* next_host) {
+  if (int rc = is_batch(c)) return rc;
+  if (int rc = batch_check_step(c, 1)) return rc;
+  CU(cudaSetDevice(c->device));
+  if (int rc = ensure_batch_graph(c)) return rc;
+  CU(cudaGraphLaunch(c->gexec, c->stream));
+  for (auto& p : c->hpos) p++;
+  if (logits_host)
+    CU(cudaMemcpyAsync(logits_host, c->blogits, c->n_seqs * (size_t)c->vocab * 4, cudaMemcpyDeviceToHost,
+                       c->stream));
+  if (next_host) CU(cudaMemcpyAsync(next_host, c->bnext, c->n_seqs * 4, cudaMemcpyDeviceToHost, c->stream));
+  return batch_sync(c);
+}
+
+// n greedy decode steps of every sequence on the device (one graph replay per
+// step); out_host[s * n + i] = sequence s's choice after step i.
+extern "C" int nrc_batch_generate(nrc_ctx* c, size_t n, uint32_t* out_host) {
+  if (int rc = is_batch(c)) return rc;
+  if (!out_host && n) return fail(NRC_ERR_INVALID, "null argument");
+  if (n == 0) return NRC_OK;
+  if (int rc = batch_check_step(c, n)) return rc;
+  CU(cudaSetDevice(c->device));
+  if (int rc = ensure_batch_graph(c)) return rc;
+  std::vector<size_t> p0 = c->hpos;
+  for (size_t i = 0; i < n; i++) CU(cudaGraphLaunch(c->gexec, c->stream));
+  for (size_t q = 0; q < c->n_seqs; q++) {
+    CU(cudaMemcpyAsync(out_host + q * n, c->bhist + q * c->ctx + p0[q], n * 4, cudaMemcpyDeviceToHost, c->stream));
+    c->hpos[q] += n;
+  }
+  return batch_sync(c);
+}
+
+// Enqueue n decode steps of every sequence without waiting (pair with
+// nrc_batch_sync): the device-resident loop the batched throughput is timed on.
+extern "C" int nrc_batch_decode_async(nrc_ctx* c, size_t n) {
+  if (int rc = is_batch(c)) return rc;
+  if (int rc = batch_check_step(c, n)) return rc;
+  CU(cudaSetDevice(c->device));
+  if (int rc = ensure_batch_graph(c)) return rc;
+  for (size_t i = 0; i < n; i++) CU(cudaGraphLaunch(c->gexec, c->stream));
+  for (auto& p : c->hpos) p += n;
+  return NRC_OK;
+}
+extern "C" int nrc_batch_sync(nrc_ctx* c, uint32_t* next_host) {
+  if (int rc = is_batch(c)) return rc;
+  CU(cudaSetDevice(c->device));
+  if (next_host) CU(cudaMemcpyAsync(next_host, c->bnext, c->n_seqs * 4, cudaMemcpyDeviceToHost, c->stream));
+  return batch_sync(c);
+}
+
+extern "C" size_t nrc_batch_size(const nrc_ctx* c) { return c ? c->n_seqs : 0; }
+extern "C" size_t nrc_batch_pos(const nrc_ctx* c, size_t seq) {
+  return (c && c->batch && seq < c->n_seqs) ? c->hpos[seq] : 0;
+}
+extern "C" int nrc_batch_kv(nrc_ctx* c, size_t seq, size_t layer, size_t pos, uint16_t* k_host, uint16_t* v_host) {
+  if (int rc = is_batch(c)) return rc;
+  if (!k_host || !v_host) return fail(NRC_ERR_INVALID, "null argument");
+  if (seq >= c->n_seqs || layer >= (size_t)c->n_layers || pos >= c->ctx) return fail(NRC_ERR_INVALID, "kv index out of range");
+  CU(cudaSetDevice(c->device));
+  const size_t off = ((layer * c->n_seqs + seq) * c->ctx + pos) * c->kv_dim;
   CU(cudaMemcpyAsync(k_host, c->kc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
   CU(cudaMemcpyAsync(v_host, c->vc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
   CU(cudaStreamSynchronize(c->stream));

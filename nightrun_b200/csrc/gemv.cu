@@ -71,6 +71,7 @@ struct Params {
   int xf_ld;
   const float* norm_w;
   float eps;
+  int fast_norm;
   int epi;
   float scale;
   float* resid;
@@ -165,7 +166,8 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
     if (p.norm_w) {
       // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain,
       // seqsum.cuh), then scale = 1 / sqrtf(ss / n + eps).
-      const float ss = seq_sum_squares_group<NCT>(xs, K, ssh, tid, [] { named_sync(1, NCT); });
+      const float ss = p.fast_norm ? tree_sum_squares_group<NCT>(xs, K, ssh, tid, [] { named_sync(1, NCT); })
+                                   : seq_sum_squares_group<NCT>(xs, K, ssh, tid, [] { named_sync(1, NCT); });
       sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), p.eps)));
     }
     if (FMT == FMT_Q8_0) {
@@ -1083,6 +1085,7 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   p.xf_ld = a.xf_ld;
   p.norm_w = a.norm_w;
   p.eps = a.eps;
+  p.fast_norm = a.fast_norm;
   p.epi = a.epi;
   p.scale = a.scale;
   p.resid = a.resid;

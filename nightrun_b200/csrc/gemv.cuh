@@ -35,6 +35,7 @@ struct GemvArgs {
   int xf_ld;
   const float* norm_w;
   float eps;
+  int fast_norm;  // tolerance mode: the RMSNorm sum of squares as a tree (not the reference's chain)
   int epi;
   float scale;
   float* resid;

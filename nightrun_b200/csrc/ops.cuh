@@ -33,10 +33,16 @@ struct RopeArgs {
   const float* cos_tab;  // [ctx][head_dim/2]
   const float* sin_tab;
   int style;  // 0 Adjacent, 1 Neox
-  uint16_t* kcache;  // this layer's [ctx][kv_dim]
+  uint16_t* kcache;  // this layer's [ctx][kv_dim] (sequence 0)
   uint16_t* vcache;
   int nt, n_heads, n_kv_heads, head_dim, ctx;
   const uint32_t* pos_dev;
+  // Several sequences in one pass: token t sits at position pos_tok[t] of
+  // sequence seq_tok[t], whose cache starts seq_stride elements after
+  // sequence 0's. Null pos_tok: positions pos_dev[0] + t of sequence 0.
+  const uint32_t* pos_tok;
+  const uint32_t* seq_tok;
+  size_t seq_stride;
 };
 cudaError_t rope_append_run(const RopeArgs& a, cudaStream_t s, bool pdl);
 
@@ -59,20 +65,18 @@ struct AttnArgs {
   const float* cos_tab;
   const float* sin_tab;
   int style;
+  // Several sequences (RopeArgs: pos_tok, seq_tok, seq_stride); null pos_tok
+  // = positions pos_dev[0] + t of sequence 0. Not with `fused`.
+  const uint32_t* pos_tok;
+  const uint32_t* seq_tok;
+  size_t seq_stride;
 };
 // Shared memory of one attention CTA (its score rows hold `ctx` positions);
 // contexts needing more than ATTN_MAX_SMEM are rejected at context creation.
 constexpr size_t ATTN_MAX_SMEM = 200 * 1024;
 size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx);
-cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl);
-// Decode attention of the tolerance mode (tree reductions, positions split
-// over `nsplit` CTAs per head, merged by the last one): scratch of
-// attention_fast_scratch_floats floats and n_heads zeroed counters.
-int attention_fast_splits(int ctx);
-size_t attention_fast_scratch_floats(int n_heads, int head_dim, int nsplit);
-size_t attention_fast_smem_bytes(int head_dim, int ctx, int nsplit);
-cudaError_t attention_fast_run(const AttnArgs& a, float* part, unsigned* count, int nsplit, cudaStream_t s,
-                               bool pdl);
+// fast: the tolerance mode's tree-reduced variant (same inputs and outputs).
+cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl, bool fast = false);
 
 // Embedding rows (QMat::dequant_row, infer.rs:37-56) times embed_scale for nt
 // tokens read from tok_dev; also clears the greedy-argmax key.
@@ -85,6 +89,14 @@ struct EmbedArgs {
   float* x;  // [nt][dim]
   unsigned long long* argmax_key;
 };
+// Multi-sequence passes: gather the classifier rows of x; then each row's
+// greedy argmax and its sequence's bookkeeping (next token, next input,
+// position after the row's token, history [seq][ctx]).
+cudaError_t gather_rows_run(const float* x, int dim, const uint32_t* rows, int nrows, float* out, cudaStream_t s,
+                            bool pdl);
+cudaError_t rows_argmax_run(const float* logits, int vocab, int nrows, const uint32_t* rows, const uint32_t* seq,
+                            const uint32_t* pos, uint32_t* bpos, uint32_t* btok, uint32_t* bnext, uint32_t* bhist,
+                            int ctx, cudaStream_t s, bool pdl);
 cudaError_t embed_run(const EmbedArgs& a, cudaStream_t s, bool pdl);
 
 // Decode the argmax key into next_tok (and tok_in[0], the next step's input),

@@ -118,6 +118,7 @@ NRC_DEV void seq_sum_serial2(int n, const TermA& ta, const TermB& tb, float& sa,
 
 struct SeqSumShared {
   float s;
+  float w[32];  // per-warp partials of the tree sums
 };
 
 // seq_sum_squares_serial for a group of NTH threads (thread 0 runs it).
@@ -127,6 +128,47 @@ NRC_DEV float seq_sum_squares_group(const float* a, int n, SeqSumShared& sh, int
   if (tid == 0) sh.s = seq_sum_squares_serial(a, n);
   sync();
   const float r = sh.s;
+  sync();
+  return r;
+}
+
+// Tolerance mode: sum of a[i]^2 for a 16-byte aligned array as a tree (each
+// thread a strided partial, warp shuffles, the warps' partials in a fixed
+// order): deterministic, not the reference's sequential order.
+template <int NTH, class Sync>
+NRC_DEV float tree_sum_squares_group(const float* a, int n, SeqSumShared& sh, int tid, const Sync& sync) {
+  static_assert(NTH % 32 == 0 && NTH <= 1024, "group of whole warps");
+  float part = 0.0f;
+  const float4* a4 = reinterpret_cast<const float4*>(a);
+  for (int i = tid; i < n / 4; i += NTH) {
+    const float4 v = a4[i];
+    part = fmaf(v.x, v.x, part);
+    part = fmaf(v.y, v.y, part);
+    part = fmaf(v.z, v.z, part);
+    part = fmaf(v.w, v.w, part);
+  }
+  for (int i = (n & ~3) + tid; i < n; i += NTH) part = fmaf(a[i], a[i], part);
+  part = warp_sum(part);
+  if ((tid & 31) == 0) sh.w[tid >> 5] = part;
+  sync();
+  float r = 0.0f;
+#pragma unroll
+  for (int w = 0; w < NTH / 32; w++) r += sh.w[w];
+  sync();
+  return r;
+}
+
+// Tolerance mode: sum of term(i) for i < n as a tree (see above).
+template <int NTH, class Term, class Sync>
+NRC_DEV float tree_sum_group(int n, const Term& term, SeqSumShared& sh, int tid, const Sync& sync) {
+  float part = 0.0f;
+  for (int i = tid; i < n; i += NTH) part += term(i);
+  part = warp_sum(part);
+  if ((tid & 31) == 0) sh.w[tid >> 5] = part;
+  sync();
+  float r = 0.0f;
+#pragma unroll
+  for (int w = 0; w < NTH / 32; w++) r += sh.w[w];
   sync();
   return r;
 }

@@ -55,6 +55,9 @@ class Model:
     def ctx(self, ctx_len):
         return InferCtx(self, ctx_len)
 
+    def batch(self, ctx_len, n_seqs):
+        return BatchCtx(self, ctx_len, n_seqs)
+
     def close(self):
         if getattr(self, "h", None):
             lib().nrc_model_free(self.h)
@@ -163,6 +166,81 @@ class InferCtx:
         v = np.empty(kvd, np.uint16)
         check(lib().nrc_ctx_kv(self.h, layer, pos, k.ctypes.data_as(C.c_void_p), v.ctypes.data_as(C.c_void_p)))
         return k, v
+
+    def stream_handle(self):
+        return lib().nrc_ctx_stream(self.h)
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().nrc_ctx_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class BatchCtx:
+    """n_seqs independent sequences decoded together (one InferCtx per stream in
+    the reference, crates/nr-model/src/infer.rs:319-778): per-sequence KV caches
+    and positions, every linear layer once per pass over all sequences."""
+
+    def __init__(self, model, ctx_len, n_seqs):
+        self.model = model
+        h = C.c_void_p()
+        check(lib().nrc_batch_new(model.h, ctx_len, n_seqs, C.byref(h)))
+        self.h = h
+        self.n = n_seqs
+        self.vocab = model.meta.vocab
+
+    def prefill(self, prompts):
+        """Prefill every sequence with its prompt (a list of n_seqs token lists);
+        returns each sequence's greedy choice."""
+        assert len(prompts) == self.n
+        toks = np.ascontiguousarray(np.concatenate([np.asarray(p, np.uint32) for p in prompts]), np.uint32)
+        lens = np.array([len(p) for p in prompts], np.uint32)
+        nxt = np.zeros(self.n, np.uint32)
+        check(lib().nrc_batch_prefill(self.h, toks.ctypes.data_as(C.c_void_p), lens.ctypes.data_as(C.c_void_p),
+                                      nxt.ctypes.data_as(C.c_void_p)))
+        return nxt
+
+    def step(self, logits=True):
+        """One decode step of every sequence; returns (logits [n][vocab] or None, next ids)."""
+        nxt = np.zeros(self.n, np.uint32)
+        lg = np.zeros((self.n, self.vocab), np.float32) if logits else None
+        check(lib().nrc_batch_step(self.h, lg.ctypes.data_as(C.c_void_p) if logits else None,
+                                   nxt.ctypes.data_as(C.c_void_p)))
+        return lg, nxt
+
+    def generate(self, n):
+        """n device-side greedy steps; returns [n_seqs][n] ids."""
+        out = np.zeros((self.n, n), np.uint32)
+        check(lib().nrc_batch_generate(self.h, n, out.ctypes.data_as(C.c_void_p)))
+        return out
+
+    def decode_async(self, n):
+        check(lib().nrc_batch_decode_async(self.h, n))
+
+    def sync(self):
+        nxt = np.zeros(self.n, np.uint32)
+        check(lib().nrc_batch_sync(self.h, nxt.ctypes.data_as(C.c_void_p)))
+        return nxt
+
+    def pos(self, seq):
+        return lib().nrc_batch_pos(self.h, seq)
+
+    def kv(self, seq, layer, pos):
+        kvd = self.model.meta.n_kv_heads * self.model.meta.head_dim
+        k = np.empty(kvd, np.uint16)
+        v = np.empty(kvd, np.uint16)
+        check(lib().nrc_batch_kv(self.h, seq, layer, pos, k.ctypes.data_as(C.c_void_p),
+                                 v.ctypes.data_as(C.c_void_p)))
+        return k, v
+
+    def reset(self):
+        check(lib().nrc_ctx_reset(self.h))
 
     def stream_handle(self):
         return lib().nrc_ctx_stream(self.h)
