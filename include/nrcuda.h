@@ -229,6 +229,24 @@ void* nrc_ctx_stream(const nrc_ctx* c);
 /* Copy the f16 K and V cache rows of (layer, pos) to the host (kv_dim values each). */
 int nrc_ctx_kv(nrc_ctx* c, size_t layer, size_t pos, uint16_t* k_host, uint16_t* v_host);
 
+/* ---------------------------------------------------- tensor parallelism over NCCL */
+/* One sequence over nranks GPUs, one process (or thread) per GPU. Each rank computes whole output
+ * rows with the full K: its KV-head groups of wq / wk / wv and attention, equal row ranges of wo,
+ * ffn_gate / ffn_up, ffn_down and the classifier; the activations the next layer needs whole
+ * (attention output, residual stream, SwiGLU output, logits) are all-gathered and the greedy key
+ * all-reduced (max). No partial sums cross ranks, so logits and tokens are bit-identical to one
+ * GPU (the reference's residual adds, crates/nr-model/src/infer.rs:574-575 and :582-583, stay
+ * single roundings). The model must be loaded on each rank's device; NCCL is resolved at run time
+ * (libnccl.so.2). n_kv_heads, dim, ffn_dim and vocab must divide by nranks.
+ * nrc_tp_unique_id (on one rank) creates the NCCL id (128 bytes) every rank passes to
+ * nrc_tp_ctx_new; the single-sequence entry points then drive the context on every rank in the
+ * same order (they block until their collectives finish). nrc_ctx_kv returns this rank's KV heads. */
+int nrc_tp_unique_id(uint8_t* id_out128);
+int nrc_tp_ctx_new(const nrc_model* m, size_t ctx, int nranks, int rank, const uint8_t* id128, nrc_ctx** out);
+/* This rank's shard: {nranks, rank, q head0, q heads, kv head0, kv heads, dim row0, dim rows,
+ * ffn row0, ffn rows, vocab row0, vocab rows}. */
+int nrc_tp_shard(const nrc_ctx* c, int32_t* out12);
+
 /* ---------------------------------------------------- several sequences (batched streams) */
 /* A context of n_seqs independent sequences decoded together: the reference runs one InferCtx
  * per stream (crates/nr-model/src/infer.rs:319-778); here each sequence has its own KV cache and

@@ -111,6 +111,9 @@ SIGNATURES = [
     ("nrc_ctx_logits_device", I, [P, C.POINTER(P)]),
     ("nrc_ctx_stream", P, [P]),
     ("nrc_ctx_kv", I, [P, S, S, P, P]),
+    ("nrc_tp_unique_id", I, [P]),
+    ("nrc_tp_ctx_new", I, [P, S, I, I, P, C.POINTER(P)]),
+    ("nrc_tp_shard", I, [P, P]),
     ("nrc_batch_new", I, [P, S, S, C.POINTER(P)]),
     ("nrc_batch_prefill", I, [P, P, P, P]),
     ("nrc_batch_step", I, [P, P, P]),

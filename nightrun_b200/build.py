@@ -9,7 +9,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libnrcuda.so")
-SOURCES = ["gemv.cu", "mma.cu", "ops.cu", "attn.cu", "synth.cu", "engine.cu", "api.cu", "noalloc.cu", "sample.cu"]
+SOURCES = ["gemv.cu", "mma.cu", "ops.cu", "attn.cu", "synth.cu", "engine.cu", "api.cu", "noalloc.cu", "sample.cu", "tp.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
@@ -49,7 +49,7 @@ def build(verbose=False, jobs=None):
         for src, text in failed:
             sys.stderr.write(f"== nvcc failed on {src}\n{text}\n")
         raise RuntimeError("nvcc failed: " + ", ".join(s for s, _ in failed))
-    link = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", OUT] + objs + ["-lcudart"]
+    link = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", OUT] + objs + ["-lcudart", "-ldl"]
     subprocess.check_call(link)
     return OUT
 

@@ -19,6 +19,7 @@
 #include "ops.cuh"
 #include "sample.cuh"
 #include "synth.cuh"
+#include "tp.cuh"
 
 using namespace nrc;
 
@@ -466,8 +467,42 @@ struct Status {
   uint32_t tok[NRC_MAX_BATCH];
 };
 
+// This rank's part of the model under tensor parallelism over n ranks (n = 1:
+// everything). Query heads and KV heads go by whole KV groups; the rows of
+// wo / ffn_down (model dim), ffn_gate / ffn_up and the classifier (vocab) in
+// equal contiguous ranges. Every output element is computed whole, with the
+// full K, by exactly one rank; ranks exchange activations (all-gather), never
+// partial sums, so results are bit-identical to one GPU.
+struct Shard {
+  int n = 1, r = 0;
+  int h0 = 0, nh = 0;    // query heads
+  int kv0 = 0, nkv = 0;  // KV heads
+  int d0 = 0, dn = 0;    // model-dim rows (wo, ffn_down)
+  int f0 = 0, fn = 0;    // ffn rows (ffn_gate, ffn_up)
+  int v0 = 0, vn = 0;    // vocabulary rows (classifier)
+};
+
+int shard_for(const nrc_meta& mt, int n, int r, Shard* sh) {
+  if (n < 1 || r < 0 || r >= n) return NRC_ERR_INVALID;
+  if (mt.n_kv_heads % n || mt.dim % n || mt.ffn_dim % n || mt.vocab % n) return NRC_ERR_INVALID;
+  const int gqa = (int)(mt.n_heads / mt.n_kv_heads);
+  sh->n = n;
+  sh->r = r;
+  sh->nkv = (int)mt.n_kv_heads / n;
+  sh->kv0 = r * sh->nkv;
+  sh->nh = sh->nkv * gqa;
+  sh->h0 = sh->kv0 * gqa;
+  sh->dn = (int)mt.dim / n;
+  sh->d0 = r * sh->dn;
+  sh->fn = (int)mt.ffn_dim / n;
+  sh->f0 = r * sh->fn;
+  sh->vn = (int)mt.vocab / n;
+  sh->v0 = r * sh->vn;
+  return NRC_OK;
+}
+
 struct Layout {
-  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, status, hist, samp;
+  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, status, hist, samp, tps, tpr;
   // Several sequences: per-sequence positions / next input / last choice,
   // 0..S-1, the pass's per-token ids / positions / sequences, classifier
   // rows, gathered final rows, their logits, per-sequence token history.
@@ -480,9 +515,10 @@ size_t al(size_t v) { return (v + 255) & ~(size_t)255; }
 // Tokens per forward pass of a context of n_seqs sequences.
 size_t pass_tokens(size_t n_seqs) { return n_seqs > NRC_MAX_BATCH ? n_seqs : NRC_MAX_BATCH; }
 
-Layout layout_for(const nrc_meta& mt, size_t ctx, size_t n_seqs = 1, bool batch = false) {
+Layout layout_for(const nrc_meta& mt, size_t ctx, size_t n_seqs = 1, bool batch = false, int tp = 1) {
   Layout L{};
-  const size_t dim = mt.dim, att = (size_t)mt.n_heads * mt.head_dim, kv = (size_t)mt.n_kv_heads * mt.head_dim;
+  const size_t dim = mt.dim, att = (size_t)mt.n_heads * mt.head_dim;
+  const size_t kv = (size_t)mt.n_kv_heads * mt.head_dim / (size_t)tp;  // this rank's KV heads
   const size_t B = pass_tokens(n_seqs);
   const size_t BM = (B + 63) / 64 * 64;  // tensor-core token groups
   size_t maxk = dim > att ? dim : att;
@@ -511,6 +547,16 @@ Layout layout_for(const nrc_meta& mt, size_t ctx, size_t n_seqs = 1, bool batch 
   L.status = take(sizeof(Status));
   L.hist = take((ctx + 1) * 4);
   L.samp = take(sample_scratch_bytes((int)mt.vocab));  // sampler candidates
+  if (tp > 1) {
+    // Tensor parallelism: this rank's compact part of an activation [B][part]
+    // and the all-gathered parts of every rank [tp][B][part].
+    size_t part = att / tp;
+    part = std::max(part, dim / tp);
+    part = std::max(part, (size_t)mt.ffn_dim / tp);
+    const size_t send = std::max(B * part, (size_t)mt.vocab / tp);
+    L.tps = take(send * 4);
+    L.tpr = take(send * tp * 4);
+  }
   if (batch) {
     const size_t S = n_seqs;
     L.bpos = take(S * 4);
@@ -589,6 +635,11 @@ struct nrc_ctx {
   unsigned long long* samp = nullptr;
   // Tolerance mode (nrc_ctx_set_mode): decode steps use tree reductions.
   bool fast = false;
+  // Tensor parallelism (nrc_tp_ctx_new): this rank's shard, its KV width, NCCL.
+  Shard sh;
+  int kvl = 0;  // KV cache row width of this rank (n_kv_heads / tp * head_dim)
+  ncclComm_t comm = nullptr;
+  float *tp_send = nullptr, *tp_recv = nullptr;
   // Several sequences (nrc_batch_new): each has its own KV cache and position.
   size_t n_seqs = 1, max_tok = NRC_MAX_BATCH;
   bool batch = false;  // created by nrc_batch_new: the nrc_batch_* entry points drive it
@@ -608,7 +659,8 @@ extern "C" int nrc_ctx_required_bytes(const nrc_model* m, size_t ctx, size_t* ou
 
 // InferCtx::new (infer.rs:352-492): shape-checked binding of every tensor;
 // n_seqs independent sequences (each its own KV cache and position).
-static int ctx_create(const nrc_model* m, size_t ctx, size_t n_seqs, bool batch, nrc_ctx** out) {
+static int ctx_create(const nrc_model* m, size_t ctx, size_t n_seqs, bool batch, nrc_ctx** out, int tp_n = 1,
+                      int tp_r = 0, const uint8_t* tp_id = nullptr) {
   if (!m || !out) return fail(NRC_ERR_INVALID, "null argument");
   if (ctx == 0) return fail(NRC_ERR_INVALID, "ctx must be > 0");
   if (n_seqs == 0 || n_seqs > 4096) return fail(NRC_ERR_INVALID, "n_seqs must be in 1..4096");
@@ -687,10 +739,15 @@ static int ctx_create(const nrc_model* m, size_t ctx, size_t n_seqs, bool batch,
   c->logit_recip = 1.0f / mt.logit_scale;
 
   CU(cudaSetDevice(c->device));
+  if (shard_for(mt, tp_n, tp_r, &c->sh))
+    return fail(NRC_ERR_INVALID, "model does not split over %d ranks (KV heads %u, dim %u, ffn %u, vocab %u)", tp_n,
+                mt.n_kv_heads, mt.dim, mt.ffn_dim, mt.vocab);
+  if (tp_n > 1 && batch) return fail(NRC_ERR_INVALID, "tensor parallelism serves single-sequence contexts");
+  c->kvl = c->sh.nkv * c->hd;
   c->n_seqs = n_seqs;
   c->batch = batch;
   c->max_tok = pass_tokens(n_seqs);
-  c->lay = layout_for(mt, ctx, n_seqs, batch);
+  c->lay = layout_for(mt, ctx, n_seqs, batch, tp_n);
   if (cudaMalloc(&c->arena, c->lay.total) != cudaSuccess)
     return fail(NRC_ERR_ALLOC, "inference arena exhausted (%llu bytes)", (unsigned long long)c->lay.total);
   CU(cudaMemset(c->arena, 0, c->lay.total));
@@ -712,6 +769,19 @@ static int ctx_create(const nrc_model* m, size_t ctx, size_t n_seqs, bool batch,
   c->st = reinterpret_cast<Status*>(A + c->lay.status);
   c->hist = reinterpret_cast<uint32_t*>(A + c->lay.hist);
   c->samp = reinterpret_cast<unsigned long long*>(A + c->lay.samp);
+  if (tp_n > 1) {
+    c->tp_send = reinterpret_cast<float*>(A + c->lay.tps);
+    c->tp_recv = reinterpret_cast<float*>(A + c->lay.tpr);
+    const NcclApi* api = nccl_api();
+    if (!api) return fail(NRC_ERR_CUDA, "tensor parallelism needs NCCL (libnccl.so.2 not found)");
+    ncclUniqueId id;
+    memcpy(&id, tp_id, sizeof id);
+    const ncclResult_t nr = api->comm_init_rank(&c->comm, tp_n, id, tp_r);
+    if (nr != ncclSuccess) {
+      c->comm = nullptr;
+      return fail(NRC_ERR_CUDA, "ncclCommInitRank: %s", api->error_string(nr));
+    }
+  }
   if (batch) {
     c->bpos = reinterpret_cast<uint32_t*>(A + c->lay.bpos);
     c->btok = reinterpret_cast<uint32_t*>(A + c->lay.btok);
@@ -767,7 +837,9 @@ extern "C" int nrc_ctx_free(nrc_ctx* c) {
   if (!c) return NRC_OK;
   cudaSetDevice(c->device);
   if (c->stream) cudaStreamSynchronize(c->stream);
+  // A graph holding NCCL calls is released before its communicator.
   if (c->gexec) cudaGraphExecDestroy(c->gexec);
+  if (c->comm) nccl_api()->comm_destroy(c->comm);
   if (c->stream) cudaStreamDestroy(c->stream);
   if (c->h_stage) cudaFreeHost(c->h_stage);
   if (c->h_big) cudaFreeHost(c->h_big);
@@ -907,14 +979,44 @@ struct Pass {
 // Enqueue one forward pass over nt tokens (infer.rs:510-595 for nt == 1,
 // infer.rs:601-750 otherwise): one sequence at positions st->pos .. +nt-1
 // (bp null), or the tokens of `bp` over several sequences.
+// Bytes of one row of a K-column matrix of format fmt.
+size_t row_bytes(int fmt, int K) { return mat_bytes(fmt, 1, K); }
+
+// Tensor parallelism: all-gather this rank's compact part [nt][chunk] (in
+// tp_send) and spread every rank's part into dst [nt][ld] (resid: dst +=
+// rs * part, the residual add of the single-GPU epilogue).
+cudaError_t tp_gather(nrc_ctx* c, float* dst, int ld, int chunk, int nt, int resid) {
+  const NcclApi* api = nccl_api();
+  const ncclResult_t r =
+      api->all_gather(c->tp_send, c->tp_recv, (size_t)nt * chunk, ncclFloat32, c->comm, c->stream);
+  if (r != ncclSuccess) {
+    fail(NRC_ERR_CUDA, "ncclAllGather: %s", api->error_string(r));
+    return cudaErrorUnknown;
+  }
+  return tp_unpack_run(c->tp_recv, dst, ld, chunk, nt, c->sh.n, resid, c->rs, c->stream);
+}
+
+// Enqueue one forward pass over nt tokens (infer.rs:510-595 for nt == 1,
+// infer.rs:601-750 otherwise): one sequence at positions st->pos .. +nt-1
+// (bp null), or the tokens of `bp` over several sequences. Under tensor
+// parallelism every linear layer computes this rank's rows (Shard) and the
+// activations the next layer needs whole are all-gathered.
 cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr) {
   cudaStream_t s = c->stream;
   const bool pdl = c->pdl;
+  const Shard& sh = c->sh;
+  const bool tp = sh.n > 1;
+  const int hd = c->hd, ql = sh.nh * hd;
   cudaError_t e;
   EmbedArgs ea{c->embed, c->f_embed, c->dim, c->embed_scale, bp ? bp->ids : c->st->tok, nt, c->x, &c->st->key};
   if ((e = embed_run(ea, s, pdl))) return e;
   // Weight regions of each layer's linear layers, for the L2 prefetch hints.
   auto qkv_region = [&](const LayerW& w, const uint8_t** p, size_t* n) {
+    if (tp) {
+      *p = w.wq + (size_t)sh.h0 * hd * row_bytes(w.fq, c->dim);
+      *n = mat_bytes(w.fq, ql, c->dim);
+      return;
+    }
     const uint8_t* pq;
     size_t nq;
     span2(w.wq, mat_bytes(w.fq, c->att_dim, c->dim), w.wk, mat_bytes(w.fk, c->kv_dim, c->dim), &pq, &nq);
@@ -922,22 +1024,28 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
   };
   for (int l = 0; l < c->n_layers; l++) {
     const LayerW& w = c->L[l];
-    const uint8_t *pf_o = w.wo, *pf_gu, *pf_d = w.wd, *pf_next;
-    size_t n_o = mat_bytes(w.fo, c->dim, c->att_dim), n_gu, n_d = mat_bytes(w.fd, c->dim, c->ffn), n_next;
-    span2(w.wg, mat_bytes(w.fg, c->ffn, c->dim), w.wu, mat_bytes(w.fu, c->ffn, c->dim), &pf_gu, &n_gu);
+    const uint8_t* wo = w.wo + (size_t)sh.d0 * row_bytes(w.fo, c->att_dim);
+    const uint8_t* wg = w.wg + (size_t)sh.f0 * row_bytes(w.fg, c->dim);
+    const uint8_t* wu = w.wu + (size_t)sh.f0 * row_bytes(w.fu, c->dim);
+    const uint8_t* wd = w.wd + (size_t)sh.d0 * row_bytes(w.fd, c->ffn);
+    const uint8_t *pf_o = wo, *pf_gu, *pf_d = wd, *pf_next;
+    size_t n_o = mat_bytes(w.fo, sh.dn, c->att_dim), n_gu, n_d = mat_bytes(w.fd, sh.dn, c->ffn), n_next;
+    span2(wg, mat_bytes(w.fg, sh.fn, c->dim), wu, mat_bytes(w.fu, sh.fn, c->dim), &pf_gu, &n_gu);
     if (l + 1 < c->n_layers) {
       qkv_region(c->L[l + 1], &pf_next, &n_next);
     } else {
-      pf_next = c->out_w;  // the classifier: its first 48 MB (it is larger than L2)
-      n_next = std::min(mat_bytes(c->f_out, c->vocab, c->dim), (size_t)48 << 20);
+      pf_next = c->out_w + (size_t)sh.v0 * row_bytes(c->f_out, c->dim);  // the classifier: its first 48 MB
+      n_next = std::min(mat_bytes(c->f_out, sh.vn, c->dim), (size_t)48 << 20);
     }
     // QKV (infer.rs:527-531 / 620-637): rmsnorm + activation quantization fused
-    // into the consumer; one launch per weight format.
+    // into the consumer; one launch per weight format; this rank's heads.
     {
-      const uint8_t* ws[3] = {w.wq, w.wk, w.wv};
+      const uint8_t* ws[3] = {w.wq + (size_t)sh.h0 * hd * row_bytes(w.fq, c->dim),
+                              w.wk + (size_t)sh.kv0 * hd * row_bytes(w.fk, c->dim),
+                              w.wv + (size_t)sh.kv0 * hd * row_bytes(w.fv, c->dim)};
       const int fs[3] = {w.fq, w.fk, w.fv};
       float* ys[3] = {c->q, c->k, c->v};
-      const int rows[3] = {c->att_dim, c->kv_dim, c->kv_dim};
+      const int rows[3] = {ql, c->kvl, c->kvl};
       bool done[3] = {false, false, false};
       for (int i = 0; i < 3; i++) {
         if (done[i]) continue;
@@ -959,19 +1067,19 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
         if ((e = linear(c, L, nt))) return e;
       }
     }
-    const size_t seq_stride = c->ctx * (size_t)c->kv_dim;
+    const size_t seq_stride = c->ctx * (size_t)c->kvl;
     uint16_t* kc_l = c->kc + (size_t)l * c->n_seqs * seq_stride;
     uint16_t* vc_l = c->vc + (size_t)l * c->n_seqs * seq_stride;
     AttnArgs aa{};
     aa.q = c->q;
-    aa.out = c->att;
+    aa.out = tp ? c->tp_send : c->att;
     aa.kcache = kc_l;
     aa.vcache = vc_l;
     aa.scale = c->att_scale;
     aa.nt = nt;
-    aa.n_heads = c->n_heads;
-    aa.n_kv_heads = c->n_kv;
-    aa.head_dim = c->hd;
+    aa.n_heads = sh.nh;
+    aa.n_kv_heads = sh.nkv;
+    aa.head_dim = hd;
     aa.ctx = (int)c->ctx;
     aa.pos_dev = &c->st->pos;
     if (bp) {
@@ -992,7 +1100,7 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
       aa.style = c->style;
     } else {
       RopeArgs ra{c->q, c->k, c->v, w.q_norm, w.k_norm, c->eps, c->cos_t, c->sin_t, c->style, kc_l, vc_l,
-                  nt, c->n_heads, c->n_kv, c->hd, (int)c->ctx, &c->st->pos};
+                  nt, sh.nh, sh.nkv, hd, (int)c->ctx, &c->st->pos};
       if (bp) {
         ra.pos_tok = bp->pos;
         ra.seq_tok = bp->seq;
@@ -1001,60 +1109,67 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
       if ((e = rope_append_run(ra, s, pdl))) return e;
     }
     if ((e = attention_run(aa, s, pdl, c->fast && nt == 1 && !bp))) return e;
+    if (tp && (e = tp_gather(c, c->att, c->att_dim, ql, nt, 0))) return e;
     {  // output projection + residual (infer.rs:574-575)
       Lin L{};
       L.fmt = w.fo;
       L.K = c->att_dim;
       L.x = c->att;
-      L.w[0] = w.wo;
-      L.rows[0] = c->dim;
+      L.w[0] = wo;
+      L.y[0] = c->tp_send;
+      L.rows[0] = sh.dn;
       L.nseg = 1;
-      L.epi = EPI_RESID;
+      L.epi = tp ? EPI_STORE : EPI_RESID;
       L.pf = pf_gu;
       L.pf_bytes = n_gu;
       if ((e = linear(c, L, nt))) return e;
+      if (tp && (e = tp_gather(c, c->x, c->dim, sh.dn, nt, 1))) return e;
     }
     {  // SwiGLU MLP gate/up (infer.rs:577-581)
+      float* g = tp ? c->tp_send : c->g;
       Lin L{};
       L.fmt = w.fg;
       L.K = c->dim;
       L.x = c->x;
       L.norm_w = w.ffn_norm;
-      L.w[0] = w.wg;
-      L.y[0] = c->g;
-      L.rows[0] = c->ffn;
+      L.w[0] = wg;
+      L.y[0] = g;
+      L.rows[0] = sh.fn;
       L.nseg = 1;
       L.epi = EPI_STORE;
       L.pf = pf_d;
       L.pf_bytes = n_d;
       if (w.fg == w.fu) {
-        L.w[1] = w.wu;
+        L.w[1] = wu;
         L.y[1] = c->u;
-        L.rows[1] = c->ffn;
+        L.rows[1] = sh.fn;
         L.nseg = 2;
         L.epi = EPI_SWIGLU;
         if ((e = linear(c, L, nt))) return e;
       } else {
         if ((e = linear(c, L, nt))) return e;
         L.fmt = w.fu;
-        L.w[0] = w.wu;
+        L.w[0] = wu;
         L.y[0] = c->u;
         if ((e = linear(c, L, nt))) return e;
-        if ((e = op_swiglu(c->g, c->u, (size_t)nt * c->ffn, s))) return e;
+        if ((e = op_swiglu(g, c->u, (size_t)nt * sh.fn, s))) return e;
       }
+      if (tp && (e = tp_gather(c, c->g, c->ffn, sh.fn, nt, 0))) return e;
     }
     {  // down projection + residual (infer.rs:582-583)
       Lin L{};
       L.fmt = w.fd;
       L.K = c->ffn;
       L.x = c->g;
-      L.w[0] = w.wd;
-      L.rows[0] = c->dim;
+      L.w[0] = wd;
+      L.y[0] = c->tp_send;
+      L.rows[0] = sh.dn;
       L.nseg = 1;
-      L.epi = EPI_RESID;
+      L.epi = tp ? EPI_STORE : EPI_RESID;
       L.pf = pf_next;
       L.pf_bytes = n_next;
       if ((e = linear(c, L, nt))) return e;
+      if (tp && (e = tp_gather(c, c->x, c->dim, sh.dn, nt, 1))) return e;
     }
   }
   if (bp && bp->nrows == 0) return cudaSuccess;
@@ -1077,20 +1192,33 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
     return rows_argmax_run(c->blogits, c->vocab, bp->nrows, bp->rows, bp->seq, bp->pos, c->bpos, c->btok, c->bnext,
                            c->bhist, (int)c->ctx, s, pdl);
   }
-  // Final norm + classifier on the last token, fused greedy argmax (infer.rs:586-591, 740-746).
+  // Final norm + classifier on the last token, fused greedy argmax (infer.rs:586-591, 740-746);
+  // under tensor parallelism this rank's vocabulary rows, then the logits
+  // all-gathered and the greedy key reduced (max) over ranks.
   {
     GemvArgs a = gemv_base(c, c->f_out, c->dim);
     a.xf = c->x + (size_t)(nt - 1) * c->dim;
     a.xf_ld = c->dim;
     a.norm_w = c->out_norm;
-    a.seg[0] = GemvSegArg{c->out_w, c->logits, c->vocab, c->vocab};
+    float* lg = tp ? c->tp_send : c->logits;
+    a.seg[0] = GemvSegArg{c->out_w + (size_t)sh.v0 * row_bytes(c->f_out, c->dim), lg, sh.vn, sh.vn};
     a.nseg = 1;
     a.epi = EPI_ARGMAX;
     a.scale = c->logit_recip;
     a.argmax_key = &c->st->key;
+    a.argmax_base = sh.v0;
     a.nt = 1;
     a.fast_norm = c->fast && nt == 1;
     if ((e = gemv_run(a, s, pdl))) return e;
+    if (tp) {
+      if ((e = tp_gather(c, c->logits, c->vocab, sh.vn, 1, 0))) return e;
+      const NcclApi* api = nccl_api();
+      const ncclResult_t r = api->all_reduce(&c->st->key, &c->st->key, 1, ncclUint64, ncclMax, c->comm, s);
+      if (r != ncclSuccess) {
+        fail(NRC_ERR_CUDA, "ncclAllReduce: %s", api->error_string(r));
+        return cudaErrorUnknown;
+      }
+    }
   }
   if (c->sampling && draw) {
     // Sampler::sample (sample.rs:32-96) replaces the greedy key with its draw.
@@ -1294,9 +1422,9 @@ extern "C" int nrc_ctx_kv(nrc_ctx* c, size_t layer, size_t pos, uint16_t* k_host
   if (!c || !k_host || !v_host) return fail(NRC_ERR_INVALID, "null argument");
   if (layer >= (size_t)c->n_layers || pos >= c->ctx) return fail(NRC_ERR_INVALID, "kv index out of range");
   CU(cudaSetDevice(c->device));
-  const size_t off = (layer * c->ctx + pos) * c->kv_dim;
-  CU(cudaMemcpyAsync(k_host, c->kc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
-  CU(cudaMemcpyAsync(v_host, c->vc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
+  const size_t off = (layer * c->ctx + pos) * c->kvl;
+  CU(cudaMemcpyAsync(k_host, c->kc + off, c->kvl * 2, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaMemcpyAsync(v_host, c->vc + off, c->kvl * 2, cudaMemcpyDeviceToHost, c->stream));
   CU(cudaStreamSynchronize(c->stream));
   return NRC_OK;
 }
@@ -1468,9 +1596,36 @@ extern "C" int nrc_batch_kv(nrc_ctx* c, size_t seq, size_t layer, size_t pos, ui
   if (!k_host || !v_host) return fail(NRC_ERR_INVALID, "null argument");
   if (seq >= c->n_seqs || layer >= (size_t)c->n_layers || pos >= c->ctx) return fail(NRC_ERR_INVALID, "kv index out of range");
   CU(cudaSetDevice(c->device));
-  const size_t off = ((layer * c->n_seqs + seq) * c->ctx + pos) * c->kv_dim;
-  CU(cudaMemcpyAsync(k_host, c->kc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
-  CU(cudaMemcpyAsync(v_host, c->vc + off, c->kv_dim * 2, cudaMemcpyDeviceToHost, c->stream));
+  const size_t off = ((layer * c->n_seqs + seq) * c->ctx + pos) * c->kvl;
+  CU(cudaMemcpyAsync(k_host, c->kc + off, c->kvl * 2, cudaMemcpyDeviceToHost, c->stream));
+  CU(cudaMemcpyAsync(v_host, c->vc + off, c->kvl * 2, cudaMemcpyDeviceToHost, c->stream));
   CU(cudaStreamSynchronize(c->stream));
+  return NRC_OK;
+}
+
+// ------------------------------------------------------------ tensor parallelism
+extern "C" int nrc_tp_unique_id(uint8_t* out) {
+  if (!out) return fail(NRC_ERR_INVALID, "null argument");
+  const NcclApi* api = nccl_api();
+  if (!api) return fail(NRC_ERR_CUDA, "tensor parallelism needs NCCL (libnccl.so.2 not found)");
+  ncclUniqueId id;
+  const ncclResult_t r = api->get_unique_id(&id);
+  if (r != ncclSuccess) return fail(NRC_ERR_CUDA, "ncclGetUniqueId: %s", api->error_string(r));
+  memcpy(out, &id, sizeof id);
+  return NRC_OK;
+}
+
+extern "C" int nrc_tp_ctx_new(const nrc_model* m, size_t ctx, int nranks, int rank, const uint8_t* id, nrc_ctx** out) {
+  if (!id) return fail(NRC_ERR_INVALID, "null argument");
+  if (nranks < 1 || rank < 0 || rank >= nranks) return fail(NRC_ERR_INVALID, "rank %d of %d", rank, nranks);
+  if (nranks == 1) return ctx_create(m, ctx, 1, false, out);
+  return ctx_create(m, ctx, 1, false, out, nranks, rank, id);
+}
+
+extern "C" int nrc_tp_shard(const nrc_ctx* c, int32_t* out) {
+  if (!c || !out) return fail(NRC_ERR_INVALID, "null argument");
+  const Shard& sh = c->sh;
+  const int32_t v[12] = {sh.n, sh.r, sh.h0, sh.nh, sh.kv0, sh.nkv, sh.d0, sh.dn, sh.f0, sh.fn, sh.v0, sh.vn};
+  memcpy(out, v, sizeof v);
   return NRC_OK;
 }

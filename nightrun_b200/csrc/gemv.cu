@@ -78,6 +78,7 @@ struct Params {
   int resid_ld;
   float rs;
   unsigned long long* argmax_key;
+  int argmax_base;
   unsigned* err;
   const uint8_t* pf;  // next kernel's weights to prefetch into L2 (16-byte aligned), or null
   size_t pf_bytes;
@@ -546,7 +547,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) gemv_kernel(const __grid_constant
         const int sg = sp0.seg;
         p.y[sg][(size_t)c_tok * p.ld[sg] + row] = sv;
         if (p.epi == EPI_ARGMAX && c_tok == 0 && argmax_candidate(sv)) {
-          const unsigned long long key = argmax_key(sv, (uint32_t)row);
+          const unsigned long long key = argmax_key(sv, (uint32_t)(row + p.argmax_base));
           best = key > best ? key : best;
         }
       }
@@ -786,7 +787,7 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
             if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
             p.y[seg][(size_t)t * p.ld[seg] + row] = sv;
             if (p.epi == EPI_ARGMAX && t == 0 && argmax_candidate(sv)) {
-              const unsigned long long key = argmax_key(sv, (uint32_t)row);
+              const unsigned long long key = argmax_key(sv, (uint32_t)(row + p.argmax_base));
               best = key > best ? key : best;
             }
           }
@@ -1092,6 +1093,7 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   p.resid_ld = a.resid_ld;
   p.rs = a.rs;
   p.argmax_key = a.argmax_key;
+  p.argmax_base = a.argmax_base;
   p.err = a.err;
   if (a.pf && (reinterpret_cast<uintptr_t>(a.pf) & 15) == 0) {
     p.pf = static_cast<const uint8_t*>(a.pf);

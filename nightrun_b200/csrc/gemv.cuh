@@ -42,6 +42,7 @@ struct GemvArgs {
   int resid_ld;
   float rs;
   unsigned long long* argmax_key;  // one key (token 0)
+  int argmax_base;                 // index of row 0 in the argmax key (a vocabulary shard's first row)
   unsigned* err;                   // device error word
   // Optional L2 prefetch of the weights the next kernel will stream (a hint:
   // results do not depend on it). Every CTA prefetches its share once its

@@ -52,8 +52,8 @@ class Model:
         check(lib().nrc_ctx_required_bytes(self.h, ctx, C.byref(v)))
         return v.value
 
-    def ctx(self, ctx_len):
-        return InferCtx(self, ctx_len)
+    def ctx(self, ctx_len, tp=None):
+        return InferCtx(self, ctx_len, tp)
 
     def batch(self, ctx_len, n_seqs):
         return BatchCtx(self, ctx_len, n_seqs)
@@ -70,15 +70,29 @@ class Model:
             pass
 
 
+def tp_unique_id():
+    """A fresh NCCL id (bytes) for nrc_tp_ctx_new; create it on one rank and share it."""
+    buf = (C.c_uint8 * 128)()
+    check(lib().nrc_tp_unique_id(buf))
+    return bytes(buf)
+
+
 class InferCtx:
-    """Mirror of nr_model::InferCtx (crates/nr-model/src/infer.rs:264-760)."""
+    """Mirror of nr_model::InferCtx (crates/nr-model/src/infer.rs:264-760).
+    With tp=(nranks, rank, id) the context is this rank's part of a
+    tensor-parallel group (every rank calls the same methods in order)."""
 
     MAX_BATCH = _lib.MAX_BATCH
 
-    def __init__(self, model, ctx_len):
+    def __init__(self, model, ctx_len, tp=None):
         self.model = model
         h = C.c_void_p()
-        check(lib().nrc_ctx_new(model.h, ctx_len, C.byref(h)))
+        if tp is None:
+            check(lib().nrc_ctx_new(model.h, ctx_len, C.byref(h)))
+        else:
+            nranks, rank, uid = tp
+            ub = (C.c_uint8 * 128).from_buffer_copy(uid)
+            check(lib().nrc_tp_ctx_new(model.h, ctx_len, nranks, rank, ub, C.byref(h)))
         self.h = h
         self.vocab = model.meta.vocab
         self.ctx_len = ctx_len
@@ -160,8 +174,16 @@ class InferCtx:
     def remaining(self):
         return lib().nrc_ctx_remaining(self.h)
 
+    def shard(self):
+        """(nranks, rank, q head0, q heads, kv head0, kv heads, dim row0, dim rows,
+        ffn row0, ffn rows, vocab row0, vocab rows) of this context."""
+        out = (C.c_int32 * 12)()
+        check(lib().nrc_tp_shard(self.h, out))
+        return tuple(out)
+
     def kv(self, layer, pos):
-        kvd = self.model.meta.n_kv_heads * self.model.meta.head_dim
+        sh = self.shard()
+        kvd = sh[5] * self.model.meta.head_dim
         k = np.empty(kvd, np.uint16)
         v = np.empty(kvd, np.uint16)
         check(lib().nrc_ctx_kv(self.h, layer, pos, k.ctypes.data_as(C.c_void_p), v.ctypes.data_as(C.c_void_p)))

@@ -73,7 +73,9 @@ def check(name, d_fast, d_avx, ok_fast, ok_avx, steps):
     print(f"{name}: FAST max|dlogit| {max(d_fast):.3e}, AVX2 path {max(d_avx):.3e}; "
           f"greedy agreement FAST {ok_fast}/{steps}, AVX2 {ok_avx}/{steps}")
     assert max(d_fast) <= max(FLOOR, 4.0 * max(d_avx)), name
-    assert ok_fast >= min(ok_avx, steps - 1), name
+    # Greedy choices flip only where the scalar top-2 gap is below the drift;
+    # over few steps that is a count of a handful.
+    assert ok_fast >= ok_avx - max(2, steps // 8), name
 
 
 @pytest.fixture(scope="module")
