@@ -112,6 +112,53 @@ int matvec_common(int fmt, float* y, const void* w, const void* x, size_t rows, 
     }
     return NRC_OK;
   }
+  if (fmt != FMT_Q8_0 && batch > 8 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+    // Tensor-core path (tcgen05 kind::i8 per sub-block), one pass per NS x ntg tokens.
+    const int NS = mma_kq_ns(fmt);
+    const size_t nsb = cols / 256;
+    const size_t per = (size_t)NS * 4;  // tokens per pass: four token groups
+    for (size_t t0 = 0; t0 < batch; t0 += per) {
+      const int nt = (int)(batch - t0 < per ? batch - t0 : per);
+      const int ntg = (nt + NS - 1) / NS;
+      uint8_t* xq = nullptr;
+      float* xd = nullptr;
+      int* xb = nullptr;
+      if (cudaMallocAsync((void**)&xq, (size_t)ntg * NS * cols, S(stream)) != cudaSuccess)
+        return nrc_fail_api(NRC_ERR_ALLOC, "activation tile allocation failed");
+      if (cudaMallocAsync((void**)&xd, (size_t)ntg * NS * nsb * 4, S(stream)) != cudaSuccess) {
+        cudaFreeAsync(xq, S(stream));
+        return nrc_fail_api(NRC_ERR_ALLOC, "activation scale allocation failed");
+      }
+      if (cudaMallocAsync((void**)&xb, (size_t)ntg * NS * nsb * 32, S(stream)) != cudaSuccess) {
+        cudaFreeAsync(xq, S(stream));
+        cudaFreeAsync(xd, S(stream));
+        return nrc_fail_api(NRC_ERR_ALLOC, "activation sum allocation failed");
+      }
+      rc = cuda_rc(mma_kq_pack_run(static_cast<const uint8_t*>(x) + t0 * nsb * 292, nt, (int)cols, NS, ntg, xq, xd,
+                                   xb, S(stream)),
+                   "kq pack");
+      MmaKqArgs m{};
+      m.fmt = fmt;
+      m.seg[0] = MmaSeg{w, y + t0 * rows, (int)rows, (int)rows};
+      m.nseg = 1;
+      m.K = (int)cols;
+      m.xq = xq;
+      m.xd = xd;
+      m.xb = xb;
+      m.nt = nt;
+      m.NS = NS;
+      m.ntg = ntg;
+      m.epi = EPI_STORE;
+      m.scale = 1.0f;
+      m.err = sc.err;
+      if (!rc) rc = cuda_rc(mma_kq_run(m, S(stream), false), "kq launch");
+      cudaFreeAsync(xq, S(stream));
+      cudaFreeAsync(xd, S(stream));
+      cudaFreeAsync(xb, S(stream));
+      if (rc) return rc;
+    }
+    return NRC_OK;
+  }
   for (size_t t0 = 0; t0 < batch; t0 += 8) {
     GemvArgs a{};
     a.fmt = fmt;

@@ -502,7 +502,7 @@ int shard_for(const nrc_meta& mt, int n, int r, Shard* sh) {
 }
 
 struct Layout {
-  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, status, hist, samp, tps, tpr;
+  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, mxb, status, hist, samp, tps, tpr;
   // Several sequences: per-sequence positions / next input / last choice,
   // 0..S-1, the pass's per-token ids / positions / sequences, classifier
   // rows, gathered final rows, their logits, per-sequence token history.
@@ -544,6 +544,7 @@ Layout layout_for(const nrc_meta& mt, size_t ctx, size_t n_seqs = 1, bool batch 
   L.sin_t = take(ctx * (mt.head_dim / 2) * 4);
   L.mxq = take(BM * maxk);            // tensor-core activation tiles (prefill)
   L.mxd = take(BM * (maxk / 32) * 4);  // and their block scales
+  L.mxb = take(BM * (maxk / 256) * 8 * 4);  // and the chunk sums of the K-quant tiles
   L.status = take(sizeof(Status));
   L.hist = take((ctx + 1) * 4);
   L.samp = take(sample_scratch_bytes((int)mt.vocab));  // sampler candidates
@@ -622,6 +623,7 @@ struct nrc_ctx {
   float *x, *q, *k, *v, *att, *g, *u, *logits, *cos_t, *sin_t;
   uint8_t* mxq;  // tensor-core activation tiles (prefill)
   float* mxd;
+  int* mxb;
   Status* st;
   uint32_t* hist;
   uint32_t* h_stage = nullptr;  // pinned host staging: tokens in, status out
@@ -766,6 +768,7 @@ static int ctx_create(const nrc_model* m, size_t ctx, size_t n_seqs, bool batch,
   c->sin_t = reinterpret_cast<float*>(A + c->lay.sin_t);
   c->mxq = A + c->lay.mxq;
   c->mxd = reinterpret_cast<float*>(A + c->lay.mxd);
+  c->mxb = reinterpret_cast<int*>(A + c->lay.mxb);
   c->st = reinterpret_cast<Status*>(A + c->lay.status);
   c->hist = reinterpret_cast<uint32_t*>(A + c->lay.hist);
   c->samp = reinterpret_cast<unsigned long long*>(A + c->lay.samp);
@@ -912,6 +915,35 @@ void span2(const uint8_t* a, size_t na, const uint8_t* b, size_t nb, const uint8
 cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
   cudaStream_t s = c->stream;
   const bool pdl = c->pdl;
+  // K-quant chunks of more than 8 tokens: tensor cores (mma_kq.cu), one launch per matrix.
+  bool kq = nt > 8 && L.fmt != FMT_Q8_0 && L.K % 256 == 0 && (size_t)L.K * 4 <= 64 * 1024;
+  for (int i = 0; i < L.nseg; i++) kq = kq && (reinterpret_cast<uintptr_t>(L.w[i]) & 15) == 0;
+  if (kq) {
+    const int NS = mma_kq_ns(L.fmt), ntg = (nt + NS - 1) / NS;
+    MmaKqActArgs qa{L.x, L.K, L.norm_w, c->eps, nt, L.K, NS, ntg, c->mxq, c->mxd, c->mxb};
+    cudaError_t e = mma_kq_act_run(qa, s, pdl);
+    if (e) return e;
+    MmaKqArgs m{};
+    m.fmt = L.fmt;
+    for (int i = 0; i < L.nseg; i++) m.seg[i] = MmaSeg{L.w[i], L.y[i], L.rows[i], L.rows[i]};
+    m.nseg = L.nseg;
+    m.K = L.K;
+    m.xq = c->mxq;
+    m.xd = c->mxd;
+    m.xb = c->mxb;
+    m.nt = nt;
+    m.NS = NS;
+    m.ntg = ntg;
+    m.epi = L.epi == EPI_RESID ? EPI_RESID : EPI_STORE;
+    m.scale = L.scale;
+    m.resid = c->x;
+    m.resid_ld = c->dim;
+    m.rs = c->rs;
+    m.err = &c->st->err;
+    if ((e = mma_kq_run(m, s, pdl))) return e;
+    if (L.epi == EPI_SWIGLU) return op_swiglu(L.y[0], L.y[1], (size_t)nt * L.rows[0], s);
+    return cudaSuccess;
+  }
   bool mma = nt > 8 && L.fmt == FMT_Q8_0 && L.K % 256 == 0 && L.K <= 16384;
   for (int i = 0; i < L.nseg; i++) mma = mma && (reinterpret_cast<uintptr_t>(L.w[i]) & 15) == 0;
   if (mma) {

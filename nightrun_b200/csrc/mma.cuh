@@ -47,6 +47,43 @@ cudaError_t mma_q8_run(const MmaArgs& a, cudaStream_t s, bool pdl);
 // Pre-quantized Q8_0 activation blocks [nt][K/32] -> the canonical tiles above.
 cudaError_t mma_pack_q8_run(const uint8_t* x, int nt, int K, int NS, int ntg, uint8_t* xq, float* xd, cudaStream_t s);
 // Bytes of the canonical activation tiles and scales for nt tokens.
+// K-quant GEMM (mma_kq.cu): Q4_K or Q6_K weights x Q8_K activations. The
+// activations are quantize_q8k'd per token into canonical tiles of 32-value
+// chunks: xq[((tg * nsb + sb) * 8 + chunk) * NS * 32 ...], their block scales
+// xd[(tg * nsb + sb) * NS + n] and chunk sums xb[((tg * nsb + sb) * NS + n) * 8
+// + chunk] (nsb = K / 256). NS is mma_kq_ns(fmt): 64 for Q4_K, 32 for Q6_K.
+struct MmaKqActArgs {
+  const float* x;
+  int x_ld;
+  const float* norm_w;  // nullable
+  float eps;
+  int nt, K, NS, ntg;
+  uint8_t* xq;
+  float* xd;
+  int* xb;
+};
+cudaError_t mma_kq_act_run(const MmaKqActArgs& a, cudaStream_t s, bool pdl);
+cudaError_t mma_kq_pack_run(const uint8_t* x, int nt, int K, int NS, int ntg, uint8_t* xq, float* xd, int* xb,
+                            cudaStream_t s);
+struct MmaKqArgs {
+  int fmt;        // FMT_Q4K or FMT_Q6K
+  MmaSeg seg[3];  // weights: 16-byte aligned
+  int nseg;
+  int K;
+  const uint8_t* xq;
+  const float* xd;
+  const int* xb;
+  int nt, NS, ntg;
+  int epi;  // EPI_STORE or EPI_RESID
+  float scale;
+  float* resid;
+  int resid_ld;
+  float rs;
+  unsigned* err;
+};
+cudaError_t mma_kq_run(const MmaKqArgs& a, cudaStream_t s, bool pdl);
+int mma_kq_ns(int fmt);
+
 inline size_t mma_xq_bytes(int nt, int K) {
   const int NS = nt <= 16 ? 16 : (nt <= 32 ? 32 : 64);
   const int ntg = (nt + NS - 1) / NS;

@@ -1,0 +1,628 @@
+// Batched K-quant GEMM (Q4_K / Q6_K weights x Q8_K activations, 9+ tokens:
+// prefill chunks and multi-sequence decode) on sm_100a tensor cores:
+// tcgen05.mma kind::i8 with TMEM accumulators.
+//
+// Reference: kquant::matmul_q4k / matmul_q6k (crates/nr-tensor/src/kquant.rs:
+// 566-639) with the scalar dot order of dot_q4k_scalar / dot_q6k_scalar
+// (kquant.rs:192-250). Per (row, token, super-block):
+//   Q4_K: sum_q = sum over 32-value sub-blocks j of f32(sc_j) * f32(dot_j), in
+//         order; sum_m = sum_j m_j * (bsum_2j + bsum_2j+1) (integer);
+//         term = (d*dx) * sum_q - (dmin*dx) * f32(sum_m)
+//   Q6_K: sum = sum over 16-value groups g of f32(sc_g) * f32(dot_g), in order;
+//         term = (d*dx) * sum
+// and the row's terms are added over super-blocks in order. The tensor core
+// produces every dot exactly: one K=32 MMA per Q4_K sub-block, and for Q6_K
+// two per 32-value chunk whose A tiles keep one 16-value half each (the other
+// half zero), each into its own TMEM slot; the epilogue applies the scales
+// with the reference's roundings in the reference's order, so outputs are
+// bit-identical to the scalar path.
+//
+// CTA = 128 weight rows x NS tokens (Q4_K NS = 64, Q6_K NS = 32: one
+// super-block's slots fill the 512 TMEM columns), one super-block per stage,
+// 14 warps:
+//   warps 0-7   epilogue: TMEM lane quarter warp % 4 (rows), token half warp / 4;
+//   warps 8-11  repack: raw rows (bulk-copied) -> canonical int8 A tiles + row scales;
+//   warp 12     producer: 1-D bulk copies of the raw rows (16-byte aligned
+//               supersets; a matrix's ragged last bytes by plain loads), the
+//               activation tiles and their scales / bsums (no multicast);
+//   warp 13     TMEM allocator and single-thread MMA issuer.
+// Every mbarrier wait is bounded (error word + clean exit, never a trap).
+#include <algorithm>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "mma.cuh"
+#include "seqsum.cuh"
+#include "tcgen05.cuh"
+
+namespace nrc {
+namespace {
+
+constexpr int NST = 2;  // pipeline stages
+constexpr int KTHR = 448;
+constexpr int WREP = 8, WPROD = 12, WMMA = 13;
+constexpr int EPI_WARPS = 8, REP_WARPS = 4;
+constexpr int RAW_SLOT = 240;  // bytes per row per stage: a 16-byte aligned superset of one super-block
+
+struct KqParams {
+  const uint8_t* w[3];
+  float* yseg[3];
+  int rows[3];
+  int ldseg[3];
+  int tile_start[4];
+  int nseg;
+  int fmt, nsb, row_bytes;  // super-blocks per row
+  const uint8_t* xq;        // canonical activation tiles [ntg][nsb][8][NS x 32]
+  const float* xd;          // [ntg][nsb][NS]
+  const int* xb;            // [ntg][nsb][NS][8] sums of each 32-value chunk (Q4_K)
+  int nt, NS, ntg;
+  int epi;
+  float scale;
+  float* resid;
+  int resid_ld;
+  float rs;
+  unsigned* err;
+  // stage layout (bytes from the stage base)
+  int off_a, off_raw, off_b, off_rmeta, off_dx, off_xb, stage_bytes, off_bar;
+  uint32_t tmem_cols;
+};
+
+template <int FMT>
+constexpr int slots() { return FMT == FMT_Q4K ? 8 : 16; }
+template <int FMT>
+constexpr int tile_ns() { return FMT == FMT_Q4K ? 64 : 32; }
+
+template <int FMT>
+__global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqParams p) {
+  constexpr int NA = slots<FMT>();
+  constexpr int NS = tile_ns<FMT>();
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
+  uint64_t* full = bars;               // producer -> repack / epilogue (tx bytes)
+  uint64_t* aready = bars + NST;       // repack -> MMA (A tiles + row scales written)
+  uint64_t* empty = bars + 2 * NST;    // MMA commit + epilogue warps -> producer
+  uint64_t* mdone = bars + 3 * NST;    // MMA commit -> epilogue (the stage's slots written)
+  uint64_t* tfree = bars + 4 * NST;    // epilogue warps -> MMA (TMEM drained), one barrier
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x / p.ntg, tg = blockIdx.x % p.ntg;
+  int sg = 0;
+  while (sg + 1 < p.nseg && tile >= p.tile_start[sg + 1]) sg++;
+  const int row0 = (tile - p.tile_start[sg]) * TC_M;
+  const int nrows = min(TC_M, p.rows[sg] - row0);
+  const uint8_t* wseg = p.w[sg];
+  const uint8_t* wend = wseg + (size_t)p.rows[sg] * p.row_bytes;
+  const int nsb = p.nsb;
+  const int bpb = FMT == FMT_Q4K ? Q4K_BYTES : Q6K_BYTES;
+
+  if (tid == 0) {
+    for (int s = 0; s < NST; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&aready[s], REP_WARPS);
+      mbar_init(&empty[s], 1 + EPI_WARPS);
+      mbar_init(&mdone[s], 1);
+    }
+    mbar_init(tfree, EPI_WARPS);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == WMMA) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                 "r"(p.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_trigger();
+  pdl_wait();  // activations and the residual stream come from the previous kernel
+  const uint32_t tbase = tmem_base_sh;
+  auto st_base = [&](int s) { return smem + (size_t)s * p.stage_bytes; };
+  auto fail = [&](unsigned bit) {
+    if (!abort_flag) {
+      abort_flag = 1;
+      atomicOr(p.err, bit);
+    }
+  };
+
+  if (warp == WPROD) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol = l2_evict_first();
+    const uintptr_t wend_al = reinterpret_cast<uintptr_t>(wend) & ~(uintptr_t)15;
+    int st = 0;
+    for (; st < nsb; st++) {
+      const int s = st % NST, u = st / NST;
+      if (u >= 1) {
+        bool ok = true;
+        if (lane == 0) ok = mbar_wait(&empty[s], (u - 1) & 1);
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) fail(ERR_WAIT_EMPTY);
+      }
+      if (abort_flag) break;
+      uint8_t* raw = st_base(s) + p.off_raw;
+      // This lane's rows: bulk-copied bytes [lo, hi) of each; a ragged end past
+      // the matrix's last 16-byte boundary goes by plain loads.
+      uint32_t mine = 0;
+      for (int r = lane; r < nrows; r += 32) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
+        const uintptr_t lo = a & ~(uintptr_t)15;
+        uintptr_t hi = (a + bpb + 15) & ~(uintptr_t)15;
+        if (hi > wend_al) hi = wend_al > lo ? wend_al : lo;
+        mine += (uint32_t)(hi - lo);
+        for (uintptr_t b = hi > a ? hi : a; b < a + bpb; b++) raw[r * RAW_SLOT + (b - lo)] = *reinterpret_cast<const uint8_t*>(b);
+      }
+      uint32_t total = mine;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
+      const size_t tix = (size_t)tg * nsb + st;
+      const uint32_t b_bytes = 8u * NS * 32, dx_bytes = NS * 4u, xb_bytes = FMT == FMT_Q4K ? NS * 32u : 0u;
+      __syncwarp();  // every lane's plain byte stores before lane 0's release arrive
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], total + b_bytes + dx_bytes + xb_bytes);
+      __syncwarp();
+      for (int r = lane; r < nrows; r += 32) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
+        const uintptr_t lo = a & ~(uintptr_t)15;
+        uintptr_t hi = (a + bpb + 15) & ~(uintptr_t)15;
+        if (hi > wend_al) hi = wend_al > lo ? wend_al : lo;
+        if (hi > lo) bulk_g2s(raw + r * RAW_SLOT, reinterpret_cast<const void*>(lo), (uint32_t)(hi - lo), &full[s], pol);
+      }
+      if (lane == 0) {
+        bulk_g2s(st_base(s) + p.off_b, p.xq + tix * 8 * NS * 32, b_bytes, &full[s], 0ull);
+        bulk_g2s(st_base(s) + p.off_dx, p.xd + tix * NS, dx_bytes, &full[s], 0ull);
+        if (FMT == FMT_Q4K) bulk_g2s(st_base(s) + p.off_xb, p.xb + tix * NS * 8, xb_bytes, &full[s], 0ull);
+      }
+    }
+    if (lane == 0)
+      for (int k = st - 1; k >= 0 && k >= st - NST; k--)
+        if (!mbar_wait(&full[k % NST], (k / NST) & 1)) atomicOr(p.err, ERR_DRAIN);
+  } else if (warp >= WREP && warp < WREP + REP_WARPS) {
+    // -------------------------------------------------------------- repack
+    const int r = tid - WREP * 32;  // weight row of this thread
+    for (int st = 0; st < nsb; st++) {
+      const int s = st % NST, u = st / NST;
+      if (abort_flag || !mbar_wait(&full[s], u & 1)) {
+        fail(ERR_WAIT_FULL);
+        break;
+      }
+      uint8_t* a = st_base(s) + p.off_a;
+      uint8_t* rm = st_base(s) + p.off_rmeta;
+      if (r < nrows) {
+        const uintptr_t ga = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
+        const uint8_t* b = st_base(s) + p.off_raw + r * RAW_SLOT + (ga & 15);
+        if (FMT == FMT_Q4K) {
+          // d, dmin (f16), 12 scale bytes (q4k_scale_min, kquant.rs:83-92), 128 bytes of nibbles.
+          float* fm = reinterpret_cast<float*>(rm);
+          fm[r] = f16_to_f32((uint32_t)b[0] | ((uint32_t)b[1] << 8));
+          fm[TC_M + r] = f16_to_f32((uint32_t)b[2] | ((uint32_t)b[3] << 8));
+          uint8_t* scm = rm + 2 * TC_M * 4 + r * 16;  // sc[8], m[8]
+          const uint8_t* sb = b + 4;
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            if (j < 4) {
+              scm[j] = sb[j] & 63;
+              scm[8 + j] = sb[j + 4] & 63;
+            } else {
+              scm[j] = (sb[j + 4] & 0x0F) | ((sb[j - 4] >> 6) << 4);
+              scm[8 + j] = (sb[j + 4] >> 4) | ((sb[j] >> 6) << 4);
+            }
+          }
+          const uint8_t* qs = b + 16;
+#pragma unroll
+          for (int c = 0; c < 4; c++) {
+            uint32_t wv[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+              wv[k] = (uint32_t)qs[32 * c + 4 * k] | ((uint32_t)qs[32 * c + 4 * k + 1] << 8) |
+                      ((uint32_t)qs[32 * c + 4 * k + 2] << 16) | ((uint32_t)qs[32 * c + 4 * k + 3] << 24);
+            uint8_t* lo = a + (2 * c) * (TC_M * 32);
+            uint8_t* hi = a + (2 * c + 1) * (TC_M * 32);
+            *reinterpret_cast<uint4*>(lo + canon_off(r, 0)) =
+                make_uint4(wv[0] & 0x0F0F0F0Fu, wv[1] & 0x0F0F0F0Fu, wv[2] & 0x0F0F0F0Fu, wv[3] & 0x0F0F0F0Fu);
+            *reinterpret_cast<uint4*>(lo + canon_off(r, 1)) =
+                make_uint4(wv[4] & 0x0F0F0F0Fu, wv[5] & 0x0F0F0F0Fu, wv[6] & 0x0F0F0F0Fu, wv[7] & 0x0F0F0F0Fu);
+            *reinterpret_cast<uint4*>(hi + canon_off(r, 0)) = make_uint4(
+                (wv[0] >> 4) & 0x0F0F0F0Fu, (wv[1] >> 4) & 0x0F0F0F0Fu, (wv[2] >> 4) & 0x0F0F0F0Fu, (wv[3] >> 4) & 0x0F0F0F0Fu);
+            *reinterpret_cast<uint4*>(hi + canon_off(r, 1)) = make_uint4(
+                (wv[4] >> 4) & 0x0F0F0F0Fu, (wv[5] >> 4) & 0x0F0F0F0Fu, (wv[6] >> 4) & 0x0F0F0F0Fu, (wv[7] >> 4) & 0x0F0F0F0Fu);
+          }
+        } else {
+          // ql[128], qh[64], scales[16] (int8), d (f16): value v = q - 32 in natural order.
+          float* fm = reinterpret_cast<float*>(rm);
+          fm[r] = f16_to_f32((uint32_t)b[208] | ((uint32_t)b[209] << 8));
+          int8_t* scm = reinterpret_cast<int8_t*>(rm + TC_M * 4) + r * 16;
+#pragma unroll
+          for (int g = 0; g < 16; g++) scm[g] = (int8_t)b[192 + g];
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            const uint8_t* ql = b + 64 * h;
+            const uint8_t* qh = b + 128 + 32 * h;
+#pragma unroll
+            for (int qd = 0; qd < 4; qd++) {  // quarter: values 128h + 32qd + l, chunk 4h + qd
+              uint32_t wv[8];
+#pragma unroll
+              for (int k = 0; k < 8; k++) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                  const int l = 4 * k + e;
+                  const uint32_t lq = qd & 1 ? ql[l + 32] : ql[l];
+                  const uint32_t q = ((qd < 2 ? (lq & 0x0F) : (lq >> 4)) | (((qh[l] >> (2 * qd)) & 3) << 4));
+                  word |= (uint32_t)(uint8_t)(int8_t)((int)q - 32) << (8 * e);
+                }
+                wv[k] = word;
+              }
+              const int c = 4 * h + qd;  // 32-value chunk
+              uint8_t* g0 = a + (2 * c) * (TC_M * 32);      // group 2c: values 0..15 of the chunk
+              uint8_t* g1 = a + (2 * c + 1) * (TC_M * 32);  // group 2c + 1: values 16..31
+              *reinterpret_cast<uint4*>(g0 + canon_off(r, 0)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+              *reinterpret_cast<uint4*>(g0 + canon_off(r, 1)) = make_uint4(0, 0, 0, 0);
+              *reinterpret_cast<uint4*>(g1 + canon_off(r, 0)) = make_uint4(0, 0, 0, 0);
+              *reinterpret_cast<uint4*>(g1 + canon_off(r, 1)) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int k = 0; k < NA; k++) {
+          *reinterpret_cast<uint4*>(a + k * (TC_M * 32) + canon_off(r, 0)) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(a + k * (TC_M * 32) + canon_off(r, 1)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&aready[s]);
+    }
+  } else if (warp == WMMA) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_i8(NS);
+      int issued = -1;  // last super-block whose MMAs were issued
+      for (int st = 0; st < nsb && !abort_flag; st++) {
+        const int s = st % NST, u = st / NST;
+        if (!mbar_wait(&aready[s], u & 1)) {
+          fail(ERR_WAIT_FULL);
+          break;
+        }
+        // Every slot of the previous super-block drained by the epilogue.
+        if (st >= 1 && !mbar_wait(tfree, (st - 1) & 1)) {
+          fail(ERR_WAIT_EMPTY);
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* a = st_base(s) + p.off_a;
+        const uint8_t* bt = st_base(s) + p.off_b;
+#pragma unroll 1
+        for (int k = 0; k < NA; k++) {
+          const int chunk = FMT == FMT_Q4K ? k : k / 2;
+          const uint64_t ad = smem_desc(a + k * (TC_M * 32), 128, 256);
+          const uint64_t bd = smem_desc(bt + chunk * (NS * 32), 128, 256);
+          tc_mma_i8(tbase + (uint32_t)(k * NS), ad, bd, idesc, 0u);
+        }
+        tc_commit(&mdone[s]);
+        tc_commit(&empty[s]);
+        issued = st;
+      }
+      // Never release TMEM with an MMA in flight: wait (bounded) for the last commit.
+      if (issued >= 0 && !mbar_wait(&mdone[issued % NST], (issued / NST) & 1)) atomicOr(p.err, ERR_DRAIN);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3, half = warp >> 2;
+    const int r = q * 32 + lane;          // TMEM lane = weight row
+    constexpr int NH = NS / 2;            // tokens of this warp
+    const int n0 = half * NH;
+    float acc[NH];
+#pragma unroll
+    for (int i = 0; i < NH; i++) acc[i] = 0.0f;
+    const uint32_t lane_base = tbase + ((uint32_t)(q * 32) << 16);
+    for (int st = 0; st < nsb && !abort_flag; st++) {
+      const int s = st % NST, u = st / NST;
+      if (!mbar_wait(&mdone[s], u & 1)) {
+        fail(ERR_WAIT_FULL);
+        break;
+      }
+      tc_fence_after();
+      const uint8_t* rm = st_base(s) + p.off_rmeta;
+      const float* dxs = reinterpret_cast<const float*>(st_base(s) + p.off_dx);
+      float scf[NA];
+      float d = 0.0f, dmin = 0.0f;
+      int mj[8];
+      if (FMT == FMT_Q4K) {
+        const float* fm = reinterpret_cast<const float*>(rm);
+        d = fm[r];
+        dmin = fm[TC_M + r];
+        const uint8_t* scm = rm + 2 * TC_M * 4 + r * 16;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          scf[j] = (float)scm[j];
+          mj[j] = scm[8 + j];
+        }
+      } else {
+        d = reinterpret_cast<const float*>(rm)[r];
+        const int8_t* scm = reinterpret_cast<const int8_t*>(rm + TC_M * 4) + r * 16;
+#pragma unroll
+        for (int g = 0; g < NA; g++) scf[g] = (float)scm[g];
+      }
+      const int* xbs = reinterpret_cast<const int*>(st_base(s) + p.off_xb);
+#pragma unroll
+      for (int c0 = 0; c0 < NH; c0 += 16) {
+        float sq[16];
+#pragma unroll
+        for (int i = 0; i < 16; i++) sq[i] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NA; k++) {
+          uint32_t v[16];
+          tc_ld16(lane_base + (uint32_t)(k * NS + n0 + c0), v);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; i++) sq[i] = __fadd_rn(sq[i], __fmul_rn(scf[k], i2f((int)v[i])));
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const int n = n0 + c0 + i;
+          const float dx = dxs[n];
+          float t;
+          if (FMT == FMT_Q4K) {
+            int sm = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) sm += mj[j] * xbs[n * 8 + j];
+            t = __fsub_rn(__fmul_rn(__fmul_rn(d, dx), sq[i]), __fmul_rn(__fmul_rn(dmin, dx), i2f(sm)));
+          } else {
+            t = __fmul_rn(__fmul_rn(d, dx), sq[i]);
+          }
+          acc[c0 + i] = __fadd_rn(acc[c0 + i], t);
+        }
+      }
+      // Slots and the stage's scales consumed.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(tfree);
+        mbar_arrive(&empty[s]);
+      }
+    }
+    if (!abort_flag && r < nrows) {
+      const int row = row0 + r;
+#pragma unroll
+      for (int i = 0; i < NH; i++) {
+        const int tok = tg * NS + n0 + i;
+        if (tok >= p.nt) break;
+        float sv = acc[i];
+        if (p.epi == EPI_RESID) {
+          float* dst = p.resid + (size_t)tok * p.resid_ld + row;
+          *dst = __fadd_rn(*dst, __fmul_rn(p.rs, sv));
+        } else {
+          if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
+          p.yseg[sg][(size_t)tok * p.ldseg[sg] + row] = sv;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == WMMA) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(p.tmem_cols) : "memory");
+  }
+}
+
+// Activations of the K-quant GEMM: one CTA (256 threads) per token slot:
+// optional exact RMSNorm (the GEMV prologue's order), then quantize_q8k
+// (kquant.rs:157-187) of every 256-value block, one warp per block, into the
+// canonical tiles of 32-value chunks, the block scale and the chunk sums.
+__global__ void __launch_bounds__(256) k_mma_kq_act(const MmaKqActArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int n = blockIdx.x;  // token slot (0 .. ntg*NS - 1)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nsb = a.K / 256;
+  const int tg = n / a.NS, nn = n % a.NS;
+  __shared__ SeqSumShared ssh;
+  auto tile = [&](int sb, int c) { return a.xq + (((size_t)tg * nsb + sb) * 8 + c) * a.NS * 32; };
+  if (n >= a.nt) {
+    for (int i = tid; i < nsb * 8; i += 256) {
+      uint8_t* t = tile(i / 8, i % 8);
+      *reinterpret_cast<uint4*>(t + canon_off(nn, 0)) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(t + canon_off(nn, 1)) = make_uint4(0, 0, 0, 0);
+      a.xb[(((size_t)tg * nsb + i / 8) * a.NS + nn) * 8 + i % 8] = 0;
+    }
+    for (int sb = tid; sb < nsb; sb += 256) a.xd[((size_t)tg * nsb + sb) * a.NS + nn] = 0.0f;
+    return;
+  }
+  extern __shared__ __align__(16) float xrow[];  // the token's K values
+  const float* x = a.x + (size_t)n * a.x_ld;
+  for (int i = tid; i < a.K; i += 256) xrow[i] = x[i];
+  __syncthreads();
+  float sc = 1.0f;
+  if (a.norm_w) {
+    // vec::rmsnorm (vec.rs:4-14): `ss += v * v` in index order (one chain, seqsum.cuh).
+    const float ss = seq_sum_squares_group<256>(xrow, a.K, ssh, tid, [] { __syncthreads(); });
+    sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.eps)));
+  }
+  for (int b = warp; b < nsb; b += 8) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      v[k] = xrow[b * 256 + lane * 8 + k];
+      if (a.norm_w) v[k] = __fmul_rn(__fmul_rn(v[k], sc), a.norm_w[b * 256 + lane * 8 + k]);
+    }
+    // First strict maximum of |v| in index order (kquant.rs:160-167).
+    float amax = 0.0f, mx = 0.0f;
+    int idx = 0x7fffffff;
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      if (fabsf(v[k]) > amax) {
+        amax = fabsf(v[k]);
+        mx = v[k];
+        idx = lane * 8 + k;
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float a2 = __shfl_xor_sync(0xffffffffu, amax, o);
+      const float m2 = __shfl_xor_sync(0xffffffffu, mx, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (a2 > amax || (a2 == amax && i2 < idx)) {
+        amax = a2;
+        mx = m2;
+        idx = i2;
+      }
+    }
+    uint32_t pk[2] = {0u, 0u};
+    int part = 0;
+    float dval = 0.0f;
+    if (amax != 0.0f) {
+      const float iscale = __fdiv_rn(-128.0f, mx);
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const float z = __fmul_rn(iscale, v[k]);
+        int q = z >= 0.0f ? rust_f2i(__fadd_rn(z, 0.5f)) : rust_f2i(__fsub_rn(z, 0.5f));
+        q = q > 127 ? 127 : q;
+        const int8_t q8 = (int8_t)(uint8_t)(q & 0xff);
+        part += q8;
+        pk[k / 4] |= ((uint32_t)(uint8_t)q8) << (8 * (k % 4));
+      }
+      dval = __fdiv_rn(1.0f, iscale);
+    }
+    // Lane holds values 8*lane .. +7 of the block: chunk lane / 4, bytes 8*(lane % 4).
+    uint8_t* t = tile(b, lane / 4);
+    const int byte = 8 * (lane % 4);
+    *reinterpret_cast<uint2*>(t + canon_off(nn, byte / 16) + byte % 16) = make_uint2(pk[0], pk[1]);
+    int s4 = part + __shfl_down_sync(0xffffffffu, part, 1);
+    s4 += __shfl_down_sync(0xffffffffu, s4, 2);
+    if ((lane & 3) == 0) a.xb[(((size_t)tg * nsb + b) * a.NS + nn) * 8 + lane / 4] = s4;
+    if (lane == 0) a.xd[((size_t)tg * nsb + b) * a.NS + nn] = dval;
+  }
+}
+
+// Pre-quantized Q8_K activation blocks [nt][nsb] (292 bytes: d f32, 256 int8,
+// 16 int16 bsums; kquant.rs:46-52) -> the canonical tiles, scales and chunk sums.
+__global__ void k_mma_kq_pack(const uint8_t* __restrict__ x, int nt, int nsb, int NS, int ntg, uint8_t* xq,
+                              float* xd, int* xb) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;  // (token slot, block, chunk)
+  if (i >= NS * ntg * nsb * 8) return;
+  const int c = i % 8, b = (i / 8) % nsb, n = i / (8 * nsb);
+  const int tg = n / NS, nn = n % NS;
+  uint8_t* t = xq + (((size_t)tg * nsb + b) * 8 + c) * NS * 32;
+  uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  int pair = 0;
+  float d = 0.0f;
+  if (n < nt) {
+    const uint8_t* s = x + ((size_t)n * nsb + b) * Q8K_BYTES;
+#pragma unroll
+    for (int k = 0; k < 8; k++)
+      w[k] = (uint32_t)s[4 + 32 * c + 4 * k] | ((uint32_t)s[5 + 32 * c + 4 * k] << 8) |
+             ((uint32_t)s[6 + 32 * c + 4 * k] << 16) | ((uint32_t)s[7 + 32 * c + 4 * k] << 24);
+    const int16_t b0 = (int16_t)((uint32_t)s[260 + 4 * c] | ((uint32_t)s[261 + 4 * c] << 8));
+    const int16_t b1 = (int16_t)((uint32_t)s[262 + 4 * c] | ((uint32_t)s[263 + 4 * c] << 8));
+    pair = (int)b0 + (int)b1;
+    uint32_t db = (uint32_t)s[0] | ((uint32_t)s[1] << 8) | ((uint32_t)s[2] << 16) | ((uint32_t)s[3] << 24);
+    d = __uint_as_float(db);
+  }
+  *reinterpret_cast<uint4*>(t + canon_off(nn, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+  *reinterpret_cast<uint4*>(t + canon_off(nn, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+  xb[(((size_t)tg * nsb + b) * NS + nn) * 8 + c] = pair;
+  if (c == 0) xd[((size_t)tg * nsb + b) * NS + nn] = d;
+}
+
+cudaError_t launch_kq(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, void** args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace
+
+int mma_kq_ns(int fmt) { return fmt == FMT_Q4K ? 64 : 32; }
+
+cudaError_t mma_kq_act_run(const MmaKqActArgs& a, cudaStream_t s, bool pdl) {
+  if (a.K % 256 || (a.NS != 32 && a.NS != 64) || a.nt > a.NS * a.ntg) return cudaErrorInvalidValue;
+  if ((size_t)a.K * 4 > 64 * 1024) return cudaErrorInvalidValue;
+  if (cudaError_t e = ensure_smem_attr((const void*)k_mma_kq_act, 64 * 1024)) return e;
+  MmaKqActArgs aa = a;
+  void* args[] = {&aa};
+  return launch_kq((const void*)k_mma_kq_act, dim3(a.NS * a.ntg), dim3(256), (size_t)a.K * 4, s, pdl, args);
+}
+
+cudaError_t mma_kq_pack_run(const uint8_t* x, int nt, int K, int NS, int ntg, uint8_t* xq, float* xd, int* xb,
+                            cudaStream_t s) {
+  if (K % 256 || nt > NS * ntg) return cudaErrorInvalidValue;
+  const int nsb = K / 256;
+  const int total = NS * ntg * nsb * 8;
+  k_mma_kq_pack<<<(total + 255) / 256, 256, 0, s>>>(x, nt, nsb, NS, ntg, xq, xd, xb);
+  return cudaGetLastError();
+}
+
+cudaError_t mma_kq_run(const MmaKqArgs& a, cudaStream_t s, bool pdl) {
+  if ((a.fmt != FMT_Q4K && a.fmt != FMT_Q6K) || a.K % 256 || a.NS != mma_kq_ns(a.fmt) || a.nseg < 1 || a.nseg > 3)
+    return cudaErrorInvalidValue;
+  KqParams p{};
+  int tiles = 0;
+  for (int i = 0; i < a.nseg; i++) {
+    // 16-byte aligned matrices: a row's aligned superset never starts before the matrix.
+    if (reinterpret_cast<uintptr_t>(a.seg[i].w) & 15) return cudaErrorInvalidValue;
+    p.w[i] = static_cast<const uint8_t*>(a.seg[i].w);
+    p.yseg[i] = a.seg[i].y;
+    p.rows[i] = a.seg[i].rows;
+    p.ldseg[i] = a.seg[i].ld > 0 ? a.seg[i].ld : a.seg[i].rows;
+    p.tile_start[i] = tiles;
+    tiles += (a.seg[i].rows + TC_M - 1) / TC_M;
+  }
+  p.tile_start[a.nseg] = tiles;
+  p.nseg = a.nseg;
+  p.fmt = a.fmt;
+  p.nsb = a.K / 256;
+  p.row_bytes = p.nsb * (a.fmt == FMT_Q4K ? Q4K_BYTES : Q6K_BYTES);
+  p.xq = a.xq;
+  p.xd = a.xd;
+  p.xb = a.xb;
+  p.nt = a.nt;
+  p.NS = a.NS;
+  p.ntg = a.ntg;
+  p.epi = a.epi;
+  p.scale = a.scale;
+  p.resid = a.resid;
+  p.resid_ld = a.resid_ld;
+  p.rs = a.rs;
+  p.err = a.err;
+  const int na = a.fmt == FMT_Q4K ? 8 : 16;
+  // Stage layout: A tiles (1024-aligned) | raw rows | B tiles | row scales | dx | chunk sums.
+  size_t o = 0;
+  p.off_a = (int)o;
+  o += (size_t)na * TC_M * 32;
+  p.off_raw = (int)o;
+  o += (size_t)TC_M * RAW_SLOT;
+  o = (o + 127) & ~(size_t)127;
+  p.off_b = (int)o;
+  o += (size_t)8 * a.NS * 32;
+  p.off_rmeta = (int)o;
+  o += a.fmt == FMT_Q4K ? (size_t)TC_M * (8 + 16) : (size_t)TC_M * (4 + 16);
+  o = (o + 15) & ~(size_t)15;
+  p.off_dx = (int)o;
+  o += (size_t)a.NS * 4;
+  p.off_xb = (int)o;
+  if (a.fmt == FMT_Q4K) o += (size_t)a.NS * 32;
+  o = (o + 1023) & ~(size_t)1023;
+  p.stage_bytes = (int)o;
+  p.off_bar = (int)(o * NST);
+  const size_t smem = o * NST + (4 * NST + 1) * 8;
+  p.tmem_cols = 512;
+  const void* fn = a.fmt == FMT_Q4K ? (const void*)k_mma_kq<FMT_Q4K> : (const void*)k_mma_kq<FMT_Q6K>;
+  if (smem > 225 * 1024) return cudaErrorInvalidValue;
+  if (cudaError_t e = ensure_smem_attr(fn, 225 * 1024)) return e;
+  if (tiles == 0) return cudaSuccess;
+  void* args[] = {&p};
+  return launch_kq(fn, dim3(tiles * a.ntg), dim3(KTHR), smem, s, pdl, args);
+}
+
+}  // namespace nrc

@@ -1,0 +1,48 @@
+// tcgen05 (5th-generation tensor core) building blocks shared by the GEMM
+// kernels: MMA issue and commit, TMEM loads, shared-memory descriptors of the
+// UMMA K-major canonical layout (no swizzle) and the int8 instruction
+// descriptor with M = 128.
+#pragma once
+#include "common.cuh"
+
+namespace nrc {
+
+constexpr int TC_M = 128;  // rows per MMA tile
+
+NRC_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+NRC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+NRC_DEV void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+NRC_DEV void tc_mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+NRC_DEV void tc_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+NRC_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// UMMA shared-memory descriptor, K-major, no swizzle: 8x16-byte core matrices,
+// `lbo` = byte distance between the two 16-byte K halves, `sbo` = between
+// consecutive 8-row groups; version 1 (sm_100).
+NRC_DEV uint64_t smem_desc(const void* p, uint32_t lbo, uint32_t sbo) {
+  const uint64_t a = (smem_u32(p) >> 4) & 0x3FFFu;
+  return a | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) | ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46);
+}
+// Instruction descriptor: D s32, A/B signed int8, both K-major, N = ns, M = 128.
+NRC_DEV uint32_t idesc_i8(int ns) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(ns >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+}
+NRC_DEV uint32_t canon_off(int r, int c) { return (uint32_t)((r & 7) * 16 + (r >> 3) * 256 + c * 128); }
+
+}  // namespace nrc
