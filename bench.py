@@ -7,10 +7,15 @@ the timed steps sit at positions 64+W .. 64+W+K-1.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Prints ONE JSON line (rank 0). `value` is device-resident throughput (graph
-replays, CUDA events on the library's stream, max over ranks); `e2e` goes
-through the public API with host buffers every step (token H2D, logits D2H).
-N > 1 runs independent sequences per GPU (data parallel, weak scaling).
+Prints ONE JSON line (rank 0). `value` is device-resident throughput of the
+exact mode (bit-identical to the reference's scalar kernels; graph replays,
+CUDA events on the library's stream, max over ranks); `e2e` goes through the
+public API with host buffers every step (token H2D, logits D2H). `modes`
+adds the tolerance mode. N > 1 runs the same single sequence tensor-parallel
+over N GPUs (NCCL all-gathers, bit-identical to one GPU: strong scaling).
+At N = 1 the line also carries the other configurations (config 2/3 decode,
+config 4 batched decode of 256 sequences, a config-1 GEMV sweep) and the
+reference's CPU path timed on this host.
 `--impl reference` times the CPU restatement of the reference's AVX2 path.
 """
 import argparse
@@ -35,14 +40,25 @@ PROMPT = 64
 PUBLISHED_TOKS = 21.7
 WORKLOAD = ("config0: Llama-3.2-1B architecture, all linear weights Q8_0, random-init synthetic weights; "
             "64-token seed-uniform prompt, then greedy decode at b=1")
+BPE = {"q8_0": 34 / 32, "q4k": 144 / 256, "q6k": 210 / 256}
 
 
 def model_bytes(cfg):
     """Algorithmic bytes per decode token: packed weights read once + KV read at mean position."""
     dim, L, ffn, vocab = cfg["dim"], cfg["n_layers"], cfg["ffn_dim"], cfg["vocab"]
     att, kv = cfg["n_heads"] * cfg["head_dim"], cfg["n_kv_heads"] * cfg["head_dim"]
-    per_layer = dim * att + 2 * dim * kv + att * dim + 3 * dim * ffn
-    w = (per_layer * L + vocab * dim) * 34 // 32
+    if cfg["quant"] == 0:
+        per_layer = dim * att + 2 * dim * kv + att * dim + 3 * dim * ffn
+        w = (per_layer * L + vocab * dim) * 34 // 32
+    else:  # Q4_K_M-style mix: Q6_K for embed/output, attn_v and ffn_down of even layers
+        q4, q6 = BPE["q4k"], BPE["q6k"]
+        w = 0.0
+        for layer in range(L):
+            even = layer % 2 == 0
+            w += (dim * att + dim * kv + att * dim + 2 * dim * ffn) * q4
+            w += dim * kv * (q6 if even else q4) + ffn * dim * (q6 if even else q4)
+        w += vocab * dim * q6
+        w = int(w)
     norms = (2 * L + 1) * dim * 4
     return w + norms, L * 2 * kv * 2  # weight bytes, KV bytes per position
 
@@ -54,6 +70,16 @@ def peaks():
             d = json.load(f)
         return d.get("hbm_gbs", 6650.0), "measured"
     return 6650.0, "fallback"
+
+
+def profile_summary():
+    """Per-kernel figures from the committed ncu summaries (launch shares,
+    DRAM traffic per launch), or {} when none is present."""
+    p = os.path.join(ROOT, "profiles", "summary.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f)
+    return {}
 
 
 class ClockSampler:
@@ -108,9 +134,13 @@ class ClockSampler:
                 "samples": len(sm), "samples_under_load": len(loaded)}
 
 
-def launches_per_step(cfg):
-    # embed + per layer (QKV, attention with RoPE/KV append fused, wo, gate/up, down) + classifier + finish
-    return 1 + cfg["n_layers"] * 5 + 2
+def launches_per_step(cfg, world=1):
+    # embed + per layer (QKV, attention with RoPE/KV append fused, wo, gate/up, down) + classifier + finish;
+    # tensor parallelism adds 3 unpack launches per layer and 1 after the classifier.
+    n = 1 + cfg["n_layers"] * 5 + 2
+    if world > 1:
+        n += cfg["n_layers"] * 3 + 1
+    return n
 
 
 def cpu_decode(blob, cfg, steps, warmup, threads):
@@ -144,7 +174,8 @@ def run_reference(args, rank, world):
               f"timed decode tokens on {threads} host threads (C++ restatement of the reference AVX2 path)")
     line = {"impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * dt / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": tps / PUBLISHED_TOKS,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": tps / PUBLISHED_TOKS,
             "dtype": "q8_0 (i8 dot, f32)", "data": "synthetic (seeded random-init weights, seed-uniform prompt)",
             "config": {"workload": WORKLOAD, "prompt": PROMPT, "batch": 1},
             "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
@@ -152,39 +183,115 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) of one classifier-shape launch, from the ncu capture
-# in profiles/gemv_lr_q8_0_classifier_128256x2048_n1.md (same command shape).
-CLASSIFIER_TRAFFIC = 282_699_520
-
-
-def gemv_roofline(torch, K, rows, cols, reps, stream):
-    """Standalone Q8_0 GEMV on the classifier shape (the largest decode launch)."""
-    from nightrun_b200 import kernels
+def synth_q8_weights(torch, rows, cols, seed):
     nb = rows * cols // 32
-    g = torch.Generator(device="cuda").manual_seed(1)
+    g = torch.Generator(device="cuda").manual_seed(seed)
     w = torch.randint(-127, 128, (nb, 34), dtype=torch.int16, device="cuda", generator=g).to(torch.int8)
     w = w.view(torch.uint8)
     w[:, 0] = 0x00
     w[:, 1] = 0x20  # f16 scale 2^-7
-    w = w.contiguous().view(-1)
+    return w.contiguous().view(-1)
+
+
+def gemv_roofline(torch, rows, cols, reps, stream):
+    """Standalone Q8_0 GEMV (one token) on an in-step shape: algorithmic bytes
+    per launch and the average launch time (CUDA events on the launching stream)."""
+    from nightrun_b200 import kernels
+    w = synth_q8_weights(torch, rows, cols, rows + cols)
     x = torch.randn(cols, device="cuda")
     xq = torch.empty(cols // 32 * 34, dtype=torch.uint8, device="cuda")
     y = torch.empty(rows, device="cuda")
     kernels.quantize(x, xq, stream=stream)
-    for _ in range(3):
-        kernels.matvec_q8(y, w, xq, rows, cols, stream=stream)
+    # Rotate over copies larger than L2 (126 MB) so every launch streams from HBM.
+    copies = [w] + [w.clone() for _ in range(max(0, (160 << 20) // w.numel()))]
+    for i in range(3):
+        kernels.matvec_q8(y, copies[i % len(copies)], xq, rows, cols, stream=stream)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     ev0.record(stream)
-    for _ in range(reps):
-        kernels.matvec_q8(y, w, xq, rows, cols, stream=stream)
+    for i in range(reps):
+        kernels.matvec_q8(y, copies[i % len(copies)], xq, rows, cols, stream=stream)
     ev1.record(stream)
     ev1.synchronize()
     kernels.sync_check(stream)
     ms = ev0.elapsed_time(ev1) / reps
-    nbytes = nb * 34 + cols // 32 * 34 + rows * 4
-    del w
+    nbytes = rows * cols // 32 * 34 + cols // 32 * 34 + rows * 4
+    del copies, w
     return nbytes, ms
+
+
+def decode_rate(torch, model, steps, mode, ctx_len=256, prompt=PROMPT):
+    """Device-resident greedy decode tokens/s of one context (graph replays)."""
+    cfg_vocab = model.meta.vocab
+    c = model.ctx(ctx_len)
+    c.set_mode(mode)
+    stream = torch.cuda.ExternalStream(c.stream_handle())
+    c.prefill(np.array(prompt_ids(prompt, cfg_vocab), np.uint32))
+    c.decode_async(3)
+    c.sync()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    c.decode_async(steps)
+    e1.record(stream)
+    c.sync()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    c.close()
+    return 1000.0 / ms, ms
+
+
+def other_configs(torch, hbm):
+    """Configs 2/3 decode (both modes), config 4 batched decode and prefill of
+    256 sequences, the config-1 Q8_0 GEMV shapes."""
+    from nightrun_b200 import Model
+    out = {}
+    for key, name in (("config2", "llama3b_q4km"), ("config3", "qwen3_4b_q4km")):
+        cfg = CONFIGS[name]
+        m = Model.synth(cfg, MODEL_SEED)
+        ex, ms = decode_rate(torch, m, 24, 0)
+        fa, _ = decode_rate(torch, m, 24, 1)
+        wb, kvb = model_bytes(cfg)
+        gbs = (wb + kvb * (PROMPT + 14)) * ex / 1e9
+        out[key] = {"model": name, "decode_tokens_per_s": ex, "decode_tokens_per_s_fast": fa, "ms_per_token": ms,
+                    "step_gbs": gbs, "step_frac_of_hbm": gbs / hbm}
+        m.close()
+    cfg = CONFIGS["granite3b_q4km"]
+    m = Model.synth(cfg, MODEL_SEED)
+    S = 256
+    b = m.batch(128 + 24, S)
+    prompts = [prompt_ids(128, cfg["vocab"], seed=MODEL_SEED + 11 + i) for i in range(S)]
+    stream = torch.cuda.ExternalStream(b.stream_handle())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    b.prefill(prompts)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    pre_ms = e0.elapsed_time(e1)
+    b.decode_async(3)
+    b.sync()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    b.decode_async(16)
+    e1.record(stream)
+    b.sync()
+    torch.cuda.synchronize()
+    step_ms = e0.elapsed_time(e1) / 16
+    wb, kvb = model_bytes(cfg)
+    step_bytes = wb + kvb * S * (128 + 11)
+    out["config4"] = {"model": "granite3b_q4km", "sequences": S, "decode_tokens_per_s": S * 1000.0 / step_ms,
+                      "ms_per_step": step_ms, "prefill_tokens_per_s": S * 128 * 1000.0 / pre_ms,
+                      "step_gbs": step_bytes / step_ms / 1e6, "step_frac_of_hbm": step_bytes / step_ms / 1e6 / hbm}
+    b.close()
+    m.close()
+    sweep = {}
+    gs = torch.cuda.Stream()
+    for rows, cols in ((2048, 2048), (8192, 2048), (2048, 8192), (128256, 2048), (9728, 2560)):
+        nb, ms = gemv_roofline(torch, rows, cols, 20, gs)
+        sweep[f"{rows}x{cols}"] = {"us": ms * 1000.0, "gbs": nb / ms / 1e6, "frac": nb / ms / 1e6 / hbm}
+    out["config1_q8_0_n1"] = sweep
+    return out
 
 
 def max_over_ranks_of(v, world, device):
@@ -199,10 +306,10 @@ def max_over_ranks_of(v, world, device):
     return float(t.item())
 
 
-def job_tokens_per_s(ms_max, steps, world):
-    """Whole-job throughput of `world` independent replicas that each decoded
-    `steps` tokens, timed by the slowest rank."""
-    return world * steps / (ms_max / 1000.0)
+def job_tokens_per_s(ms_max, tokens):
+    """Whole-job throughput: the tokens of the job (one tensor-parallel sequence:
+    every rank serves the same tokens) over the slowest rank's time."""
+    return tokens / (ms_max / 1000.0)
 
 
 def run_ours(args, rank, world, local_rank):
@@ -213,12 +320,20 @@ def run_ours(args, rank, world, local_rank):
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    import nightrun_b200 as NB
     from nightrun_b200 import Model
     cfg = CONFIGS[CFG_NAME]
     W, Kst = args.warmup, args.steps
     sampler = ClockSampler(local_rank)
     model = Model.synth(cfg, MODEL_SEED, device=local_rank)
-    ctx = model.ctx(PROMPT + W + Kst + 8)
+    tp = None
+    if world > 1:
+        uid = [NB.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        tp = (world, rank, uid[0])
+    mode = 1 if args.mode == "fast" else 0
+    ctx = model.ctx(PROMPT + 2 * (W + Kst) + 16, tp=tp)
+    ctx.set_mode(mode)
     stream = torch.cuda.ExternalStream(ctx.stream_handle())
     prompt = np.array(prompt_ids(PROMPT, cfg["vocab"]), np.uint32)
 
@@ -244,7 +359,7 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
-    value = job_tokens_per_s(ms, Kst, world)
+    value = job_tokens_per_s(ms, Kst)
 
     # ---- end to end through the public API: host token in, host logits out, every step
     ctx.reset()
@@ -269,51 +384,72 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    e2e_value = job_tokens_per_s(e2e_ms, Kst, world)
+    e2e_value = job_tokens_per_s(e2e_ms, Kst)
+    ctx.close()
 
-    # ---- dominant kernel: Q8_0 GEMV on the classifier shape (vocab x dim)
-    gstream = torch.cuda.Stream()
-    gbytes, gms = gemv_roofline(torch, None, vocab, cfg["dim"], 20, gstream)
-    clocks = sampler.stop()
     hbm, hbm_kind = peaks()
-    achieved = gbytes / (gms / 1000.0) / 1e9
     wbytes, kv_per_pos = model_bytes(cfg)
     mean_pos = PROMPT + W + Kst / 2.0
     step_bytes = wbytes + kv_per_pos * mean_pos
-    step_gbs = step_bytes * (value / world) / 1e9
-
+    step_gbs = step_bytes * value / 1e9
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": Kst, "warmup": W,
-            "ms_per_step": ms / Kst, "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": ms / Kst, "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": value / PUBLISHED_TOKS, "dtype": "q8_0 (i8 dot, f32)",
             "data": "synthetic (seeded random-init weights, seed-uniform prompt)",
             "config": {"workload": WORKLOAD, "prompt": PROMPT, "batch": 1,
-                       "parallelism": f"dp{world} (independent sequences)" if world > 1 else "single GPU",
+                       "parallelism": f"tp{world} (one sequence over NCCL all-gathers)" if world > 1 else "single GPU",
+                       "mode": args.mode,
                        "l2": "inputs larger than L2 (1.31 GB of weights streamed per step)"},
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": vocab * 4 + 8},
-            "gpu_launches": launches_per_step(cfg) * Kst,
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": CLASSIFIER_TRAFFIC,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of the same "
-                                           "shape (profiles/gemv_lr_q8_0_classifier_128256x2048_n1.md)",
-                         "kernel": f"gemv_lr_kernel<1> Q8_0 {vocab}x{cfg['dim']} (classifier), {gms * 1000:.1f} us/launch",
-                         "peak_kind": hbm_kind,
-                         "algorithmic_bytes_per_launch": gbytes},
-            "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / hbm},
-            "clocks": clocks}
+            "gpu_launches": launches_per_step(cfg, world) * Kst,
+            "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_gbs, "frac": step_gbs / hbm,
+                              "peak_kind": hbm_kind}}
+    if world == 1:
+        # The tolerance mode on the same workload.
+        fast, _ = decode_rate(torch, model, Kst, 1 - mode, ctx_len=PROMPT + W + Kst + 16)
+        line["modes"] = {args.mode: value, ("fast" if mode == 0 else "exact"): fast,
+                         "note": "exact: bit-identical to the reference's scalar kernels; fast: tree-reduced RMSNorm "
+                                 "and attention sums (drift comparable to the reference's own AVX2 path)"}
+        # Dominant in-step kernel family: the small Q8_0 linears (QKV / wo / down run the same streaming
+        # GEMV at 2048-8192 columns); measured standalone on the wo shape; and the largest launch (classifier).
+        prof = profile_summary()
+        gstream = torch.cuda.Stream()
+        nb, gms = gemv_roofline(torch, cfg["dim"], cfg["n_heads"] * cfg["head_dim"], 50, gstream)
+        achieved = nb / (gms / 1000.0) / 1e9
+        small = prof.get("gemv_small_linears", {})
+        line["roofline"] = {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                            "traffic": small.get("dram_bytes_per_launch"),
+                            "kernel": f"gemv_lr_kernel Q8_0 {cfg['dim']}x{cfg['dim']} (wo shape; QKV / wo / down "
+                                      f"family), {gms * 1000:.2f} us/launch",
+                            "step_share": small.get("step_share"), "peak_kind": hbm_kind,
+                            "algorithmic_bytes_per_launch": nb}
+        cb, cms = gemv_roofline(torch, vocab, cfg["dim"], 20, gstream)
+        ca = cb / (cms / 1000.0) / 1e9
+        cls = prof.get("gemv_classifier", {})
+        line["roofline_classifier"] = {"bound": "hbm", "achieved": ca, "peak": hbm, "unit": "GB/s", "frac": ca / hbm,
+                                       "traffic": cls.get("dram_bytes_per_launch"),
+                                       "kernel": f"gemv_lr_kernel Q8_0 {vocab}x{cfg['dim']}, {cms * 1000:.1f} us/launch",
+                                       "step_share": cls.get("step_share"), "algorithmic_bytes_per_launch": cb}
+        if not args.no_other_configs:
+            line["other_configs"] = other_configs(torch, hbm)
+    line["clocks"] = sampler.stop()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         blob = model.export()
         threads = os.cpu_count()
         steps = args.cpu_steps
         tps, dt = cpu_decode(blob, cfg, steps, 2, threads)
+        tps1, dt1 = cpu_decode(blob, cfg, max(4, steps // 8), 1, 1)
         line["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
                                 "sample": f"config0 greedy decode, {PROMPT}-token prompt then {steps} tokens "
-                                          f"({dt:.1f} s) with the C++ restatement of the reference AVX2 path"}
+                                          f"({dt:.1f} s) with the C++ restatement of the reference AVX2 path",
+                                "one_thread": {"value": tps1, "cores": 1, "sample": f"{max(4, steps // 8)} tokens "
+                                                                                     f"({dt1:.1f} s)"}}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    ctx.close()
     model.close()
     if world > 1:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -323,7 +459,9 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="exact", choices=["exact", "fast"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-other-configs", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=96)
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))

@@ -1,8 +1,8 @@
-"""The multi-GPU bench path on CPU: `bench.py --gpus N` runs N independent
-decode replicas (config 0 fits one GPU; there is no collective on the data
-path), times every region as the max over ranks and reports whole-job
-tokens/s. Two `gloo` ranks here check that reduction and the reference arm's
-rank handling (only rank 0 runs and prints)."""
+"""The multi-GPU bench path on CPU: `bench.py --gpus N` runs one sequence
+tensor-parallel over N ranks, times every region as the max over ranks and
+reports the job's tokens/s (every rank serves the same tokens). Two `gloo`
+ranks here check that reduction and the reference arm's rank handling (only
+rank 0 runs and prints)."""
 import os
 import socket
 import sys
@@ -29,7 +29,7 @@ def _rank(rank, world, port, q):
     try:
         local_ms = 100.0 + 50.0 * rank  # the slower rank sets the job time
         ms = bench.max_over_ranks_of(local_ms, world, "cpu")
-        value = bench.job_tokens_per_s(ms, 128, world)
+        value = bench.job_tokens_per_s(ms, 128)
         # The reference arm does its work on rank 0 only; the others return at once.
         other = bench.run_reference(None, rank, world) if rank != 0 else None
         q.put((rank, ms, value, other))
@@ -37,7 +37,7 @@ def _rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_two_replicas_max_over_ranks_and_job_throughput():
+def test_two_ranks_max_over_ranks_and_job_throughput():
     world, port = 2, _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -50,7 +50,7 @@ def test_two_replicas_max_over_ranks_and_job_throughput():
     got = sorted(q.get(timeout=5) for _ in range(world))
     for rank, ms, value, other in got:
         assert ms == pytest.approx(150.0)  # max over ranks, seen by every rank
-        assert value == pytest.approx(world * 128 / 0.150)
+        assert value == pytest.approx(128 / 0.150)  # one sequence served by every rank
         assert other is None
 
 
@@ -58,4 +58,4 @@ def test_single_rank_needs_no_process_group():
     sys.path.insert(0, ROOT)
     import bench
     assert bench.max_over_ranks_of(12.5, 1, "cpu") == 12.5
-    assert bench.job_tokens_per_s(1000.0, 128, 1) == pytest.approx(128.0)
+    assert bench.job_tokens_per_s(1000.0, 128) == pytest.approx(128.0)
