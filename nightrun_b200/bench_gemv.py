@@ -5,6 +5,7 @@ matvec/matmul entry points on device-resident random weights.
     python -m nightrun_b200.bench_gemv --fmt q8_0 --rows 128256 --cols 2048 --n 1 --reps 3
 
 Algorithmic bytes per launch = packed weight bytes + activation blocks + f32 outputs.
+Consecutive launches use different weight copies (more than L2 together).
 """
 import argparse
 import json
@@ -41,13 +42,16 @@ def run(fmt, rows, cols, n, reps, stream):
     (kernels.quantize if fmt == "q8_0" else kernels.quantize_q8k)(x, xq, stream=stream)
     y = torch.empty(n * rows, device="cuda")
     fn = {"q8_0": kernels.matmul_q8, "q4k": kernels.matmul_q4k, "q6k": kernels.matmul_q6k}[fmt]
-    for _ in range(3):
-        fn(y, w, xq, rows, cols, n, stream=stream)
+    # Rotate over weight copies larger than L2 (126 MB) together, so every
+    # launch streams its weights from HBM.
+    copies = [w] + [w.clone() for _ in range(max(0, (160 << 20) // w.numel()))]
+    for i in range(3):
+        fn(y, copies[i % len(copies)], xq, rows, cols, n, stream=stream)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(stream)
-    for _ in range(reps):
-        fn(y, w, xq, rows, cols, n, stream=stream)
+    for i in range(reps):
+        fn(y, copies[i % len(copies)], xq, rows, cols, n, stream=stream)
     e1.record(stream)
     e1.synchronize()
     kernels.sync_check(stream)

@@ -502,7 +502,7 @@ int shard_for(const nrc_meta& mt, int n, int r, Shard* sh) {
 }
 
 struct Layout {
-  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, mxb, status, hist, samp, tps, tpr;
+  size_t kc, vc, x, q, k, v, att, g, u, logits, cos_t, sin_t, mxq, mxd, mxb, xsh, status, hist, samp, tps, tpr;
   // Several sequences: per-sequence positions / next input / last choice,
   // 0..S-1, the pass's per-token ids / positions / sequences, classifier
   // rows, gathered final rows, their logits, per-sequence token history.
@@ -545,6 +545,9 @@ Layout layout_for(const nrc_meta& mt, size_t ctx, size_t n_seqs = 1, bool batch 
   L.mxq = take(BM * maxk);            // tensor-core activation tiles (prefill)
   L.mxd = take(BM * (maxk / 32) * 4);  // and their block scales
   L.mxb = take(BM * (maxk / 256) * 8 * 4);  // and the chunk sums of the K-quant tiles
+  // Quantized attention-norm activations shared by the QKV launches of one layer
+  // (8 tokens of Q8_0 or Q8_K blocks).
+  L.xsh = take(8 * std::max(dim / 32 * 34, dim / 256 * 292 + 292));
   L.status = take(sizeof(Status));
   L.hist = take((ctx + 1) * 4);
   L.samp = take(sample_scratch_bytes((int)mt.vocab));  // sampler candidates
@@ -624,6 +627,7 @@ struct nrc_ctx {
   uint8_t* mxq;  // tensor-core activation tiles (prefill)
   float* mxd;
   int* mxb;
+  uint8_t* xsh;
   Status* st;
   uint32_t* hist;
   uint32_t* h_stage = nullptr;  // pinned host staging: tokens in, status out
@@ -769,6 +773,7 @@ static int ctx_create(const nrc_model* m, size_t ctx, size_t n_seqs, bool batch,
   c->mxq = A + c->lay.mxq;
   c->mxd = reinterpret_cast<float*>(A + c->lay.mxd);
   c->mxb = reinterpret_cast<int*>(A + c->lay.mxb);
+  c->xsh = A + c->lay.xsh;
   c->st = reinterpret_cast<Status*>(A + c->lay.status);
   c->hist = reinterpret_cast<uint32_t*>(A + c->lay.hist);
   c->samp = reinterpret_cast<unsigned long long*>(A + c->lay.samp);
@@ -858,6 +863,11 @@ cudaError_t gemv_tokens(GemvArgs a, int nt, int x_ld_f, cudaStream_t s, bool pdl
     GemvArgs b = a;
     b.nt = nt - t0 < 8 ? nt - t0 : 8;
     if (b.xf) b.xf = a.xf + (size_t)t0 * x_ld_f;
+    if (a.xq) {
+      const size_t blk = a.fmt == FMT_Q8_0 ? (size_t)(a.K / 32) * 34 : (size_t)(a.K / 256) * 292;
+      b.xq = static_cast<const uint8_t*>(a.xq) + (size_t)t0 * blk;
+    }
+    if (t0 > 0) b.xq_out = nullptr;  // the sharing serves one group of at most 8 tokens
     for (int i = 0; i < b.nseg; i++)
       if (b.seg[i].y) b.seg[i].y = a.seg[i].y + (size_t)t0 * a.seg[i].ld;
     if (b.resid) b.resid = a.resid + (size_t)t0 * a.resid_ld;
@@ -894,6 +904,10 @@ struct Lin {
   int nseg;
   int epi;
   float scale = 1.0f;  // EPI_STORE: y = sum * scale
+  // Streaming GEMV only: export the quantized input (xq_out), or take it
+  // already quantized (xq, then x / norm_w are not read).
+  uint8_t* xq_out = nullptr;
+  const uint8_t* xq = nullptr;
   // Weights of the next linear layer, prefetched into L2 while this one runs.
   const uint8_t* pf;
   size_t pf_bytes;
@@ -975,9 +989,14 @@ cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
   }
   GemvArgs a = gemv_base(c, L.fmt, L.K);
   a.scale = L.scale;
-  a.xf = L.x;
-  a.xf_ld = L.K;
-  a.norm_w = L.norm_w;
+  if (L.xq) {
+    a.xq = L.xq;
+  } else {
+    a.xf = L.x;
+    a.xf_ld = L.K;
+    a.norm_w = L.norm_w;
+    a.xq_out = L.xq_out;
+  }
   a.epi = L.epi;
   for (int i = 0; i < L.nseg; i++) a.seg[i] = GemvSegArg{L.w[i], L.y[i], L.rows[i], L.rows[i]};
   a.nseg = L.nseg;
@@ -1079,6 +1098,11 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
       float* ys[3] = {c->q, c->k, c->v};
       const int rows[3] = {ql, c->kvl, c->kvl};
       bool done[3] = {false, false, false};
+      // Q4_K and Q6_K launches both read Q8_K activations: the first launch
+      // exports them (at most 8 tokens), the next one reads them back.
+      const bool kq_mix = nt <= 8 && fs[0] != FMT_Q8_0 && fs[1] != FMT_Q8_0 && fs[2] != FMT_Q8_0 &&
+                          !(fs[0] == fs[1] && fs[1] == fs[2]);
+      bool first = true;
       for (int i = 0; i < 3; i++) {
         if (done[i]) continue;
         Lin L{};
@@ -1089,6 +1113,13 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
         L.epi = EPI_STORE;
         L.pf = pf_o;
         L.pf_bytes = n_o;
+        if (kq_mix) {
+          if (first)
+            L.xq_out = c->xsh;
+          else
+            L.xq = c->xsh;
+          first = false;
+        }
         for (int j = i; j < 3; j++)
           if (!done[j] && fs[j] == fs[i]) {
             L.w[L.nseg] = ws[j];

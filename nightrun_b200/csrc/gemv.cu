@@ -67,6 +67,7 @@ struct Params {
   int nstage;       // a multiple of ncw: every slot belongs to one warp
   int ncw;          // consumer warps that own tiles (the others only help with the prologue)
   const uint8_t* xq;
+  uint8_t* xq_out;
   const float* xf;
   int xf_ld;
   const float* norm_w;
@@ -247,6 +248,31 @@ NRC_DEV void build_x_f32(const Params& p, uint8_t* smem) {
       }
     }
     named_sync(1, NCT);  // xs is reused by the next token / the term buffer
+  }
+  if (p.xq_out && blockIdx.x == 0) {
+    // The activations as blocks for a following launch (XMODE 0 reads them back).
+    for (int i = tid; i < p.nt * p.bpr; i += NCT) {
+      const int tok = i / p.bpr, b = i % p.bpr;
+      const uint32_t* src = xq + xq_index(FMT, p, tok, b);
+      if (FMT == FMT_Q8_0) {
+        uint8_t* d = p.xq_out + (size_t)i * Q8_0_BYTES;
+        const uint16_t hb = f32_to_f16(xd[tok * p.bpr + b]);  // exact: the scale is an f16 value
+        d[0] = (uint8_t)(hb & 0xff);
+        d[1] = (uint8_t)(hb >> 8);
+        for (int k = 0; k < 8; k++) {
+          const uint32_t w = src[k];
+          d[2 + 4 * k] = (uint8_t)w;
+          d[3 + 4 * k] = (uint8_t)(w >> 8);
+          d[4 + 4 * k] = (uint8_t)(w >> 16);
+          d[5 + 4 * k] = (uint8_t)(w >> 24);
+        }
+      } else {
+        uint32_t* d = reinterpret_cast<uint32_t*>(p.xq_out + (size_t)i * Q8K_BYTES);
+        d[0] = __float_as_uint(xd[tok * p.bpr + b]);
+        for (int k = 0; k < 64; k++) d[1 + k] = src[k];
+        for (int j = 0; j < 8; j++) d[65 + j] = (uint32_t)(uint16_t)(int16_t)xb[(tok * p.bpr + b) * 8 + j];
+      }
+    }
   }
 }
 
@@ -1082,6 +1108,7 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   }
   p.off_nw = -1;
   p.xq = static_cast<const uint8_t*>(a.xq);
+  p.xq_out = a.xf ? static_cast<uint8_t*>(a.xq_out) : nullptr;
   p.xf = a.xf;
   p.xf_ld = a.xf_ld;
   p.norm_w = a.norm_w;

@@ -33,6 +33,11 @@ struct GemvArgs {
   const void* xq;
   const float* xf;
   int xf_ld;
+  // With xf: CTA 0 also stores the quantized activations here as blocks
+  // (Q8_0 34 B, or Q8_K 292 B whose bsums hold each 32-value sum in the even
+  // slot), so a following launch over other weights of the same input takes
+  // them as xq instead of normalizing and quantizing again.
+  void* xq_out;
   const float* norm_w;
   float eps;
   int fast_norm;  // tolerance mode: the RMSNorm sum of squares as a tree (not the reference's chain)
