@@ -21,7 +21,9 @@ namespace nrc {
 namespace {
 
 constexpr int ATT_THREADS = 128;  // >= head_dim: one V output chain per thread
-constexpr int ATT_VCH = 128;      // V rows staged per pass
+// V rows staged per pass: 128 for single-token decode (few CTAs, deep
+// staging), 32 when many tokens run (more CTAs resident per SM).
+constexpr int ATT_VCH_DECODE = 128, ATT_VCH_MANY = 32;
 
 NRC_DEV float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)bits)); }  // exact
 
@@ -150,8 +152,11 @@ NRC_DEV void cp_async_wait() {
 // FAST (tolerance mode): the same structure with fused multiply-adds in the
 // dot products, the softmax sum as a CTA tree and the V sums split over
 // ATT_THREADS / head_dim position groups combined in a fixed order.
-template <bool FAST>
-__global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
+// HD: head_dim as a constant (32, 64 or 128), so a thread's K row lives in
+// HD / 8 registers of 16 bytes; the register bound keeps three (HD 128) or
+// four CTAs resident per SM when many (token, head) CTAs run.
+template <bool FAST, int HD>
+__global__ void __launch_bounds__(ATT_THREADS, HD >= 128 ? 3 : 4) k_attention(const AttnArgs a) {
   pdl_wait();
   pdl_trigger();
   const int h = blockIdx.x, tok = blockIdx.y;
@@ -170,7 +175,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   uint16_t* vnew = knew + hd;                                   // [hd] new v (f16, fused)
   float* sc = reinterpret_cast<float*>(vnew + hd);              // [ctx] scores, then probabilities
   const int sc_len = ((a.ctx + 3) & ~3) > ATT_THREADS ? ((a.ctx + 3) & ~3) : ATT_THREADS;
-  uint16_t* vs = reinterpret_cast<uint16_t*>(sc + sc_len);      // [2][ATT_VCH][hd]
+  uint16_t* vs = reinterpret_cast<uint16_t*>(sc + sc_len);      // [2][vch][hd]
+  const int vch = a.nt > 1 ? ATT_VCH_MANY : ATT_VCH_DECODE;
   __shared__ float red[ATT_THREADS / 32];
   __shared__ SeqSumShared ssh;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -181,8 +187,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   // comes from shared memory.
   const int cached = fused ? (int)pos : npos;
   auto stage_v = [&](int t0, int buf) {
-    const int tn = min(ATT_VCH, cached - t0);
-    uint16_t* dst = vs + (size_t)buf * ATT_VCH * hd;
+    const int tn = min(vch, cached - t0);
+    uint16_t* dst = vs + (size_t)buf * vch * hd;
     for (int i = tid; i < tn * cpr; i += ATT_THREADS) {
       const int r = i / cpr, c = i - r * cpr;
       cp_async16(dst + r * hd + c * 8, vbase + (size_t)(t0 + r) * kv_dim + c * 8);
@@ -192,12 +198,11 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   stage_v(0, 0);
   // The K row of this thread's first position, loaded now so its latency
   // overlaps the RoPE work below.
-  uint4 k0[16];
+  uint4 k0[HD / 8];
   if (tid < cached) {
     const uint4* kr = reinterpret_cast<const uint4*>(kbase + (size_t)tid * kv_dim);
 #pragma unroll
-    for (int c = 0; c < 16; c++)
-      if (c < cpr) k0[c] = kr[c];
+    for (int c = 0; c < HD / 8; c++) k0[c] = kr[c];
   }
   if (fused) {
     const float* ct = a.cos_tab + (size_t)pos * half;
@@ -237,8 +242,8 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
     float s = 0.0f;
     if (t == tid && t < cached) {
 #pragma unroll
-      for (int c = 0; c < 16; c++) {
-        if (c < cpr) {
+      for (int c = 0; c < HD / 8; c++) {
+        {
           const uint32_t w[4] = {k0[c].x, k0[c].y, k0[c].z, k0[c].w};
           const float* qd = qs + c * 8;
 #pragma unroll
@@ -304,15 +309,15 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attention(const AttnArgs a) {
   const int H = FAST ? ATT_THREADS / hd : 1;
   const int d = FAST ? tid % hd : tid, grp = FAST ? tid / hd : 0;
   int buf = 0;
-  for (int t0 = 0; t0 < npos; t0 += ATT_VCH, buf ^= 1) {
-    const int tn = min(ATT_VCH, npos - t0);
-    if (t0 + ATT_VCH < cached) {
-      stage_v(t0 + ATT_VCH, buf ^ 1);
+  for (int t0 = 0; t0 < npos; t0 += vch, buf ^= 1) {
+    const int tn = min(vch, npos - t0);
+    if (t0 + vch < cached) {
+      stage_v(t0 + vch, buf ^ 1);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
-    uint16_t* vb = vs + (size_t)buf * ATT_VCH * hd;
+    uint16_t* vb = vs + (size_t)buf * vch * hd;
     if (fused && (int)pos < t0 + tn)
       for (int i = tid; i < hd; i += ATT_THREADS) vb[((int)pos - t0) * hd + i] = vnew[i];
     __syncthreads();
@@ -476,22 +481,29 @@ cudaError_t rope_append_run(const RopeArgs& a, cudaStream_t s, bool pdl) {
   return launch((const void*)k_rope_append, dim3((items + wpb - 1) / wpb), dim3(32 * wpb), 0, s, pdl, args);
 }
 
-size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx) {
+size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx, int nt) {
   (void)n_heads;
   (void)n_kv_heads;
   // q + rope scratch (4 hd floats) | new k, v (2 hd f16) | scores (at least one float per thread: the
   // tolerance mode combines its V partial sums there) | 2 V chunks
   const int sc = ((ctx + 3) & ~3) > ATT_THREADS ? ((ctx + 3) & ~3) : ATT_THREADS;
-  return (size_t)head_dim * 4 * 4 + (size_t)head_dim * 2 * 2 + (size_t)sc * 4 + (size_t)2 * ATT_VCH * head_dim * 2;
+  const int vch = nt > 1 ? ATT_VCH_MANY : ATT_VCH_DECODE;
+  return (size_t)head_dim * 4 * 4 + (size_t)head_dim * 2 * 2 + (size_t)sc * 4 + (size_t)2 * vch * head_dim * 2;
 }
 
 cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl, bool fast) {
   if (a.n_kv_heads < 1 || a.n_heads % a.n_kv_heads || a.head_dim % 32 || a.head_dim > ATT_THREADS ||
       (a.fused && (a.nt != 1 || a.pos_tok)))
     return cudaErrorInvalidValue;
-  const size_t smem = attention_smem_bytes(a.n_heads, a.n_kv_heads, a.head_dim, a.ctx);
+  const size_t smem = attention_smem_bytes(a.n_heads, a.n_kv_heads, a.head_dim, a.ctx, a.nt);
   if (smem > ATTN_MAX_SMEM) return cudaErrorInvalidValue;
-  const void* fn = fast ? (const void*)k_attention<true> : (const void*)k_attention<false>;
+  const void* fn = nullptr;
+  switch (a.head_dim) {
+    case 32: fn = fast ? (const void*)k_attention<true, 32> : (const void*)k_attention<false, 32>; break;
+    case 64: fn = fast ? (const void*)k_attention<true, 64> : (const void*)k_attention<false, 64>; break;
+    case 128: fn = fast ? (const void*)k_attention<true, 128> : (const void*)k_attention<false, 128>; break;
+    default: return cudaErrorInvalidValue;
+  }
   if (cudaError_t e = ensure_smem_attr(fn, ATTN_MAX_SMEM)) return e;
   AttnArgs aa = a;
   void* args[] = {&aa};

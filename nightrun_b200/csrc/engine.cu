@@ -675,7 +675,7 @@ static int ctx_create(const nrc_model* m, size_t ctx, size_t n_seqs, bool batch,
   if (mt.head_dim % 32 || mt.head_dim > 128 || mt.n_kv_heads == 0 || mt.n_heads % mt.n_kv_heads)
     return fail(NRC_ERR_INVALID, "unsupported attention shape (head_dim %u, heads %u/%u)", mt.head_dim, mt.n_heads,
                 mt.n_kv_heads);
-  if (attention_smem_bytes(mt.n_heads, mt.n_kv_heads, mt.head_dim, (int)ctx) > ATTN_MAX_SMEM)
+  if (attention_smem_bytes(mt.n_heads, mt.n_kv_heads, mt.head_dim, (int)ctx, 1) > ATTN_MAX_SMEM)
     return fail(NRC_ERR_INVALID, "context of %zu positions exceeds the attention kernel's score buffer", ctx);
   nrc_ctx* c = new nrc_ctx();
   c->m = m;

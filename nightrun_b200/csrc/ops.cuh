@@ -74,7 +74,7 @@ struct AttnArgs {
 // Shared memory of one attention CTA (its score rows hold `ctx` positions);
 // contexts needing more than ATTN_MAX_SMEM are rejected at context creation.
 constexpr size_t ATTN_MAX_SMEM = 200 * 1024;
-size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx);
+size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx, int nt);
 // fast: the tolerance mode's tree-reduced variant (same inputs and outputs).
 cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl, bool fast = false);
 
