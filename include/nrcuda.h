@@ -48,6 +48,12 @@ const char* nrc_last_error(void);
 /* Synchronize `stream` and report (then clear) any error a kernel-level entry point's kernel
  * recorded on the current device (NRC_ERR_DEVICE: a bounded wait expired). */
 int nrc_sync_check(void* stream);
+/* Diagnostic with no counterpart in the reference: runs one kernel whose bounded wait can never be
+ * satisfied (kind 0: an mbarrier arrival withheld; kind 1: a shared-memory flag never raised) and
+ * gives up after limit_ns (1 ns .. 10 s), exactly as the pipelined kernels' waits do. Returns
+ * NRC_ERR_DEVICE (the expiry was recorded and reported, the error word cleared); the device and
+ * every context stay usable. */
+int nrc_wait_selftest(int kind, uint64_t limit_ns, void* stream);
 /* Library version: major*10000 + minor*100 + patch. */
 int nrc_version(void);
 

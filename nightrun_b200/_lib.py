@@ -64,6 +64,7 @@ SIGNATURES = [
     ("nrc_last_error", C.c_char_p, []),
     ("nrc_version", I, []),
     ("nrc_sync_check", I, [P]),
+    ("nrc_wait_selftest", I, [I, U64, P]),
     ("nrc_quantize_q8_0", I, [P, P, S, P]),
     ("nrc_dequantize_q8_0", I, [P, P, S, P]),
     ("nrc_quantize_q8k", I, [P, P, S, P]),

@@ -116,14 +116,15 @@ int matvec_common(int fmt, float* y, const void* w, const void* x, size_t rows, 
     // Tensor-core path (tcgen05 kind::i8 per sub-block), one pass per NS x ntg tokens.
     const int NS = mma_kq_ns(fmt);
     const size_t nsb = cols / 256;
-    const size_t per = (size_t)NS * 4;  // tokens per pass: four token groups
+    const size_t per = (size_t)NS * 8;  // tokens per pass: eight token groups
     for (size_t t0 = 0; t0 < batch; t0 += per) {
       const int nt = (int)(batch - t0 < per ? batch - t0 : per);
       const int ntg = (nt + NS - 1) / NS;
       uint8_t* xq = nullptr;
       float* xd = nullptr;
       int* xb = nullptr;
-      if (cudaMallocAsync((void**)&xq, (size_t)ntg * NS * cols, S(stream)) != cudaSuccess)
+      const int masked = fmt == FMT_Q6K ? 1 : 0;
+      if (cudaMallocAsync((void**)&xq, (size_t)ntg * NS * cols * (masked ? 2 : 1), S(stream)) != cudaSuccess)
         return nrc_fail_api(NRC_ERR_ALLOC, "activation tile allocation failed");
       if (cudaMallocAsync((void**)&xd, (size_t)ntg * NS * nsb * 4, S(stream)) != cudaSuccess) {
         cudaFreeAsync(xq, S(stream));
@@ -134,8 +135,8 @@ int matvec_common(int fmt, float* y, const void* w, const void* x, size_t rows, 
         cudaFreeAsync(xd, S(stream));
         return nrc_fail_api(NRC_ERR_ALLOC, "activation sum allocation failed");
       }
-      rc = cuda_rc(mma_kq_pack_run(static_cast<const uint8_t*>(x) + t0 * nsb * 292, nt, (int)cols, NS, ntg, xq, xd,
-                                   xb, S(stream)),
+      rc = cuda_rc(mma_kq_pack_run(static_cast<const uint8_t*>(x) + t0 * nsb * 292, nt, (int)cols, NS, ntg, masked, xq,
+                                   xd, xb, S(stream)),
                    "kq pack");
       MmaKqArgs m{};
       m.fmt = fmt;
@@ -329,6 +330,16 @@ int nrc_expf_hash(uint64_t* out_dev, int chunk0, int nchunks, void* stream) {
     return nrc_fail_api(NRC_ERR_INVALID, "bad expf_hash range");
   return cuda_rc(op_expf_hash(reinterpret_cast<unsigned long long*>(out_dev), chunk0, nchunks, S(stream)),
                  "expf_hash");
+}
+
+int nrc_wait_selftest(int kind, uint64_t limit_ns, void* stream) {
+  if (kind != 0 && kind != 1) return nrc_fail_api(NRC_ERR_INVALID, "kind must be 0 or 1");
+  if (limit_ns == 0 || limit_ns > 10000000000ull) return nrc_fail_api(NRC_ERR_INVALID, "limit outside 1 ns .. 10 s");
+  DevScratch sc;
+  int rc = dev_scratch(&sc);
+  if (rc) return rc;
+  if ((rc = cuda_rc(op_wait_selftest(sc.err, limit_ns, kind, S(stream)), "wait self-test"))) return rc;
+  return nrc_sync_check(stream);
 }
 
 int nrc_sync_check(void* stream) {

@@ -542,7 +542,7 @@ Layout layout_for(const nrc_meta& mt, size_t ctx, size_t n_seqs = 1, bool batch 
   L.logits = take((size_t)mt.vocab * 4);
   L.cos_t = take(ctx * (mt.head_dim / 2) * 4);
   L.sin_t = take(ctx * (mt.head_dim / 2) * 4);
-  L.mxq = take(BM * maxk);            // tensor-core activation tiles (prefill)
+  L.mxq = take(BM * maxk * 2);        // tensor-core activation tiles (x 2: the Q6_K masked halves)
   L.mxd = take(BM * (maxk / 32) * 4);  // and their block scales
   L.mxb = take(BM * (maxk / 256) * 8 * 4);  // and the chunk sums of the K-quant tiles
   // Quantized attention-norm activations shared by the QKV launches of one layer
@@ -934,7 +934,7 @@ cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
   for (int i = 0; i < L.nseg; i++) kq = kq && (reinterpret_cast<uintptr_t>(L.w[i]) & 15) == 0;
   if (kq) {
     const int NS = mma_kq_ns(L.fmt), ntg = (nt + NS - 1) / NS;
-    MmaKqActArgs qa{L.x, L.K, L.norm_w, c->eps, nt, L.K, NS, ntg, c->mxq, c->mxd, c->mxb};
+    MmaKqActArgs qa{L.x, L.K, L.norm_w, c->eps, nt, L.K, NS, ntg, c->mxq, c->mxd, c->mxb, L.fmt == FMT_Q6K ? 1 : 0};
     cudaError_t e = mma_kq_act_run(qa, s, pdl);
     if (e) return e;
     MmaKqArgs m{};

@@ -93,7 +93,10 @@ namespace nrc {
   0x1.f50765b6e4540p+0, 0x1.9d3e12dd8a18bp-54, \
   0x1.fa7c1819e90d8p+0, 0x1.74853f3a5931ep-55,
 
-__constant__ const double EXPCR_T_DEV[128] = {EXPCR_TABLE};
+// In global memory, read through the L1 cache: the lanes of a warp index
+// different entries, which the constant cache would serve one address at a
+// time.
+static __device__ double EXPCR_T_DEV[128] = {EXPCR_TABLE};
 
 NRC_DEV float expf_cr(float xf) {
   // NaN: the quieted input, sign and payload kept (what x + x gives on the
@@ -115,7 +118,7 @@ NRC_DEV float expf_cr(float xf) {
   const long long k = __double2ll_rn(kd);
   const int j = (int)(k & 63);
   const long long e = (k - j) / 64;
-  const double th = EXPCR_T_DEV[2 * j], tl = EXPCR_T_DEV[2 * j + 1];
+  const double th = __ldg(&EXPCR_T_DEV[2 * j]), tl = __ldg(&EXPCR_T_DEV[2 * j + 1]);
   const double qq = __fma_rn(th, p, tl);
   double yh = __dadd_rn(th, qq);
   double yl = __dadd_rn(__dadd_rn(th, -yh), qq);

@@ -49,9 +49,11 @@ cudaError_t mma_pack_q8_run(const uint8_t* x, int nt, int K, int NS, int ntg, ui
 // Bytes of the canonical activation tiles and scales for nt tokens.
 // K-quant GEMM (mma_kq.cu): Q4_K or Q6_K weights x Q8_K activations. The
 // activations are quantize_q8k'd per token into canonical tiles of 32-value
-// chunks: xq[((tg * nsb + sb) * 8 + chunk) * NS * 32 ...], their block scales
+// chunks, xq[((tg * nsb + sb) * T + tile) * NS * 32 ...] with T = 8 tiles per
+// super-block, or T = 16 for Q6_K weights (masked: each chunk as two tiles
+// keeping one 16-value half, the other half zero), their block scales
 // xd[(tg * nsb + sb) * NS + n] and chunk sums xb[((tg * nsb + sb) * NS + n) * 8
-// + chunk] (nsb = K / 256). NS is mma_kq_ns(fmt): 64 for Q4_K, 32 for Q6_K.
+// + chunk] (nsb = K / 256). NS is mma_kq_ns(fmt) (32 tokens).
 struct MmaKqActArgs {
   const float* x;
   int x_ld;
@@ -61,10 +63,11 @@ struct MmaKqActArgs {
   uint8_t* xq;
   float* xd;
   int* xb;
+  int masked;  // Q6_K layout
 };
 cudaError_t mma_kq_act_run(const MmaKqActArgs& a, cudaStream_t s, bool pdl);
-cudaError_t mma_kq_pack_run(const uint8_t* x, int nt, int K, int NS, int ntg, uint8_t* xq, float* xd, int* xb,
-                            cudaStream_t s);
+cudaError_t mma_kq_pack_run(const uint8_t* x, int nt, int K, int NS, int ntg, int masked, uint8_t* xq, float* xd,
+                            int* xb, cudaStream_t s);
 struct MmaKqArgs {
   int fmt;        // FMT_Q4K or FMT_Q6K
   MmaSeg seg[3];  // weights: 16-byte aligned

@@ -38,11 +38,12 @@
 namespace nrc {
 namespace {
 
-constexpr int NST = 2;  // pipeline stages
+constexpr int KNS = 32;      // tokens per CTA
 constexpr int KTHR = 448;
 constexpr int WREP = 8, WPROD = 12, WMMA = 13;
 constexpr int EPI_WARPS = 8, REP_WARPS = 4;
-constexpr int RAW_SLOT = 240;  // bytes per row per stage: a 16-byte aligned superset of one super-block
+constexpr int NMR = 4;       // row / token scale ring (repack -> epilogue)
+constexpr int RMETA = 24;    // bytes per row in a scale slot: d, dmin (f32) + sc[8], m[8] (Q6_K: d + sc[16])
 
 struct KqParams {
   const uint8_t* w[3];
@@ -52,37 +53,42 @@ struct KqParams {
   int tile_start[4];
   int nseg;
   int fmt, nsb, row_bytes;  // super-blocks per row
-  const uint8_t* xq;        // canonical activation tiles [ntg][nsb][8][NS x 32]
-  const float* xd;          // [ntg][nsb][NS]
-  const int* xb;            // [ntg][nsb][NS][8] sums of each 32-value chunk (Q4_K)
-  int nt, NS, ntg;
+  const uint8_t* xq;        // canonical activation tiles [ntg][nsb][NBT][KNS x 32]
+  const float* xd;          // [ntg][nsb][KNS]
+  const int* xb;            // [ntg][nsb][KNS][8] sums of each 32-value chunk (Q4_K)
+  int nt, ntg;
   int epi;
   float scale;
   float* resid;
   int resid_ld;
   float rs;
   unsigned* err;
-  // stage layout (bytes from the stage base)
-  int off_a, off_raw, off_b, off_rmeta, off_dx, off_xb, stage_bytes, off_bar;
-  uint32_t tmem_cols;
+  int off_a, off_raw, off_b, stage_bytes, off_meta, off_bar, raw_slot;
+};
+
+// Per format: MMAs (TMEM slots) per super-block, A tiles, B tiles, TMEM
+// buffers, pipeline stages.
+template <int FMT> struct KqShape {
+  static constexpr int NA = FMT == FMT_Q4K ? 8 : 16;   // MMAs = TMEM slots per super-block
+  static constexpr int NAT = 8;                        // A tiles: the 8 chunks of 32 values
+  static constexpr int NBT = FMT == FMT_Q4K ? 8 : 16;  // B tiles (Q6_K: each chunk's two masked halves)
+  static constexpr int NB = 512 / (NA * KNS);          // TMEM buffers (super-blocks in flight)
+  static constexpr int NST = FMT == FMT_Q4K ? 3 : 2;   // smem stages
 };
 
 template <int FMT>
-constexpr int slots() { return FMT == FMT_Q4K ? 8 : 16; }
-template <int FMT>
-constexpr int tile_ns() { return FMT == FMT_Q4K ? 64 : 32; }
-
-template <int FMT>
 __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqParams p) {
-  constexpr int NA = slots<FMT>();
-  constexpr int NS = tile_ns<FMT>();
+  using SH = KqShape<FMT>;
+  constexpr int NA = SH::NA, NB = SH::NB, NST = SH::NST;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
-  uint64_t* full = bars;               // producer -> repack / epilogue (tx bytes)
-  uint64_t* aready = bars + NST;       // repack -> MMA (A tiles + row scales written)
-  uint64_t* empty = bars + 2 * NST;    // MMA commit + epilogue warps -> producer
-  uint64_t* mdone = bars + 3 * NST;    // MMA commit -> epilogue (the stage's slots written)
-  uint64_t* tfree = bars + 4 * NST;    // epilogue warps -> MMA (TMEM drained), one barrier
+  uint64_t* full = bars;                  // producer -> repack (tx bytes)
+  uint64_t* aready = full + NST;          // repack -> MMA (A tiles, scales written)
+  uint64_t* empty = aready + NST;         // MMA commit -> producer (stage consumed)
+  uint64_t* mdone = empty + NST;          // MMA commit -> epilogue (the super-block's slots written)
+  uint64_t* tfree = mdone + NST;          // epilogue warps -> MMA (TMEM buffer drained)
+  uint64_t* mfree = tfree + NB;           // epilogue warps -> repack (scale slot read)
+  uint64_t* mready = mfree + NMR;         // repack warps -> epilogue (scale slot written)
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -100,16 +106,20 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
     for (int s = 0; s < NST; s++) {
       mbar_init(&full[s], 1);
       mbar_init(&aready[s], REP_WARPS);
-      mbar_init(&empty[s], 1 + EPI_WARPS);
+      mbar_init(&empty[s], 1);
       mbar_init(&mdone[s], 1);
     }
-    mbar_init(tfree, EPI_WARPS);
+    for (int b = 0; b < NB; b++) mbar_init(&tfree[b], EPI_WARPS);
+    for (int m = 0; m < NMR; m++) {
+      mbar_init(&mfree[m], EPI_WARPS);
+      mbar_init(&mready[m], REP_WARPS);
+    }
     abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == WMMA) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
-                 "r"(p.tmem_cols)
+                 "r"(512)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -120,6 +130,7 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
   pdl_wait();  // activations and the residual stream come from the previous kernel
   const uint32_t tbase = tmem_base_sh;
   auto st_base = [&](int s) { return smem + (size_t)s * p.stage_bytes; };
+  auto meta = [&](int m) { return smem + p.off_meta + (size_t)m * (TC_M * RMETA + KNS * 36); };
   auto fail = [&](unsigned bit) {
     if (!abort_flag) {
       abort_flag = 1;
@@ -129,8 +140,13 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
 
   if (warp == WPROD) {
     // ------------------------------------------------------------ producer
+    // Raw rows of each super-block (16-byte aligned supersets, one bulk copy
+    // per row; a matrix's ragged last bytes by plain loads) and the
+    // super-block's activation tiles; a stage is refilled as soon as its MMAs
+    // completed (the epilogue reads its scales from the scale ring).
     const uint64_t pol = l2_evict_first();
     const uintptr_t wend_al = reinterpret_cast<uintptr_t>(wend) & ~(uintptr_t)15;
+    const uint32_t b_bytes = (uint32_t)SH::NBT * KNS * 32;
     int st = 0;
     for (; st < nsb; st++) {
       const int s = st % NST, u = st / NST;
@@ -142,8 +158,6 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
       }
       if (abort_flag) break;
       uint8_t* raw = st_base(s) + p.off_raw;
-      // This lane's rows: bulk-copied bytes [lo, hi) of each; a ragged end past
-      // the matrix's last 16-byte boundary goes by plain loads.
       uint32_t mine = 0;
       for (int r = lane; r < nrows; r += 32) {
         const uintptr_t a = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
@@ -151,28 +165,25 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
         uintptr_t hi = (a + bpb + 15) & ~(uintptr_t)15;
         if (hi > wend_al) hi = wend_al > lo ? wend_al : lo;
         mine += (uint32_t)(hi - lo);
-        for (uintptr_t b = hi > a ? hi : a; b < a + bpb; b++) raw[r * RAW_SLOT + (b - lo)] = *reinterpret_cast<const uint8_t*>(b);
+        for (uintptr_t b = hi > a ? hi : a; b < a + bpb; b++)
+          raw[r * p.raw_slot + (b - lo)] = *reinterpret_cast<const uint8_t*>(b);
       }
       uint32_t total = mine;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-      const size_t tix = (size_t)tg * nsb + st;
-      const uint32_t b_bytes = 8u * NS * 32, dx_bytes = NS * 4u, xb_bytes = FMT == FMT_Q4K ? NS * 32u : 0u;
       __syncwarp();  // every lane's plain byte stores before lane 0's release arrive
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], total + b_bytes + dx_bytes + xb_bytes);
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], total + b_bytes);
       __syncwarp();
       for (int r = lane; r < nrows; r += 32) {
         const uintptr_t a = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
         const uintptr_t lo = a & ~(uintptr_t)15;
         uintptr_t hi = (a + bpb + 15) & ~(uintptr_t)15;
         if (hi > wend_al) hi = wend_al > lo ? wend_al : lo;
-        if (hi > lo) bulk_g2s(raw + r * RAW_SLOT, reinterpret_cast<const void*>(lo), (uint32_t)(hi - lo), &full[s], pol);
+        if (hi > lo)
+          bulk_g2s(raw + r * p.raw_slot, reinterpret_cast<const void*>(lo), (uint32_t)(hi - lo), &full[s], pol);
       }
-      if (lane == 0) {
-        bulk_g2s(st_base(s) + p.off_b, p.xq + tix * 8 * NS * 32, b_bytes, &full[s], 0ull);
-        bulk_g2s(st_base(s) + p.off_dx, p.xd + tix * NS, dx_bytes, &full[s], 0ull);
-        if (FMT == FMT_Q4K) bulk_g2s(st_base(s) + p.off_xb, p.xb + tix * NS * 8, xb_bytes, &full[s], 0ull);
-      }
+      if (lane == 0)
+        bulk_g2s(st_base(s) + p.off_b, p.xq + ((size_t)tg * nsb + st) * b_bytes, b_bytes, &full[s], 0ull);
     }
     if (lane == 0)
       for (int k = st - 1; k >= 0 && k >= st - NST; k--)
@@ -181,22 +192,22 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
     // -------------------------------------------------------------- repack
     const int r = tid - WREP * 32;  // weight row of this thread
     for (int st = 0; st < nsb; st++) {
-      const int s = st % NST, u = st / NST;
-      if (abort_flag || !mbar_wait(&full[s], u & 1)) {
+      const int s = st % NST, u = st / NST, m = st % NMR;
+      if (abort_flag || !mbar_wait(&full[s], u & 1) || (st >= NMR && !mbar_wait(&mfree[m], ((st / NMR) - 1) & 1))) {
         fail(ERR_WAIT_FULL);
         break;
       }
       uint8_t* a = st_base(s) + p.off_a;
-      uint8_t* rm = st_base(s) + p.off_rmeta;
+      uint8_t* rm = meta(m) + r * RMETA;
       if (r < nrows) {
         const uintptr_t ga = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
-        const uint8_t* b = st_base(s) + p.off_raw + r * RAW_SLOT + (ga & 15);
+        const uint8_t* b = st_base(s) + p.off_raw + r * p.raw_slot + (ga & 15);
         if (FMT == FMT_Q4K) {
           // d, dmin (f16), 12 scale bytes (q4k_scale_min, kquant.rs:83-92), 128 bytes of nibbles.
           float* fm = reinterpret_cast<float*>(rm);
-          fm[r] = f16_to_f32((uint32_t)b[0] | ((uint32_t)b[1] << 8));
-          fm[TC_M + r] = f16_to_f32((uint32_t)b[2] | ((uint32_t)b[3] << 8));
-          uint8_t* scm = rm + 2 * TC_M * 4 + r * 16;  // sc[8], m[8]
+          fm[0] = f16_to_f32((uint32_t)b[0] | ((uint32_t)b[1] << 8));
+          fm[1] = f16_to_f32((uint32_t)b[2] | ((uint32_t)b[3] << 8));
+          uint8_t* scm = rm + 8;  // sc[8], m[8]
           const uint8_t* sb = b + 4;
 #pragma unroll
           for (int j = 0; j < 8; j++) {
@@ -208,14 +219,13 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
               scm[8 + j] = (sb[j + 4] >> 4) | ((sb[j] >> 6) << 4);
             }
           }
-          const uint8_t* qs = b + 16;
+          // 16-byte loads: the rows sit 144 bytes (9 x 16) apart, so eight threads'
+          // loads never share a bank group.
+          const uint4* qs = reinterpret_cast<const uint4*>(b + 16);
 #pragma unroll
           for (int c = 0; c < 4; c++) {
-            uint32_t wv[8];
-#pragma unroll
-            for (int k = 0; k < 8; k++)
-              wv[k] = (uint32_t)qs[32 * c + 4 * k] | ((uint32_t)qs[32 * c + 4 * k + 1] << 8) |
-                      ((uint32_t)qs[32 * c + 4 * k + 2] << 16) | ((uint32_t)qs[32 * c + 4 * k + 3] << 24);
+            const uint4 q0 = qs[2 * c], q1 = qs[2 * c + 1];
+            const uint32_t wv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
             uint8_t* lo = a + (2 * c) * (TC_M * 32);
             uint8_t* hi = a + (2 * c + 1) * (TC_M * 32);
             *reinterpret_cast<uint4*>(lo + canon_off(r, 0)) =
@@ -230,8 +240,8 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
         } else {
           // ql[128], qh[64], scales[16] (int8), d (f16): value v = q - 32 in natural order.
           float* fm = reinterpret_cast<float*>(rm);
-          fm[r] = f16_to_f32((uint32_t)b[208] | ((uint32_t)b[209] << 8));
-          int8_t* scm = reinterpret_cast<int8_t*>(rm + TC_M * 4) + r * 16;
+          fm[0] = f16_to_f32((uint32_t)b[208] | ((uint32_t)b[209] << 8));
+          int8_t* scm = reinterpret_cast<int8_t*>(rm + 4);
 #pragma unroll
           for (int g = 0; g < 16; g++) scm[g] = (int8_t)b[192 + g];
 #pragma unroll
@@ -239,7 +249,7 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
             const uint8_t* ql = b + 64 * h;
             const uint8_t* qh = b + 128 + 32 * h;
 #pragma unroll
-            for (int qd = 0; qd < 4; qd++) {  // quarter: values 128h + 32qd + l, chunk 4h + qd
+            for (int qd = 0; qd < 4; qd++) {  // quarter: values 128h + 32qd + l = chunk 4h + qd
               uint32_t wv[8];
 #pragma unroll
               for (int k = 0; k < 8; k++) {
@@ -253,52 +263,61 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
                 }
                 wv[k] = word;
               }
-              const int c = 4 * h + qd;  // 32-value chunk
-              uint8_t* g0 = a + (2 * c) * (TC_M * 32);      // group 2c: values 0..15 of the chunk
-              uint8_t* g1 = a + (2 * c + 1) * (TC_M * 32);  // group 2c + 1: values 16..31
-              *reinterpret_cast<uint4*>(g0 + canon_off(r, 0)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-              *reinterpret_cast<uint4*>(g0 + canon_off(r, 1)) = make_uint4(0, 0, 0, 0);
-              *reinterpret_cast<uint4*>(g1 + canon_off(r, 0)) = make_uint4(0, 0, 0, 0);
-              *reinterpret_cast<uint4*>(g1 + canon_off(r, 1)) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+              uint8_t* t = a + (4 * h + qd) * (TC_M * 32);
+              *reinterpret_cast<uint4*>(t + canon_off(r, 0)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+              *reinterpret_cast<uint4*>(t + canon_off(r, 1)) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
             }
           }
         }
       } else {
 #pragma unroll 1
-        for (int k = 0; k < NA; k++) {
+        for (int k = 0; k < SH::NAT; k++) {
           *reinterpret_cast<uint4*>(a + k * (TC_M * 32) + canon_off(r, 0)) = make_uint4(0, 0, 0, 0);
           *reinterpret_cast<uint4*>(a + k * (TC_M * 32) + canon_off(r, 1)) = make_uint4(0, 0, 0, 0);
         }
       }
+      // The super-block's token scales (and Q4_K chunk sums) into the scale slot.
+      {
+        const size_t tix = (size_t)tg * nsb + st;
+        float* dxs = reinterpret_cast<float*>(meta(m) + TC_M * RMETA);
+        int* xbs = reinterpret_cast<int*>(dxs + KNS);
+        if (r < KNS) dxs[r] = p.xd[tix * KNS + r];
+        if (FMT == FMT_Q4K)
+          for (int i = r; i < KNS * 8; i += TC_M) xbs[i] = p.xb[tix * KNS * 8 + i];
+      }
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
       __syncwarp();
-      if (lane == 0) mbar_arrive(&aready[s]);
+      if (lane == 0) {
+        mbar_arrive(&aready[s]);
+        mbar_arrive(&mready[m]);
+      }
     }
   } else if (warp == WMMA) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = idesc_i8(NS);
+      const uint32_t idesc = idesc_i8(KNS);
       int issued = -1;  // last super-block whose MMAs were issued
       for (int st = 0; st < nsb && !abort_flag; st++) {
-        const int s = st % NST, u = st / NST;
+        const int s = st % NST, u = st / NST, bf = st % NB;
         if (!mbar_wait(&aready[s], u & 1)) {
           fail(ERR_WAIT_FULL);
           break;
         }
-        // Every slot of the previous super-block drained by the epilogue.
-        if (st >= 1 && !mbar_wait(tfree, (st - 1) & 1)) {
+        // The TMEM buffer drained by the epilogue (super-block st - NB).
+        if (st >= NB && !mbar_wait(&tfree[bf], ((st / NB) - 1) & 1)) {
           fail(ERR_WAIT_EMPTY);
           break;
         }
         tc_fence_after();
         const uint8_t* a = st_base(s) + p.off_a;
         const uint8_t* bt = st_base(s) + p.off_b;
+        const uint32_t dbase = tbase + (uint32_t)(bf * NA * KNS);
 #pragma unroll 1
         for (int k = 0; k < NA; k++) {
-          const int chunk = FMT == FMT_Q4K ? k : k / 2;
-          const uint64_t ad = smem_desc(a + k * (TC_M * 32), 128, 256);
-          const uint64_t bd = smem_desc(bt + chunk * (NS * 32), 128, 256);
-          tc_mma_i8(tbase + (uint32_t)(k * NS), ad, bd, idesc, 0u);
+          const int at = FMT == FMT_Q4K ? k : k / 2;  // Q6_K: group k = half (k % 2) of chunk k / 2
+          const uint64_t ad = smem_desc(a + at * (TC_M * 32), 128, 256);
+          const uint64_t bd = smem_desc(bt + k * (KNS * 32), 128, 256);
+          tc_mma_i8(dbase + (uint32_t)(k * KNS), ad, bd, idesc, 0u);
         }
         tc_commit(&mdone[s]);
         tc_commit(&empty[s]);
@@ -311,84 +330,85 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3, half = warp >> 2;
-    const int r = q * 32 + lane;          // TMEM lane = weight row
-    constexpr int NH = NS / 2;            // tokens of this warp
-    const int n0 = half * NH;
-    float acc[NH];
+    const int r = q * 32 + lane;  // TMEM lane = weight row
+    const int n0 = half * 16;     // this warp's 16 tokens
+    float acc[16];
 #pragma unroll
-    for (int i = 0; i < NH; i++) acc[i] = 0.0f;
+    for (int i = 0; i < 16; i++) acc[i] = 0.0f;
     const uint32_t lane_base = tbase + ((uint32_t)(q * 32) << 16);
     for (int st = 0; st < nsb && !abort_flag; st++) {
-      const int s = st % NST, u = st / NST;
-      if (!mbar_wait(&mdone[s], u & 1)) {
+      const int s = st % NST, u = st / NST, bf = st % NB, m = st % NMR;
+      // mdone and mready complete at most one phase ahead of this warp: their
+      // next phases need this super-block's tfree / mfree.
+      if (!mbar_wait(&mdone[s], u & 1) || !mbar_wait(&mready[m], (st / NMR) & 1)) {
         fail(ERR_WAIT_FULL);
         break;
       }
       tc_fence_after();
-      const uint8_t* rm = st_base(s) + p.off_rmeta;
-      const float* dxs = reinterpret_cast<const float*>(st_base(s) + p.off_dx);
+      const uint8_t* rm = meta(m) + r * RMETA;
+      const float* dxs = reinterpret_cast<const float*>(meta(m) + TC_M * RMETA);
+      const int* xbs = reinterpret_cast<const int*>(dxs + KNS);
       float scf[NA];
-      float d = 0.0f, dmin = 0.0f;
+      float d, dmin = 0.0f;
       int mj[8];
       if (FMT == FMT_Q4K) {
         const float* fm = reinterpret_cast<const float*>(rm);
-        d = fm[r];
-        dmin = fm[TC_M + r];
-        const uint8_t* scm = rm + 2 * TC_M * 4 + r * 16;
+        d = fm[0];
+        dmin = fm[1];
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-          scf[j] = (float)scm[j];
-          mj[j] = scm[8 + j];
+          scf[j] = (float)rm[8 + j];
+          mj[j] = rm[16 + j];
         }
       } else {
-        d = reinterpret_cast<const float*>(rm)[r];
-        const int8_t* scm = reinterpret_cast<const int8_t*>(rm + TC_M * 4) + r * 16;
+        d = reinterpret_cast<const float*>(rm)[0];
+        const int8_t* scm = reinterpret_cast<const int8_t*>(rm + 4);
 #pragma unroll
         for (int g = 0; g < NA; g++) scf[g] = (float)scm[g];
       }
-      const int* xbs = reinterpret_cast<const int*>(st_base(s) + p.off_xb);
+      const uint32_t slot0 = lane_base + (uint32_t)(bf * NA * KNS + n0);
+      float sq[16];
 #pragma unroll
-      for (int c0 = 0; c0 < NH; c0 += 16) {
-        float sq[16];
+      for (int i = 0; i < 16; i++) sq[i] = 0.0f;
+      // Two slots per TMEM round trip; each slot's dots in slot order.
 #pragma unroll
-        for (int i = 0; i < 16; i++) sq[i] = 0.0f;
+      for (int k = 0; k < NA; k += 2) {
+        uint32_t v0[16], v1[16];
+        tc_ld16(slot0 + (uint32_t)(k * KNS), v0);
+        tc_ld16(slot0 + (uint32_t)((k + 1) * KNS), v1);
+        tc_wait_ld();
 #pragma unroll
-        for (int k = 0; k < NA; k++) {
-          uint32_t v[16];
-          tc_ld16(lane_base + (uint32_t)(k * NS + n0 + c0), v);
-          tc_wait_ld();
+        for (int i = 0; i < 16; i++) sq[i] = __fadd_rn(sq[i], __fmul_rn(scf[k], i2f((int)v0[i])));
 #pragma unroll
-          for (int i = 0; i < 16; i++) sq[i] = __fadd_rn(sq[i], __fmul_rn(scf[k], i2f((int)v[i])));
-        }
-#pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const int n = n0 + c0 + i;
-          const float dx = dxs[n];
-          float t;
-          if (FMT == FMT_Q4K) {
-            int sm = 0;
-#pragma unroll
-            for (int j = 0; j < 8; j++) sm += mj[j] * xbs[n * 8 + j];
-            t = __fsub_rn(__fmul_rn(__fmul_rn(d, dx), sq[i]), __fmul_rn(__fmul_rn(dmin, dx), i2f(sm)));
-          } else {
-            t = __fmul_rn(__fmul_rn(d, dx), sq[i]);
-          }
-          acc[c0 + i] = __fadd_rn(acc[c0 + i], t);
-        }
+        for (int i = 0; i < 16; i++) sq[i] = __fadd_rn(sq[i], __fmul_rn(scf[k + 1], i2f((int)v1[i])));
       }
-      // Slots and the stage's scales consumed.
+      // TMEM buffer drained: hand it back before the scalar tail.
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(tfree);
-        mbar_arrive(&empty[s]);
+      if (lane == 0) mbar_arrive(&tfree[bf]);
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const int n = n0 + i;
+        const float dx = dxs[n];
+        float t;
+        if (FMT == FMT_Q4K) {
+          int sm = 0;
+#pragma unroll
+          for (int j = 0; j < 8; j++) sm += mj[j] * xbs[n * 8 + j];
+          t = __fsub_rn(__fmul_rn(__fmul_rn(d, dx), sq[i]), __fmul_rn(__fmul_rn(dmin, dx), i2f(sm)));
+        } else {
+          t = __fmul_rn(__fmul_rn(d, dx), sq[i]);
+        }
+        acc[i] = __fadd_rn(acc[i], t);
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mfree[m]);
     }
     if (!abort_flag && r < nrows) {
       const int row = row0 + r;
 #pragma unroll
-      for (int i = 0; i < NH; i++) {
-        const int tok = tg * NS + n0 + i;
+      for (int i = 0; i < 16; i++) {
+        const int tok = tg * KNS + n0 + i;
         if (tok >= p.nt) break;
         float sv = acc[i];
         if (p.epi == EPI_RESID) {
@@ -405,7 +425,7 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
   __syncthreads();
   tc_fence_after();
   if (warp == WMMA) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(p.tmem_cols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(512) : "memory");
   }
 }
 
@@ -420,15 +440,16 @@ __global__ void __launch_bounds__(256) k_mma_kq_act(const MmaKqActArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nsb = a.K / 256;
   const int tg = n / a.NS, nn = n % a.NS;
+  const int nbt = a.masked ? 16 : 8;  // tiles per super-block
   __shared__ SeqSumShared ssh;
-  auto tile = [&](int sb, int c) { return a.xq + (((size_t)tg * nsb + sb) * 8 + c) * a.NS * 32; };
+  auto tile = [&](int sb, int c) { return a.xq + (((size_t)tg * nsb + sb) * nbt + c) * a.NS * 32; };
   if (n >= a.nt) {
-    for (int i = tid; i < nsb * 8; i += 256) {
-      uint8_t* t = tile(i / 8, i % 8);
+    for (int i = tid; i < nsb * nbt; i += 256) {
+      uint8_t* t = tile(i / nbt, i % nbt);
       *reinterpret_cast<uint4*>(t + canon_off(nn, 0)) = make_uint4(0, 0, 0, 0);
       *reinterpret_cast<uint4*>(t + canon_off(nn, 1)) = make_uint4(0, 0, 0, 0);
-      a.xb[(((size_t)tg * nsb + i / 8) * a.NS + nn) * 8 + i % 8] = 0;
     }
+    for (int i = tid; i < nsb * 8; i += 256) a.xb[(((size_t)tg * nsb + i / 8) * a.NS + nn) * 8 + i % 8] = 0;
     for (int sb = tid; sb < nsb; sb += 256) a.xd[((size_t)tg * nsb + sb) * a.NS + nn] = 0.0f;
     return;
   }
@@ -487,9 +508,14 @@ __global__ void __launch_bounds__(256) k_mma_kq_act(const MmaKqActArgs a) {
       dval = __fdiv_rn(1.0f, iscale);
     }
     // Lane holds values 8*lane .. +7 of the block: chunk lane / 4, bytes 8*(lane % 4).
-    uint8_t* t = tile(b, lane / 4);
-    const int byte = 8 * (lane % 4);
-    *reinterpret_cast<uint2*>(t + canon_off(nn, byte / 16) + byte % 16) = make_uint2(pk[0], pk[1]);
+    const int byte = 8 * (lane % 4), hf = byte / 16;
+    if (a.masked) {
+      // Two tiles per chunk, each keeping one 16-value half (the other half zero).
+      *reinterpret_cast<uint2*>(tile(b, 2 * (lane / 4) + hf) + canon_off(nn, hf) + byte % 16) = make_uint2(pk[0], pk[1]);
+      *reinterpret_cast<uint2*>(tile(b, 2 * (lane / 4) + 1 - hf) + canon_off(nn, hf) + byte % 16) = make_uint2(0u, 0u);
+    } else {
+      *reinterpret_cast<uint2*>(tile(b, lane / 4) + canon_off(nn, hf) + byte % 16) = make_uint2(pk[0], pk[1]);
+    }
     int s4 = part + __shfl_down_sync(0xffffffffu, part, 1);
     s4 += __shfl_down_sync(0xffffffffu, s4, 2);
     if ((lane & 3) == 0) a.xb[(((size_t)tg * nsb + b) * a.NS + nn) * 8 + lane / 4] = s4;
@@ -499,13 +525,14 @@ __global__ void __launch_bounds__(256) k_mma_kq_act(const MmaKqActArgs a) {
 
 // Pre-quantized Q8_K activation blocks [nt][nsb] (292 bytes: d f32, 256 int8,
 // 16 int16 bsums; kquant.rs:46-52) -> the canonical tiles, scales and chunk sums.
-__global__ void k_mma_kq_pack(const uint8_t* __restrict__ x, int nt, int nsb, int NS, int ntg, uint8_t* xq,
-                              float* xd, int* xb) {
+__global__ void k_mma_kq_pack(const uint8_t* __restrict__ x, int nt, int nsb, int NS, int ntg, int masked,
+                              uint8_t* xq, float* xd, int* xb) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;  // (token slot, block, chunk)
   if (i >= NS * ntg * nsb * 8) return;
   const int c = i % 8, b = (i / 8) % nsb, n = i / (8 * nsb);
   const int tg = n / NS, nn = n % NS;
-  uint8_t* t = xq + (((size_t)tg * nsb + b) * 8 + c) * NS * 32;
+  const int nbt = masked ? 16 : 8;
+  uint8_t* t = xq + (((size_t)tg * nsb + b) * nbt + (masked ? 2 * c : c)) * NS * 32;
   uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   int pair = 0;
   float d = 0.0f;
@@ -521,8 +548,16 @@ __global__ void k_mma_kq_pack(const uint8_t* __restrict__ x, int nt, int nsb, in
     uint32_t db = (uint32_t)s[0] | ((uint32_t)s[1] << 8) | ((uint32_t)s[2] << 16) | ((uint32_t)s[3] << 24);
     d = __uint_as_float(db);
   }
-  *reinterpret_cast<uint4*>(t + canon_off(nn, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
-  *reinterpret_cast<uint4*>(t + canon_off(nn, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+  if (masked) {
+    uint8_t* t1 = t + NS * 32;  // the chunk's second tile: values 16..31
+    *reinterpret_cast<uint4*>(t + canon_off(nn, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(t + canon_off(nn, 1)) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(t1 + canon_off(nn, 0)) = make_uint4(0, 0, 0, 0);
+    *reinterpret_cast<uint4*>(t1 + canon_off(nn, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+  } else {
+    *reinterpret_cast<uint4*>(t + canon_off(nn, 0)) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(t + canon_off(nn, 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+  }
   xb[(((size_t)tg * nsb + b) * NS + nn) * 8 + c] = pair;
   if (c == 0) xd[((size_t)tg * nsb + b) * NS + nn] = d;
 }
@@ -543,10 +578,13 @@ cudaError_t launch_kq(const void* fn, dim3 grid, dim3 block, size_t smem, cudaSt
 
 }  // namespace
 
-int mma_kq_ns(int fmt) { return fmt == FMT_Q4K ? 64 : 32; }
+int mma_kq_ns(int fmt) {
+  (void)fmt;
+  return KNS;
+}
 
 cudaError_t mma_kq_act_run(const MmaKqActArgs& a, cudaStream_t s, bool pdl) {
-  if (a.K % 256 || (a.NS != 32 && a.NS != 64) || a.nt > a.NS * a.ntg) return cudaErrorInvalidValue;
+  if (a.K % 256 || a.NS != KNS || a.nt > a.NS * a.ntg) return cudaErrorInvalidValue;
   if ((size_t)a.K * 4 > 64 * 1024) return cudaErrorInvalidValue;
   if (cudaError_t e = ensure_smem_attr((const void*)k_mma_kq_act, 64 * 1024)) return e;
   MmaKqActArgs aa = a;
@@ -554,17 +592,17 @@ cudaError_t mma_kq_act_run(const MmaKqActArgs& a, cudaStream_t s, bool pdl) {
   return launch_kq((const void*)k_mma_kq_act, dim3(a.NS * a.ntg), dim3(256), (size_t)a.K * 4, s, pdl, args);
 }
 
-cudaError_t mma_kq_pack_run(const uint8_t* x, int nt, int K, int NS, int ntg, uint8_t* xq, float* xd, int* xb,
-                            cudaStream_t s) {
-  if (K % 256 || nt > NS * ntg) return cudaErrorInvalidValue;
+cudaError_t mma_kq_pack_run(const uint8_t* x, int nt, int K, int NS, int ntg, int masked, uint8_t* xq, float* xd,
+                            int* xb, cudaStream_t s) {
+  if (K % 256 || nt > NS * ntg || NS != KNS) return cudaErrorInvalidValue;
   const int nsb = K / 256;
   const int total = NS * ntg * nsb * 8;
-  k_mma_kq_pack<<<(total + 255) / 256, 256, 0, s>>>(x, nt, nsb, NS, ntg, xq, xd, xb);
+  k_mma_kq_pack<<<(total + 255) / 256, 256, 0, s>>>(x, nt, nsb, NS, ntg, masked, xq, xd, xb);
   return cudaGetLastError();
 }
 
 cudaError_t mma_kq_run(const MmaKqArgs& a, cudaStream_t s, bool pdl) {
-  if ((a.fmt != FMT_Q4K && a.fmt != FMT_Q6K) || a.K % 256 || a.NS != mma_kq_ns(a.fmt) || a.nseg < 1 || a.nseg > 3)
+  if ((a.fmt != FMT_Q4K && a.fmt != FMT_Q6K) || a.K % 256 || a.NS != KNS || a.nseg < 1 || a.nseg > 3)
     return cudaErrorInvalidValue;
   KqParams p{};
   int tiles = 0;
@@ -587,7 +625,6 @@ cudaError_t mma_kq_run(const MmaKqArgs& a, cudaStream_t s, bool pdl) {
   p.xd = a.xd;
   p.xb = a.xb;
   p.nt = a.nt;
-  p.NS = a.NS;
   p.ntg = a.ntg;
   p.epi = a.epi;
   p.scale = a.scale;
@@ -595,29 +632,29 @@ cudaError_t mma_kq_run(const MmaKqArgs& a, cudaStream_t s, bool pdl) {
   p.resid_ld = a.resid_ld;
   p.rs = a.rs;
   p.err = a.err;
-  const int na = a.fmt == FMT_Q4K ? 8 : 16;
-  // Stage layout: A tiles (1024-aligned) | raw rows | B tiles | row scales | dx | chunk sums.
+  const bool q4 = a.fmt == FMT_Q4K;
+  const int nst = q4 ? KqShape<FMT_Q4K>::NST : KqShape<FMT_Q6K>::NST;
+  const int nbt = q4 ? KqShape<FMT_Q4K>::NBT : KqShape<FMT_Q6K>::NBT;
+  const int nb = q4 ? KqShape<FMT_Q4K>::NB : KqShape<FMT_Q6K>::NB;
+  // Q4_K rows are 16-byte multiples (a super-block's bytes copy as they are);
+  // Q6_K super-blocks take a 16-byte aligned superset of up to 240 bytes.
+  p.raw_slot = q4 ? Q4K_BYTES : 240;
+  // Stage: A tiles (1024-aligned) | raw rows | B tiles. Then the scale ring and the barriers.
   size_t o = 0;
-  p.off_a = (int)o;
-  o += (size_t)na * TC_M * 32;
+  p.off_a = 0;
+  o += (size_t)8 * TC_M * 32;
   p.off_raw = (int)o;
-  o += (size_t)TC_M * RAW_SLOT;
+  o += (size_t)TC_M * p.raw_slot;
   o = (o + 127) & ~(size_t)127;
   p.off_b = (int)o;
-  o += (size_t)8 * a.NS * 32;
-  p.off_rmeta = (int)o;
-  o += a.fmt == FMT_Q4K ? (size_t)TC_M * (8 + 16) : (size_t)TC_M * (4 + 16);
-  o = (o + 15) & ~(size_t)15;
-  p.off_dx = (int)o;
-  o += (size_t)a.NS * 4;
-  p.off_xb = (int)o;
-  if (a.fmt == FMT_Q4K) o += (size_t)a.NS * 32;
+  o += (size_t)nbt * KNS * 32;
   o = (o + 1023) & ~(size_t)1023;
   p.stage_bytes = (int)o;
-  p.off_bar = (int)(o * NST);
-  const size_t smem = o * NST + (4 * NST + 1) * 8;
-  p.tmem_cols = 512;
-  const void* fn = a.fmt == FMT_Q4K ? (const void*)k_mma_kq<FMT_Q4K> : (const void*)k_mma_kq<FMT_Q6K>;
+  p.off_meta = (int)(o * nst);
+  const size_t meta_bytes = (size_t)NMR * (TC_M * RMETA + KNS * 36);
+  p.off_bar = (int)((p.off_meta + meta_bytes + 15) & ~(size_t)15);
+  const size_t smem = p.off_bar + (size_t)(4 * nst + nb + 2 * NMR) * 8;
+  const void* fn = q4 ? (const void*)k_mma_kq<FMT_Q4K> : (const void*)k_mma_kq<FMT_Q6K>;
   if (smem > 225 * 1024) return cudaErrorInvalidValue;
   if (cudaError_t e = ensure_smem_attr(fn, 225 * 1024)) return e;
   if (tiles == 0) return cudaSuccess;

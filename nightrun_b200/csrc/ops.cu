@@ -211,6 +211,28 @@ __global__ void k_swiglu(float* __restrict__ g, const float* __restrict__ u, siz
   g[i] = __fmul_rn(__fdiv_rn(x, __fadd_rn(1.0f, expf_cr(-x))), u[i]);
 }
 
+// Self-test of the bounded waits every pipelined kernel uses: one thread
+// waits on something nobody completes (kind 0: an mbarrier expecting two
+// arrivals that gets one; kind 1: a shared-memory flag nobody raises). The
+// wait gives up after limit_ns, the kernel records the bit its production
+// callers record and returns; nothing traps, the context stays usable.
+__global__ void k_wait_selftest(unsigned* err, unsigned long long limit_ns, int kind) {
+  __shared__ uint64_t bar;
+  __shared__ uint32_t flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 2);
+    flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_arrive(&bar);  // the second arrival is withheld
+  __syncwarp();
+  if (threadIdx.x == 1) {
+    const bool ok = kind == 0 ? mbar_wait(&bar, 0, limit_ns) : flag_wait_geq(&flag, 1, limit_ns);
+    if (!ok) atomicOr(err, kind == 0 ? ERR_WAIT_FULL : ERR_WAIT_EMPTY);
+  }
+}
+
 // Elementwise correctly rounded expf (checked against the CPU oracle bit for bit).
 __global__ void k_expf(const float* __restrict__ x, float* __restrict__ y, size_t n) {
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -302,6 +324,10 @@ cudaError_t op_softmax(float* x, size_t n, size_t rows, cudaStream_t s) {
 }
 cudaError_t op_swiglu(float* g, const float* u, size_t n, cudaStream_t s) {
   if (n) k_swiglu<<<blocks_for(n, 256), 256, 0, s>>>(g, u, n);
+  return cudaGetLastError();
+}
+cudaError_t op_wait_selftest(unsigned* err, unsigned long long limit_ns, int kind, cudaStream_t s) {
+  k_wait_selftest<<<1, 32, 0, s>>>(err, limit_ns, kind);
   return cudaGetLastError();
 }
 cudaError_t op_expf(const float* x, float* y, size_t n, cudaStream_t s) {

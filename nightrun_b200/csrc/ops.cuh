@@ -18,6 +18,7 @@ cudaError_t op_softmax(float* x, size_t n, size_t rows, cudaStream_t s);
 cudaError_t op_swiglu(float* g, const float* u, size_t n, cudaStream_t s);
 cudaError_t op_argmax(const float* x, size_t n, unsigned long long* key_scratch, uint32_t* out, cudaStream_t s);
 cudaError_t op_expf(const float* x, float* y, size_t n, cudaStream_t s);
+cudaError_t op_wait_selftest(unsigned* err, unsigned long long limit_ns, int kind, cudaStream_t s);
 cudaError_t op_expf_hash(unsigned long long* out, int chunk0, int nchunks, cudaStream_t s);
 
 // Position-dependent kernels of the forward pass. Positions are read from

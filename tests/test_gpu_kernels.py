@@ -356,3 +356,24 @@ def test_rope_bit_exact(K, orc, style, hd):
         t = dev(x)
         K.rope_apply(t, hd, freqs, pos, style)
         assert host_bytes(t) == orc.rope_apply(x, hd, ref_f, pos, style).tobytes()
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+def test_bounded_wait_expires_cleanly(K, orc, kind):
+    """A wait that can never be satisfied (an mbarrier arrival withheld, or a
+    flag nobody raises) gives up after its limit: the host gets NRC_ERR_DEVICE,
+    the error word is cleared, and the next kernels run correctly."""
+    import time
+    from nightrun_b200 import NrcError, lib
+    t0 = time.time()
+    rc = lib().nrc_wait_selftest(kind, 20_000_000, None)  # 20 ms
+    assert rc == -4, rc  # NRC_ERR_DEVICE
+    assert time.time() - t0 < 5.0
+    K.sync_check()  # cleared: no stale error
+    w = make_weights(orc, "q8_0", 64, 512, 5)
+    x = make_acts(orc, "q8_0", 512, 6)
+    got = gpu_matmul(K, "q8_0", w, x, 64, 512, 1)[0]
+    assert got.tobytes() == orc.matvec("q8_0", w, x, 64, 512).tobytes()
+    with pytest.raises(NrcError):
+        from nightrun_b200._lib import check
+        check(lib().nrc_wait_selftest(2, 1000, None))
