@@ -195,6 +195,20 @@ NRC_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
+// 16-byte asynchronous copy global -> shared through L2 (both addresses
+// 16-byte aligned). Many small copies per stage cost one LSU request each,
+// where one bulk copy per small span would queue behind the TMA unit.
+NRC_DEV void cp_async16(void* dst, const void* src, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "l"(policy)
+               : "memory");
+}
+// One arrival on `bar` once all of this thread's earlier cp.async copies
+// have landed (.noinc: the arrival is part of the barrier's expected count).
+NRC_DEV void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+NRC_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 // Fire-and-forget prefetch of [src, src + bytes) into L2 (both 16-byte
 // multiples); nothing waits for it.
 NRC_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {

@@ -38,6 +38,7 @@
 #include "expf_cr.cuh"
 #include "gemv.cuh"
 #include "seqsum.cuh"
+#include "tma.cuh"
 #include "units.cuh"
 
 namespace nrc {
@@ -627,14 +628,6 @@ struct LrParams {
 
 // 2-D tiled TMA load of one box into shared memory, completion counted on
 // `bar`. dst 128-byte aligned; x * 4 bytes a multiple of 16. No multicast.
-NRC_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
-      : "memory");
-}
-
 // The group's matrix and first row.
 NRC_DEV void lr_group(const LrParams& lp, int g, int& seg, int& row0) {
   seg = 0;
@@ -950,19 +943,6 @@ int occupancy(KernelFn fn, int smem, int smem_optin) {
 }
 
 // ------------------------------------------------------------- lane-per-row host
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  });
-  return fn;
-}
-
 // rows x (row_bytes / 8) u64 view of a Q8_0 matrix; box = `ops` octet columns
 // of 32 / ops rows (8704 bytes, the rows' octets back to back).
 bool encode_rows_map(CUtensorMap* m, const void* w, int rows, int row_bytes, int ops) {

@@ -34,6 +34,8 @@
 #include "mma.cuh"
 #include "seqsum.cuh"
 #include "tcgen05.cuh"
+#include "tma.cuh"
+#include "units.cuh"
 
 namespace nrc {
 namespace {
@@ -63,26 +65,36 @@ struct KqParams {
   int resid_ld;
   float rs;
   unsigned* err;
-  int off_a, off_raw, off_b, stage_bytes, off_meta, off_bar, raw_slot;
+  int rfull[3];  // rows of each matrix covered by its tensor map (a multiple of 8)
+  int off_a, off_raw, off_tail, off_b, off_xd, off_xb, stage_bytes, off_meta, off_bar;
+  CUtensorMap tmap[3];  // per matrix: dims {8 * row_bytes, rows / 8} (u8), box {BW, 16}
 };
 
 // Per format: MMAs (TMEM slots) per super-block, A tiles, B tiles, TMEM
-// buffers, pipeline stages.
+// buffers, pipeline stages, the width of a tensor-map box (the 16-byte
+// aligned window holding one super-block of a row: Q4_K super-blocks are
+// 16-byte aligned, a Q6_K one starts at an even offset) and of a raw slot
+// for rows copied by cp.async (up to 240 bytes for Q6_K).
 template <int FMT> struct KqShape {
   static constexpr int NA = FMT == FMT_Q4K ? 8 : 16;   // MMAs = TMEM slots per super-block
   static constexpr int NAT = 8;                        // A tiles: the 8 chunks of 32 values
   static constexpr int NBT = FMT == FMT_Q4K ? 8 : 16;  // B tiles (Q6_K: each chunk's two masked halves)
   static constexpr int NB = 512 / (NA * KNS);          // TMEM buffers (super-blocks in flight)
   static constexpr int NST = FMT == FMT_Q4K ? 3 : 2;   // smem stages
+  static constexpr int BW = FMT == FMT_Q4K ? Q4K_BYTES : 224;
+  static constexpr int RAW = FMT == FMT_Q4K ? Q4K_BYTES : 240;
 };
+
+// Byte q in [0, 63] -> int8 q - 32, four lanes at once (no borrow between bytes).
+NRC_DEV uint32_t q6_minus32(uint32_t q) { return ((q | 0x80808080u) - 0x20202020u) ^ 0x80808080u; }
 
 template <int FMT>
 __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqParams p) {
   using SH = KqShape<FMT>;
-  constexpr int NA = SH::NA, NB = SH::NB, NST = SH::NST;
+  constexpr int NA = SH::NA, NB = SH::NB, NST = SH::NST, RAW = SH::RAW, BW = SH::BW;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
-  uint64_t* full = bars;                  // producer -> repack (tx bytes)
+  uint64_t* full = bars;                  // producer -> repack (32 lane arrivals + tx bytes)
   uint64_t* aready = full + NST;          // repack -> MMA (A tiles, scales written)
   uint64_t* empty = aready + NST;         // MMA commit -> producer (stage consumed)
   uint64_t* mdone = empty + NST;          // MMA commit -> epilogue (the super-block's slots written)
@@ -101,10 +113,16 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
   const uint8_t* wend = wseg + (size_t)p.rows[sg] * p.row_bytes;
   const int nsb = p.nsb;
   const int bpb = FMT == FMT_Q4K ? Q4K_BYTES : Q6K_BYTES;
+  // Rows [row0, row0 + tma_rows) come through the tensor map: eight 2-D
+  // copies per super-block, copy j bringing rows j, j + 8, ... of the tile
+  // (consecutive 8-row groups are contiguous, 16-byte aligned spans, so any
+  // row length works). The matrix's last rows % 8 rows are copied by cp.async.
+  const int tma_rows = max(0, min(nrows, p.rfull[sg] - row0));
+  const int tail0 = row0 + tma_rows;  // first row (absolute) of the cp.async tail
 
   if (tid == 0) {
     for (int s = 0; s < NST; s++) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 32 + 1);
       mbar_init(&aready[s], REP_WARPS);
       mbar_init(&empty[s], 1);
       mbar_init(&mdone[s], 1);
@@ -140,13 +158,19 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
 
   if (warp == WPROD) {
     // ------------------------------------------------------------ producer
-    // Raw rows of each super-block (16-byte aligned supersets, one bulk copy
-    // per row; a matrix's ragged last bytes by plain loads) and the
-    // super-block's activation tiles; a stage is refilled as soon as its MMAs
-    // completed (the epilogue reads its scales from the scale ring).
+    // Per super-block: the eight tensor-map copies of the tile's rows (lane 0,
+    // one request per 16 rows), the tail rows as 16-byte cp.async copies
+    // (their ragged last bytes by plain loads), each lane's arrival on `full`
+    // once its copies landed, and the super-block's activation tiles, token
+    // scales and chunk sums as bulk copies. No multicast anywhere. A stage is
+    // refilled as soon as its MMAs completed (the epilogue reads its scales
+    // from the scale ring).
     const uint64_t pol = l2_evict_first();
     const uintptr_t wend_al = reinterpret_cast<uintptr_t>(wend) & ~(uintptr_t)15;
     const uint32_t b_bytes = (uint32_t)SH::NBT * KNS * 32;
+    const uint32_t tx_bytes = (tma_rows ? 8u * 16u * BW : 0u) + b_bytes + KNS * 4 + (FMT == FMT_Q4K ? KNS * 32 : 0);
+    constexpr int CH = RAW / 16;  // 16-byte chunks per tail slot
+    const int ntail = nrows - tma_rows;
     int st = 0;
     for (; st < nsb; st++) {
       const int s = st % NST, u = st / NST;
@@ -156,35 +180,44 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) fail(ERR_WAIT_EMPTY);
       }
-      if (abort_flag) break;
-      uint8_t* raw = st_base(s) + p.off_raw;
-      uint32_t mine = 0;
-      for (int r = lane; r < nrows; r += 32) {
-        const uintptr_t a = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
-        const uintptr_t lo = a & ~(uintptr_t)15;
-        uintptr_t hi = (a + bpb + 15) & ~(uintptr_t)15;
-        if (hi > wend_al) hi = wend_al > lo ? wend_al : lo;
-        mine += (uint32_t)(hi - lo);
-        for (uintptr_t b = hi > a ? hi : a; b < a + bpb; b++)
-          raw[r * p.raw_slot + (b - lo)] = *reinterpret_cast<const uint8_t*>(b);
+      if (__any_sync(0xffffffffu, abort_flag)) break;
+      const size_t sb_off = (size_t)st * bpb;
+      if (ntail) {
+        uint8_t* tail = st_base(s) + p.off_tail;
+        if (lane == 0) {
+          // Only the matrix's last row can end past its last 16-byte boundary.
+          const int t = ntail - 1;
+          const uintptr_t a = reinterpret_cast<uintptr_t>(wseg + (size_t)(tail0 + t) * p.row_bytes + sb_off);
+          const uintptr_t lo = a & ~(uintptr_t)15;
+          for (uintptr_t b = wend_al > a ? wend_al : a; b < a + bpb; b++)
+            tail[t * RAW + (b - lo)] = *reinterpret_cast<const uint8_t*>(b);
+        }
+        for (int i = lane; i < ntail * CH; i += 32) {
+          const int t = i / CH, c = i - t * CH;
+          const uintptr_t a = reinterpret_cast<uintptr_t>(wseg + (size_t)(tail0 + t) * p.row_bytes + sb_off);
+          const uintptr_t g = (a & ~(uintptr_t)15) + 16u * c;
+          if (g < a + bpb && g < wend_al) cp_async16(tail + t * RAW + 16 * c, reinterpret_cast<const void*>(g), pol);
+        }
       }
-      uint32_t total = mine;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-      __syncwarp();  // every lane's plain byte stores before lane 0's release arrive
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], total + b_bytes);
-      __syncwarp();
-      for (int r = lane; r < nrows; r += 32) {
-        const uintptr_t a = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
-        const uintptr_t lo = a & ~(uintptr_t)15;
-        uintptr_t hi = (a + bpb + 15) & ~(uintptr_t)15;
-        if (hi > wend_al) hi = wend_al > lo ? wend_al : lo;
-        if (hi > lo)
-          bulk_g2s(raw + r * p.raw_slot, reinterpret_cast<const void*>(lo), (uint32_t)(hi - lo), &full[s], pol);
+      __syncwarp();  // the plain byte stores before lane 0's release arrive
+      if (lane == 0) {
+        const size_t tix = (size_t)tg * nsb + st;
+        mbar_arrive_expect_tx(&full[s], tx_bytes);
+        if (tma_rows) {
+          uint8_t* raw = st_base(s) + p.off_raw;
+#pragma unroll 1
+          for (int j = 0; j < 8; j++) {
+            const int x = (int)(((size_t)j * p.row_bytes + sb_off) & ~(size_t)15);
+            tma_load_2d(raw + j * (16 * BW), &p.tmap[sg], x, row0 / 8, &full[s], pol);
+          }
+        }
+        bulk_g2s(st_base(s) + p.off_b, p.xq + tix * b_bytes, b_bytes, &full[s], 0ull);
+        bulk_g2s(st_base(s) + p.off_xd, p.xd + tix * KNS, KNS * 4, &full[s], 0ull);
+        if (FMT == FMT_Q4K) bulk_g2s(st_base(s) + p.off_xb, p.xb + tix * KNS * 8, KNS * 32, &full[s], 0ull);
       }
-      if (lane == 0)
-        bulk_g2s(st_base(s) + p.off_b, p.xq + ((size_t)tg * nsb + st) * b_bytes, b_bytes, &full[s], 0ull);
+      cp_async_arrive_noinc(&full[s]);
     }
+    cp_async_wait_all();
     if (lane == 0)
       for (int k = st - 1; k >= 0 && k >= st - NST; k--)
         if (!mbar_wait(&full[k % NST], (k / NST) & 1)) atomicOr(p.err, ERR_DRAIN);
@@ -200,8 +233,15 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
       uint8_t* a = st_base(s) + p.off_a;
       uint8_t* rm = meta(m) + r * RMETA;
       if (r < nrows) {
-        const uintptr_t ga = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
-        const uint8_t* b = st_base(s) + p.off_raw + r * p.raw_slot + (ga & 15);
+        const uint8_t* b;
+        if (r < tma_rows) {
+          // Copy j = r % 8, box row r / 8; the super-block at its offset in the box.
+          const size_t off = (size_t)(r & 7) * p.row_bytes + (size_t)st * bpb;
+          b = st_base(s) + p.off_raw + ((r & 7) * 16 + (r >> 3)) * BW + (off & 15);
+        } else {
+          const uintptr_t ga = reinterpret_cast<uintptr_t>(wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * bpb);
+          b = st_base(s) + p.off_tail + (r - tma_rows) * RAW + (ga & 15);
+        }
         if (FMT == FMT_Q4K) {
           // d, dmin (f16), 12 scale bytes (q4k_scale_min, kquant.rs:83-92), 128 bytes of nibbles.
           float* fm = reinterpret_cast<float*>(rm);
@@ -238,34 +278,36 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
                 (wv[4] >> 4) & 0x0F0F0F0Fu, (wv[5] >> 4) & 0x0F0F0F0Fu, (wv[6] >> 4) & 0x0F0F0F0Fu, (wv[7] >> 4) & 0x0F0F0F0Fu);
           }
         } else {
-          // ql[128], qh[64], scales[16] (int8), d (f16): value v = q - 32 in natural order.
+          // ql[128], qh[64], scales[16] (int8), d (f16): value v = q - 32 in natural
+          // order (kquant.rs:112-142). The super-block sits at an even offset: whole
+          // words are loaded and realigned by funnel shifts, four values per word.
+          uint32_t tl[5];
+          load_words_unaligned<5>(b + 192, tl);
           float* fm = reinterpret_cast<float*>(rm);
-          fm[0] = f16_to_f32((uint32_t)b[208] | ((uint32_t)b[209] << 8));
-          int8_t* scm = reinterpret_cast<int8_t*>(rm + 4);
+          fm[0] = f16_to_f32(tl[4] & 0xffffu);
+          uint32_t* scw = reinterpret_cast<uint32_t*>(rm + 4);
 #pragma unroll
-          for (int g = 0; g < 16; g++) scm[g] = (int8_t)b[192 + g];
+          for (int k = 0; k < 4; k++) scw[k] = tl[k];
 #pragma unroll
           for (int h = 0; h < 2; h++) {
-            const uint8_t* ql = b + 64 * h;
-            const uint8_t* qh = b + 128 + 32 * h;
+            uint32_t ql[16], qh[8];
+            load_words_unaligned<16>(b + 64 * h, ql);
+            load_words_unaligned<8>(b + 128 + 32 * h, qh);
+            // Values 128h + 32qd + l (l = 4k .. 4k+3): chunk 4h + qd, word k.
+            uint32_t o[4][8];
 #pragma unroll
-            for (int qd = 0; qd < 4; qd++) {  // quarter: values 128h + 32qd + l = chunk 4h + qd
-              uint32_t wv[8];
+            for (int k = 0; k < 8; k++) {
+              const uint32_t wl = ql[k], wl2 = ql[k + 8], wh = qh[k];
+              o[0][k] = q6_minus32((wl & 0x0F0F0F0Fu) | ((wh & 0x03030303u) << 4));
+              o[1][k] = q6_minus32((wl2 & 0x0F0F0F0Fu) | (((wh >> 2) & 0x03030303u) << 4));
+              o[2][k] = q6_minus32(((wl >> 4) & 0x0F0F0F0Fu) | (((wh >> 4) & 0x03030303u) << 4));
+              o[3][k] = q6_minus32(((wl2 >> 4) & 0x0F0F0F0Fu) | (((wh >> 6) & 0x03030303u) << 4));
+            }
 #pragma unroll
-              for (int k = 0; k < 8; k++) {
-                uint32_t word = 0;
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                  const int l = 4 * k + e;
-                  const uint32_t lq = qd & 1 ? ql[l + 32] : ql[l];
-                  const uint32_t q = ((qd < 2 ? (lq & 0x0F) : (lq >> 4)) | (((qh[l] >> (2 * qd)) & 3) << 4));
-                  word |= (uint32_t)(uint8_t)(int8_t)((int)q - 32) << (8 * e);
-                }
-                wv[k] = word;
-              }
+            for (int qd = 0; qd < 4; qd++) {
               uint8_t* t = a + (4 * h + qd) * (TC_M * 32);
-              *reinterpret_cast<uint4*>(t + canon_off(r, 0)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-              *reinterpret_cast<uint4*>(t + canon_off(r, 1)) = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+              *reinterpret_cast<uint4*>(t + canon_off(r, 0)) = make_uint4(o[qd][0], o[qd][1], o[qd][2], o[qd][3]);
+              *reinterpret_cast<uint4*>(t + canon_off(r, 1)) = make_uint4(o[qd][4], o[qd][5], o[qd][6], o[qd][7]);
             }
           }
         }
@@ -276,14 +318,13 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
           *reinterpret_cast<uint4*>(a + k * (TC_M * 32) + canon_off(r, 1)) = make_uint4(0, 0, 0, 0);
         }
       }
-      // The super-block's token scales (and Q4_K chunk sums) into the scale slot.
+      // The super-block's token scales (and Q4_K chunk sums), copied with the
+      // stage, into the scale slot.
       {
-        const size_t tix = (size_t)tg * nsb + st;
         float* dxs = reinterpret_cast<float*>(meta(m) + TC_M * RMETA);
-        int* xbs = reinterpret_cast<int*>(dxs + KNS);
-        if (r < KNS) dxs[r] = p.xd[tix * KNS + r];
-        if (FMT == FMT_Q4K)
-          for (int i = r; i < KNS * 8; i += TC_M) xbs[i] = p.xb[tix * KNS * 8 + i];
+        if (r < KNS) dxs[r] = reinterpret_cast<const float*>(st_base(s) + p.off_xd)[r];
+        if (FMT == FMT_Q4K && r < KNS * 2)
+          reinterpret_cast<int4*>(dxs + KNS)[r] = reinterpret_cast<const int4*>(st_base(s) + p.off_xb)[r];
       }
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
       __syncwarp();
@@ -329,6 +370,11 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    // Every dot is an integer below 2^17 in magnitude and every scale an
+    // integer below 2^7 (Q4_K: |dot| <= 32*15*128, sc <= 63; Q6_K: |dot| <=
+    // 16*32*128, |sc| <= 128), so f32(sc) * f32(dot) is exact (< 2^24) and
+    // fma(f32(dot), f32(sc), sum) rounds exactly like the reference's
+    // `sum += sc as f32 * dot as f32`; two tokens per packed FMA.
     const int q = warp & 3, half = warp >> 2;
     const int r = q * 32 + lane;  // TMEM lane = weight row
     const int n0 = half * 16;     // this warp's 16 tokens
@@ -355,21 +401,23 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
         const float* fm = reinterpret_cast<const float*>(rm);
         d = fm[0];
         dmin = fm[1];
+        const uint2 sw = *reinterpret_cast<const uint2*>(rm + 8), mw = *reinterpret_cast<const uint2*>(rm + 16);
 #pragma unroll
         for (int j = 0; j < 8; j++) {
-          scf[j] = (float)rm[8 + j];
-          mj[j] = rm[16 + j];
+          scf[j] = (float)(((j < 4 ? sw.x : sw.y) >> (8 * (j & 3))) & 0xffu);
+          mj[j] = (int)(((j < 4 ? mw.x : mw.y) >> (8 * (j & 3))) & 0xffu);
         }
       } else {
         d = reinterpret_cast<const float*>(rm)[0];
-        const int8_t* scm = reinterpret_cast<const int8_t*>(rm + 4);
+        const uint32_t* sw = reinterpret_cast<const uint32_t*>(rm + 4);  // 4-byte aligned
+        const uint32_t sws[4] = {sw[0], sw[1], sw[2], sw[3]};
 #pragma unroll
-        for (int g = 0; g < NA; g++) scf[g] = (float)scm[g];
+        for (int g = 0; g < NA; g++) scf[g] = (float)(int)(int8_t)(sws[g >> 2] >> (8 * (g & 3)));
       }
       const uint32_t slot0 = lane_base + (uint32_t)(bf * NA * KNS + n0);
-      float sq[16];
+      float2 sq[8];
 #pragma unroll
-      for (int i = 0; i < 16; i++) sq[i] = 0.0f;
+      for (int i = 0; i < 8; i++) sq[i] = make_float2(0.0f, 0.0f);
       // Two slots per TMEM round trip; each slot's dots in slot order.
 #pragma unroll
       for (int k = 0; k < NA; k += 2) {
@@ -377,10 +425,11 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
         tc_ld16(slot0 + (uint32_t)(k * KNS), v0);
         tc_ld16(slot0 + (uint32_t)((k + 1) * KNS), v1);
         tc_wait_ld();
+        const float2 s0 = make_float2(scf[k], scf[k]), s1 = make_float2(scf[k + 1], scf[k + 1]);
 #pragma unroll
-        for (int i = 0; i < 16; i++) sq[i] = __fadd_rn(sq[i], __fmul_rn(scf[k], i2f((int)v0[i])));
+        for (int i = 0; i < 8; i++) sq[i] = __ffma2_rn(small_i2f2(v0[2 * i], v0[2 * i + 1]), s0, sq[i]);
 #pragma unroll
-        for (int i = 0; i < 16; i++) sq[i] = __fadd_rn(sq[i], __fmul_rn(scf[k + 1], i2f((int)v1[i])));
+        for (int i = 0; i < 8; i++) sq[i] = __ffma2_rn(small_i2f2(v1[2 * i], v1[2 * i + 1]), s1, sq[i]);
       }
       // TMEM buffer drained: hand it back before the scalar tail.
       tc_fence_before();
@@ -390,14 +439,16 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
       for (int i = 0; i < 16; i++) {
         const int n = n0 + i;
         const float dx = dxs[n];
+        const float sqi = (i & 1) ? sq[i >> 1].y : sq[i >> 1].x;
         float t;
         if (FMT == FMT_Q4K) {
-          int sm = 0;
-#pragma unroll
-          for (int j = 0; j < 8; j++) sm += mj[j] * xbs[n * 8 + j];
-          t = __fsub_rn(__fmul_rn(__fmul_rn(d, dx), sq[i]), __fmul_rn(__fmul_rn(dmin, dx), i2f(sm)));
+          const int4 xa = reinterpret_cast<const int4*>(xbs + n * 8)[0];
+          const int4 xc = reinterpret_cast<const int4*>(xbs + n * 8)[1];
+          const int sm = mj[0] * xa.x + mj[1] * xa.y + mj[2] * xa.z + mj[3] * xa.w + mj[4] * xc.x + mj[5] * xc.y +
+                         mj[6] * xc.z + mj[7] * xc.w;  // |sm| <= 8*63*4096 < 2^22
+          t = __fsub_rn(__fmul_rn(__fmul_rn(d, dx), sqi), __fmul_rn(__fmul_rn(dmin, dx), small_i2f((uint32_t)sm)));
         } else {
-          t = __fmul_rn(__fmul_rn(d, dx), sq[i]);
+          t = __fmul_rn(__fmul_rn(d, dx), sqi);
         }
         acc[i] = __fadd_rn(acc[i], t);
       }
@@ -633,21 +684,43 @@ cudaError_t mma_kq_run(const MmaKqArgs& a, cudaStream_t s, bool pdl) {
   p.rs = a.rs;
   p.err = a.err;
   const bool q4 = a.fmt == FMT_Q4K;
+  for (int i = 0; i < a.nseg; i++) {
+    // 8-row groups of the matrix as rows of a 2-D u8 tensor (stride 8 * row_bytes,
+    // a multiple of 16 for both formats); a box is one super-block window of 16 groups.
+    p.rfull[i] = a.seg[i].rows / 8 * 8;
+    if (p.rfull[i] == 0) continue;
+    auto enc = tensor_map_encoder();
+    if (!enc) return cudaErrorNotSupported;
+    const cuuint64_t dims[2] = {(cuuint64_t)8 * p.row_bytes, (cuuint64_t)(a.seg[i].rows / 8)};
+    const cuuint64_t strides[1] = {(cuuint64_t)8 * p.row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)(q4 ? KqShape<FMT_Q4K>::BW : KqShape<FMT_Q6K>::BW), 16};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&p.tmap[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(a.seg[i].w), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
   const int nst = q4 ? KqShape<FMT_Q4K>::NST : KqShape<FMT_Q6K>::NST;
   const int nbt = q4 ? KqShape<FMT_Q4K>::NBT : KqShape<FMT_Q6K>::NBT;
   const int nb = q4 ? KqShape<FMT_Q4K>::NB : KqShape<FMT_Q6K>::NB;
-  // Q4_K rows are 16-byte multiples (a super-block's bytes copy as they are);
-  // Q6_K super-blocks take a 16-byte aligned superset of up to 240 bytes.
-  p.raw_slot = q4 ? Q4K_BYTES : 240;
-  // Stage: A tiles (1024-aligned) | raw rows | B tiles. Then the scale ring and the barriers.
+  // Stage: A tiles (1024-aligned) | raw rows | B tiles | token scales | chunk
+  // sums. Then the scale ring and the barriers.
+  const int raw_slot = q4 ? KqShape<FMT_Q4K>::RAW : KqShape<FMT_Q6K>::RAW;
+  const int bw = q4 ? KqShape<FMT_Q4K>::BW : KqShape<FMT_Q6K>::BW;
   size_t o = 0;
   p.off_a = 0;
   o += (size_t)8 * TC_M * 32;
-  p.off_raw = (int)o;
-  o += (size_t)TC_M * p.raw_slot;
+  p.off_raw = (int)o;  // 128-byte aligned, as every box (16 x bw bytes, bw * 16 % 128 == 0)
+  o += (size_t)8 * 16 * bw;
+  p.off_tail = (int)o;
+  o += (size_t)8 * raw_slot;
   o = (o + 127) & ~(size_t)127;
   p.off_b = (int)o;
   o += (size_t)nbt * KNS * 32;
+  p.off_xd = (int)o;
+  o += (size_t)KNS * 4;
+  p.off_xb = (int)o;
+  o += (size_t)KNS * 32;
   o = (o + 1023) & ~(size_t)1023;
   p.stage_bytes = (int)o;
   p.off_meta = (int)(o * nst);

@@ -9,6 +9,16 @@ namespace nrc {
 
 constexpr int TC_M = 128;  // rows per MMA tile
 
+// int32 -> f32 for |v| < 2^22 in two full-rate operations: the bits of
+// 1.5 * 2^23 + v are that float exactly, and subtracting 1.5 * 2^23 is exact.
+constexpr uint32_t TC_MAGIC_BITS = 0x4B400000u;
+constexpr float TC_MAGIC_F = 12582912.0f;
+NRC_DEV float small_i2f(uint32_t v) { return __fsub_rn(__uint_as_float(v + TC_MAGIC_BITS), TC_MAGIC_F); }
+NRC_DEV float2 small_i2f2(uint32_t a, uint32_t b) {
+  return __fadd2_rn(make_float2(__uint_as_float(a + TC_MAGIC_BITS), __uint_as_float(b + TC_MAGIC_BITS)),
+                    make_float2(-TC_MAGIC_F, -TC_MAGIC_F));
+}
+
 NRC_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 NRC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 NRC_DEV void tc_commit(uint64_t* bar) {

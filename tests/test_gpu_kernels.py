@@ -201,6 +201,26 @@ def test_matmul_q8_tensor_core_bit_exact(K, orc, shape, batch):
                              f"max diff {np.nanmax(np.abs(got - ref))}")
 
 
+@pytest.mark.parametrize("fmt", ["q4k", "q6k"])
+@pytest.mark.parametrize("shape", [(5, 256), (37, 512), (133, 2560), (300, 3072), (128, 9728), (1000, 2048)])
+@pytest.mark.parametrize("batch", [9, 33, 70])
+def test_matmul_kquant_tensor_core_bit_exact(K, orc, fmt, shape, batch):
+    """K-quant weights with more than 8 tokens run on tcgen05 (one kind::i8
+    MMA per 32-value sub-block, Q6_K as masked 16-value halves). Rows come in
+    8-row groups through a 2-D tensor map and the last rows % 8 by cp.async,
+    so the shapes cover fewer than 8 rows, ragged tails, several 128-row tiles
+    and super-block counts whose rows are not 16-byte multiples (Q6_K 10, 12,
+    38 per row)."""
+    rows, cols = shape
+    w = make_weights(orc, fmt, rows, cols, 70 + rows + batch, adversarial=(batch % 2 == 1))
+    xs = make_acts(orc, fmt, cols, 71 + batch, batch)
+    ref = orc.matmul(fmt, w, xs, rows, cols, batch)
+    got = gpu_matmul(K, fmt, w, xs, rows, cols, batch)
+    if got.tobytes() != ref.tobytes():
+        bad = np.argwhere(got.view(np.uint32) != ref.view(np.uint32))
+        raise AssertionError(f"{fmt} {rows}x{cols} b{batch}: {len(bad)} differ, first {bad[:4].tolist()}")
+
+
 @pytest.mark.parametrize("fmt", ["q8_0", "q4k", "q6k"])
 @pytest.mark.parametrize("offset", [2, 4, 6, 8, 14])
 def test_matvec_unaligned_weights(K, orc, fmt, offset):
