@@ -14,8 +14,9 @@
 //              slot, exact scaling, running f32 sums in registers;
 //   warps 4-7  repack: raw Q8_0 rows (TMA-staged) -> UMMA K-major canonical
 //              int8 tiles + f32 row scales;
-//   warp 8     producer: 1-D bulk copies of raw weight rows, activation tiles
-//              and activation scales into a 2-stage ring (no multicast);
+//   warp 8     producer: per stage one 2-D tensor copy of the tile's raw
+//              weight rows (128 rows x 8 blocks) and bulk copies of the
+//              activation tiles and scales, into a 2-stage ring (no multicast);
 //   warp 9     TMEM allocator and single-thread MMA issuer.
 // Every mbarrier wait is bounded (error word + clean exit, never a trap).
 #include <algorithm>
@@ -25,6 +26,7 @@
 #include "mma.cuh"
 #include "seqsum.cuh"
 #include "tcgen05.cuh"
+#include "tma.cuh"
 
 namespace nrc {
 namespace {
@@ -58,6 +60,7 @@ struct Params {
   unsigned* err;
   int off_raw, off_a, off_b, off_dw, off_dx, off_bar, stage_bytes;
   uint32_t tmem_cols;
+  CUtensorMap tmap[3];  // per matrix: dims {row_bytes / 2, rows} (u16), box {KB * 34 / 2, TM}
 };
 
 template <int NS>
@@ -77,7 +80,6 @@ __global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Para
   while (sg + 1 < p.nseg && tile >= p.tile_start[sg + 1]) sg++;
   const int row0 = (tile - p.tile_start[sg]) * TM;
   const int nrows = min(TM, p.rows[sg] - row0);
-  const uint8_t* wseg = p.w[sg];
   const int nstages = p.bpr / KB;
 
   if (tid == 0) {
@@ -121,7 +123,7 @@ __global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Para
   if (warp == WP) {
     // ------------------------------------------------------------ producer
     const uint64_t pol = l2_evict_first();
-    const uint32_t raw_bytes = (uint32_t)nrows * KB * 34;
+    const uint32_t raw_bytes = (uint32_t)TM * KB * 34;  // whole box: rows past the matrix read as zero
     const uint32_t b_bytes = (uint32_t)KB * NS * 32;
     const uint32_t dx_bytes = (uint32_t)KB * NS * 4;
     int st = 0;
@@ -133,14 +135,11 @@ __global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Para
         ok = __shfl_sync(0xffffffffu, ok, 0);
         if (!ok) fail(ERR_WAIT_EMPTY);
       }
-      if (abort_flag) break;
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], raw_bytes + b_bytes + dx_bytes);
-      __syncwarp();
-      for (int r = lane; r < nrows; r += 32) {
-        const uint8_t* src = wseg + (size_t)(row0 + r) * p.row_bytes + (size_t)st * KB * 34;
-        bulk_g2s(st_raw(s) + r * KB * 34, src, KB * 34, &full[s], pol);
-      }
+      if (__any_sync(0xffffffffu, abort_flag)) break;
       if (lane == 0) {
+        mbar_arrive_expect_tx(&full[s], raw_bytes + b_bytes + dx_bytes);
+        // x = st * 272 bytes: a multiple of 16, as a tensor copy needs.
+        tma_load_2d(st_raw(s), &p.tmap[sg], st * (KB * 34 / 2), row0, &full[s], pol);
         const size_t tile = ((size_t)tg * p.bpr + (size_t)st * KB);
         bulk_g2s(st_b(s), p.xq + tile * NS * 32, b_bytes, &full[s], 0ull);
         bulk_g2s(st_dx(s), p.xd + tile * NS, dx_bytes, &full[s], 0ull);
@@ -477,7 +476,21 @@ cudaError_t mma_q8_run(const MmaArgs& a, cudaStream_t s, bool pdl) {
   p.resid_ld = a.resid_ld;
   p.rs = a.rs;
   p.err = a.err;
-  // Stage layout: A canonical (1024-aligned) | raw rows | B | dw | dx.
+  auto enc = tensor_map_encoder();
+  if (!enc) return cudaErrorNotSupported;
+  for (int i = 0; i < a.nseg; i++) {
+    // rows x (row_bytes / 2) u16 view (row_bytes = 272 * K / 256, a multiple of 16).
+    const cuuint64_t dims[2] = {(cuuint64_t)(p.row_bytes / 2), (cuuint64_t)a.seg[i].rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)p.row_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)(KB * 34 / 2), (cuuint32_t)TM};
+    const cuuint32_t estr[2] = {1, 1};
+    if (a.seg[i].rows > 0 &&
+        enc(&p.tmap[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(a.seg[i].w), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  // Stage layout: A canonical (1024-aligned) | raw rows (128-aligned) | B | dw | dx.
   size_t o = 0;
   p.off_a = (int)o;
   o += (size_t)KB * TM * 32;

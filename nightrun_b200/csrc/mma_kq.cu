@@ -71,17 +71,18 @@ struct KqParams {
 };
 
 // Per format: MMAs (TMEM slots) per super-block, A tiles, B tiles, TMEM
-// buffers, pipeline stages, the width of a tensor-map box (the 16-byte
-// aligned window holding one super-block of a row: Q4_K super-blocks are
-// 16-byte aligned, a Q6_K one starts at an even offset) and of a raw slot
-// for rows copied by cp.async (up to 240 bytes for Q6_K).
+// buffers, pipeline stages, the width of a tensor-map box (a 16-byte aligned
+// window holding one super-block of a row: Q4_K super-blocks are 16-byte
+// aligned, a Q6_K one starts at an even offset; both widths are an odd
+// number of 16-byte units, so rows 8 apart land in different bank groups)
+// and of a raw slot for rows copied by cp.async (up to 240 bytes for Q6_K).
 template <int FMT> struct KqShape {
   static constexpr int NA = FMT == FMT_Q4K ? 8 : 16;   // MMAs = TMEM slots per super-block
   static constexpr int NAT = 8;                        // A tiles: the 8 chunks of 32 values
   static constexpr int NBT = FMT == FMT_Q4K ? 8 : 16;  // B tiles (Q6_K: each chunk's two masked halves)
   static constexpr int NB = 512 / (NA * KNS);          // TMEM buffers (super-blocks in flight)
   static constexpr int NST = FMT == FMT_Q4K ? 3 : 2;   // smem stages
-  static constexpr int BW = FMT == FMT_Q4K ? Q4K_BYTES : 224;
+  static constexpr int BW = FMT == FMT_Q4K ? Q4K_BYTES : 240;
   static constexpr int RAW = FMT == FMT_Q4K ? Q4K_BYTES : 240;
 };
 
@@ -223,7 +224,11 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
         if (!mbar_wait(&full[k % NST], (k / NST) & 1)) atomicOr(p.err, ERR_DRAIN);
   } else if (warp >= WREP && warp < WREP + REP_WARPS) {
     // -------------------------------------------------------------- repack
-    const int r = tid - WREP * 32;  // weight row of this thread
+    // Weight row of this thread: r = 8g + j with, in every 8 consecutive lanes,
+    // eight different 8-row groups g (their box rows sit in different bank
+    // groups) and eight different j (their canonical-tile rows do too).
+    const int rw = warp - WREP, ri = lane & 7, rq = lane >> 3;
+    const int r = 8 * (ri + 8 * (rw & 1)) + ((ri + rq + 4 * (rw >> 1)) & 7);
     for (int st = 0; st < nsb; st++) {
       const int s = st % NST, u = st / NST, m = st % NMR;
       if (abort_flag || !mbar_wait(&full[s], u & 1) || (st >= NMR && !mbar_wait(&mfree[m], ((st / NMR) - 1) & 1))) {
@@ -293,21 +298,24 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
             uint32_t ql[16], qh[8];
             load_words_unaligned<16>(b + 64 * h, ql);
             load_words_unaligned<8>(b + 128 + 32 * h, qh);
-            // Values 128h + 32qd + l (l = 4k .. 4k+3): chunk 4h + qd, word k.
-            uint32_t o[4][8];
+            // Values 128h + 32qd + l (l = 4k .. 4k+3): chunk 4h + qd, word k;
+            // words 0-3 of each chunk, then words 4-7 (one 16-byte half each).
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
-              const uint32_t wl = ql[k], wl2 = ql[k + 8], wh = qh[k];
-              o[0][k] = q6_minus32((wl & 0x0F0F0F0Fu) | ((wh & 0x03030303u) << 4));
-              o[1][k] = q6_minus32((wl2 & 0x0F0F0F0Fu) | (((wh >> 2) & 0x03030303u) << 4));
-              o[2][k] = q6_minus32(((wl >> 4) & 0x0F0F0F0Fu) | (((wh >> 4) & 0x03030303u) << 4));
-              o[3][k] = q6_minus32(((wl2 >> 4) & 0x0F0F0F0Fu) | (((wh >> 6) & 0x03030303u) << 4));
-            }
+            for (int c = 0; c < 2; c++) {
+              uint32_t o[4][4];
 #pragma unroll
-            for (int qd = 0; qd < 4; qd++) {
-              uint8_t* t = a + (4 * h + qd) * (TC_M * 32);
-              *reinterpret_cast<uint4*>(t + canon_off(r, 0)) = make_uint4(o[qd][0], o[qd][1], o[qd][2], o[qd][3]);
-              *reinterpret_cast<uint4*>(t + canon_off(r, 1)) = make_uint4(o[qd][4], o[qd][5], o[qd][6], o[qd][7]);
+              for (int kk = 0; kk < 4; kk++) {
+                const int k = 4 * c + kk;
+                const uint32_t wl = ql[k], wl2 = ql[k + 8], wh = qh[k];
+                o[0][kk] = q6_minus32((wl & 0x0F0F0F0Fu) | ((wh & 0x03030303u) << 4));
+                o[1][kk] = q6_minus32((wl2 & 0x0F0F0F0Fu) | (((wh >> 2) & 0x03030303u) << 4));
+                o[2][kk] = q6_minus32(((wl >> 4) & 0x0F0F0F0Fu) | (((wh >> 4) & 0x03030303u) << 4));
+                o[3][kk] = q6_minus32(((wl2 >> 4) & 0x0F0F0F0Fu) | (((wh >> 6) & 0x03030303u) << 4));
+              }
+#pragma unroll
+              for (int qd = 0; qd < 4; qd++)
+                *reinterpret_cast<uint4*>(a + (4 * h + qd) * (TC_M * 32) + canon_off(r, c)) =
+                    make_uint4(o[qd][0], o[qd][1], o[qd][2], o[qd][3]);
             }
           }
         }
@@ -319,12 +327,24 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
         }
       }
       // The super-block's token scales (and Q4_K chunk sums), copied with the
-      // stage, into the scale slot.
-      {
+      // stage, into the scale slot. A chunk sum s (|s| <= 4096) is kept as the
+      // bytes lo = s & 255 (unsigned) and hi = s >> 8 (signed), s = lo + 256 hi,
+      // so the epilogue forms sum_j m_j * s_j with four dp4a.
+      if (r < KNS) {
         float* dxs = reinterpret_cast<float*>(meta(m) + TC_M * RMETA);
-        if (r < KNS) dxs[r] = reinterpret_cast<const float*>(st_base(s) + p.off_xd)[r];
-        if (FMT == FMT_Q4K && r < KNS * 2)
-          reinterpret_cast<int4*>(dxs + KNS)[r] = reinterpret_cast<const int4*>(st_base(s) + p.off_xb)[r];
+        dxs[r] = reinterpret_cast<const float*>(st_base(s) + p.off_xd)[r];
+        if (FMT == FMT_Q4K) {
+          const int4* xs = reinterpret_cast<const int4*>(st_base(s) + p.off_xb) + 2 * r;
+          const int4 a0 = xs[0], a1 = xs[1];
+          const int v[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+          uint32_t lo[2] = {0, 0}, hi[2] = {0, 0};
+#pragma unroll
+          for (int j = 0; j < 8; j++) {
+            lo[j >> 2] |= (uint32_t)(v[j] & 255) << (8 * (j & 3));
+            hi[j >> 2] |= (uint32_t)((v[j] >> 8) & 255) << (8 * (j & 3));
+          }
+          reinterpret_cast<uint4*>(dxs + KNS)[r] = make_uint4(lo[0], lo[1], hi[0], hi[1]);
+        }
       }
       fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
       __syncwarp();
@@ -344,8 +364,8 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
           fail(ERR_WAIT_FULL);
           break;
         }
-        // The TMEM buffer drained by the epilogue (super-block st - NB).
-        if (st >= NB && !mbar_wait(&tfree[bf], ((st / NB) - 1) & 1)) {
+        // The TMEM buffer drained and preset by the epilogue (first use: preset only).
+        if (!mbar_wait(&tfree[bf], (st / NB) & 1)) {
           fail(ERR_WAIT_EMPTY);
           break;
         }
@@ -358,7 +378,7 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
           const int at = FMT == FMT_Q4K ? k : k / 2;  // Q6_K: group k = half (k % 2) of chunk k / 2
           const uint64_t ad = smem_desc(a + at * (TC_M * 32), 128, 256);
           const uint64_t bd = smem_desc(bt + k * (KNS * 32), 128, 256);
-          tc_mma_i8(dbase + (uint32_t)(k * KNS), ad, bd, idesc, 0u);
+          tc_mma_i8(dbase + (uint32_t)(k * KNS), ad, bd, idesc, 1u);  // onto the preset cell
         }
         tc_commit(&mdone[s]);
         tc_commit(&empty[s]);
@@ -370,18 +390,31 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    // Every dot is an integer below 2^17 in magnitude and every scale an
-    // integer below 2^7 (Q4_K: |dot| <= 32*15*128, sc <= 63; Q6_K: |dot| <=
-    // 16*32*128, |sc| <= 128), so f32(sc) * f32(dot) is exact (< 2^24) and
-    // fma(f32(dot), f32(sc), sum) rounds exactly like the reference's
-    // `sum += sc as f32 * dot as f32`; two tokens per packed FMA.
+    // Every TMEM cell is preset to the bits of 1.5 * 2^23 before its MMA adds
+    // the dot onto it, so a cell holds the float 1.5 * 2^23 + dot exactly
+    // (|dot| < 2^17) and one subtraction recovers f32(dot). Every dot is an
+    // integer below 2^17 in magnitude and every scale an integer below 2^7
+    // (Q4_K: |dot| <= 32*15*128, sc <= 63; Q6_K: |dot| <= 16*32*128, |sc| <=
+    // 128), so f32(sc) * f32(dot) is exact (< 2^24) and fma(f32(dot), f32(sc),
+    // sum) rounds exactly like the reference's `sum += sc as f32 * dot as f32`;
+    // two tokens per packed operation throughout.
     const int q = warp & 3, half = warp >> 2;
     const int r = q * 32 + lane;  // TMEM lane = weight row
     const int n0 = half * 16;     // this warp's 16 tokens
-    float acc[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) acc[i] = 0.0f;
     const uint32_t lane_base = tbase + ((uint32_t)(q * 32) << 16);
+    const float2 mneg = make_float2(-TC_MAGIC_F, -TC_MAGIC_F);
+    auto preset_buffer = [&](int bf) {
+#pragma unroll
+      for (int k = 0; k < NA; k++) tc_st16_fill(lane_base + (uint32_t)(bf * NA * KNS + k * KNS + n0), TC_MAGIC_BITS);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tfree[bf]);
+    };
+    for (int b = 0; b < NB; b++) preset_buffer(b);
+    float2 acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
     for (int st = 0; st < nsb && !abort_flag; st++) {
       const int s = st % NST, u = st / NST, bf = st % NB, m = st % NMR;
       // mdone and mready complete at most one phase ahead of this warp: their
@@ -391,66 +424,88 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
         break;
       }
       tc_fence_after();
+      const uint32_t slot0 = lane_base + (uint32_t)(bf * NA * KNS + n0);
+      uint32_t va[32], vb[32];
+      tc_ld16(slot0, va);
+      tc_ld16(slot0 + (uint32_t)KNS, va + 16);
       const uint8_t* rm = meta(m) + r * RMETA;
       const float* dxs = reinterpret_cast<const float*>(meta(m) + TC_M * RMETA);
-      const int* xbs = reinterpret_cast<const int*>(dxs + KNS);
-      float scf[NA];
+      const uint4* lohi = reinterpret_cast<const uint4*>(dxs + KNS);
+      // Row scales: Q4_K d, dmin, sc[8] (u8), m[8] (u8); Q6_K d, sc[16] (i8),
+      // kept packed and widened per slot.
       float d, dmin = 0.0f;
-      int mj[8];
+      uint2 mw = make_uint2(0, 0);
+      uint32_t sws[4];
       if (FMT == FMT_Q4K) {
         const float* fm = reinterpret_cast<const float*>(rm);
         d = fm[0];
         dmin = fm[1];
-        const uint2 sw = *reinterpret_cast<const uint2*>(rm + 8), mw = *reinterpret_cast<const uint2*>(rm + 16);
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-          scf[j] = (float)(((j < 4 ? sw.x : sw.y) >> (8 * (j & 3))) & 0xffu);
-          mj[j] = (int)(((j < 4 ? mw.x : mw.y) >> (8 * (j & 3))) & 0xffu);
-        }
+        const uint2 sw = *reinterpret_cast<const uint2*>(rm + 8);
+        mw = *reinterpret_cast<const uint2*>(rm + 16);
+        sws[0] = sw.x;
+        sws[1] = sw.y;
       } else {
         d = reinterpret_cast<const float*>(rm)[0];
         const uint32_t* sw = reinterpret_cast<const uint32_t*>(rm + 4);  // 4-byte aligned
-        const uint32_t sws[4] = {sw[0], sw[1], sw[2], sw[3]};
 #pragma unroll
-        for (int g = 0; g < NA; g++) scf[g] = (float)(int)(int8_t)(sws[g >> 2] >> (8 * (g & 3)));
+        for (int k = 0; k < 4; k++) sws[k] = sw[k];
       }
-      const uint32_t slot0 = lane_base + (uint32_t)(bf * NA * KNS + n0);
+      auto scale_of = [&](int k) {
+        const uint32_t b = (sws[k >> 2] >> (8 * (k & 3))) & 0xffu;
+        return FMT == FMT_Q4K ? (float)b : (float)(int)(int8_t)b;
+      };
+      tc_wait_ld_regs<32>(va);
       float2 sq[8];
 #pragma unroll
       for (int i = 0; i < 8; i++) sq[i] = make_float2(0.0f, 0.0f);
-      // Two slots per TMEM round trip; each slot's dots in slot order.
+      // Two slots per TMEM round trip, the next pair's loads in flight while
+      // this pair is scaled; each slot's dots in slot order.
 #pragma unroll
       for (int k = 0; k < NA; k += 2) {
-        uint32_t v0[16], v1[16];
-        tc_ld16(slot0 + (uint32_t)(k * KNS), v0);
-        tc_ld16(slot0 + (uint32_t)((k + 1) * KNS), v1);
-        tc_wait_ld();
-        const float2 s0 = make_float2(scf[k], scf[k]), s1 = make_float2(scf[k + 1], scf[k + 1]);
-#pragma unroll
-        for (int i = 0; i < 8; i++) sq[i] = __ffma2_rn(small_i2f2(v0[2 * i], v0[2 * i + 1]), s0, sq[i]);
-#pragma unroll
-        for (int i = 0; i < 8; i++) sq[i] = __ffma2_rn(small_i2f2(v1[2 * i], v1[2 * i + 1]), s1, sq[i]);
-      }
-      // TMEM buffer drained: hand it back before the scalar tail.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tfree[bf]);
-#pragma unroll
-      for (int i = 0; i < 16; i++) {
-        const int n = n0 + i;
-        const float dx = dxs[n];
-        const float sqi = (i & 1) ? sq[i >> 1].y : sq[i >> 1].x;
-        float t;
-        if (FMT == FMT_Q4K) {
-          const int4 xa = reinterpret_cast<const int4*>(xbs + n * 8)[0];
-          const int4 xc = reinterpret_cast<const int4*>(xbs + n * 8)[1];
-          const int sm = mj[0] * xa.x + mj[1] * xa.y + mj[2] * xa.z + mj[3] * xa.w + mj[4] * xc.x + mj[5] * xc.y +
-                         mj[6] * xc.z + mj[7] * xc.w;  // |sm| <= 8*63*4096 < 2^22
-          t = __fsub_rn(__fmul_rn(__fmul_rn(d, dx), sqi), __fmul_rn(__fmul_rn(dmin, dx), small_i2f((uint32_t)sm)));
-        } else {
-          t = __fmul_rn(__fmul_rn(d, dx), sqi);
+        uint32_t* cur = ((k >> 1) & 1) ? vb : va;
+        uint32_t* nxt = ((k >> 1) & 1) ? va : vb;
+        if (k + 2 < NA) {
+          tc_ld16(slot0 + (uint32_t)((k + 2) * KNS), nxt);
+          tc_ld16(slot0 + (uint32_t)((k + 3) * KNS), nxt + 16);
         }
-        acc[i] = __fadd_rn(acc[i], t);
+        const float sc0 = scale_of(k), sc1 = scale_of(k + 1);
+        const float2 s0 = make_float2(sc0, sc0), s1 = make_float2(sc1, sc1);
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+          sq[i] = __ffma2_rn(add2_rn(make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), mneg),
+                             s0, sq[i]);
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+          sq[i] = __ffma2_rn(
+              add2_rn(make_float2(__uint_as_float(cur[16 + 2 * i]), __uint_as_float(cur[16 + 2 * i + 1])), mneg), s1,
+              sq[i]);
+        if (k + 2 < NA) tc_wait_ld_regs<32>(nxt);
+      }
+      // Buffer drained: preset its cells again and hand it back before the tail.
+      preset_buffer(bf);
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const int n = n0 + 2 * i;
+        const float2 dx2 = *reinterpret_cast<const float2*>(dxs + n);
+        const float2 dd = mul2_rn(make_float2(d, d), dx2);  // feeds products only
+        if (FMT == FMT_Q4K) {
+          const uint4 l0 = lohi[n], l1 = lohi[n + 1];
+          const int sm0 = (int)(__dp4a(mw.x, l0.x, 0u) + __dp4a(mw.y, l0.y, 0u)) +
+                          256 * (__dp4a((int)mw.x, (int)l0.z, 0) + __dp4a((int)mw.y, (int)l0.w, 0));
+          const int sm1 = (int)(__dp4a(mw.x, l1.x, 0u) + __dp4a(mw.y, l1.y, 0u)) +
+                          256 * (__dp4a((int)mw.x, (int)l1.z, 0) + __dp4a((int)mw.y, (int)l1.w, 0));
+          // |sm| <= 8 * 63 * 4096 < 2^22: exact through the magic constant.
+          const float2 fsm = add2_rn(make_float2(__uint_as_float((uint32_t)sm0 + TC_MAGIC_BITS),
+                                                 __uint_as_float((uint32_t)sm1 + TC_MAGIC_BITS)),
+                                     mneg);
+          const float2 dm = mul2_rn(make_float2(dmin, dmin), dx2);
+          const float tx = __fsub_rn(__fmul_rn(dd.x, sq[i].x), __fmul_rn(dm.x, fsm.x));
+          const float ty = __fsub_rn(__fmul_rn(dd.y, sq[i].y), __fmul_rn(dm.y, fsm.y));
+          acc[i] = add2_rn(acc[i], make_float2(tx, ty));  // fed by subtractions
+        } else {
+          acc[i].x = __fadd_rn(acc[i].x, __fmul_rn(dd.x, sq[i].x));
+          acc[i].y = __fadd_rn(acc[i].y, __fmul_rn(dd.y, sq[i].y));
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&mfree[m]);
@@ -461,7 +516,7 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
       for (int i = 0; i < 16; i++) {
         const int tok = tg * KNS + n0 + i;
         if (tok >= p.nt) break;
-        float sv = acc[i];
+        float sv = (i & 1) ? acc[i >> 1].y : acc[i >> 1].x;
         if (p.epi == EPI_RESID) {
           float* dst = p.resid + (size_t)tok * p.resid_ld + row;
           *dst = __fadd_rn(*dst, __fmul_rn(p.rs, sv));

@@ -41,6 +41,52 @@ NRC_DEV void tc_ld16(uint32_t taddr, uint32_t* r) {
       : "memory");
 }
 NRC_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Wait for this thread's tcgen05.ld, then pin the loaded registers behind the
+// wait (empty volatile asm per register): no use of them moves above it.
+template <int N>
+NRC_DEV void tc_wait_ld_regs(uint32_t* r) {
+  tc_wait_ld();
+#pragma unroll
+  for (int i = 0; i < N; i++) asm volatile("" : "+r"(r[i]));
+}
+NRC_DEV void tc_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+// The same 32-bit value into 16 consecutive columns of this thread's lane.
+NRC_DEV void tc_st16_fill(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(
+                   taddr),
+               "r"(v)
+               : "memory");
+}
+NRC_DEV void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Packed f32 pairs, one rounding per operation. The assembler still fuses a
+// packed multiply that feeds a packed add or subtract into FFMA2, so these
+// serve only where no product feeds a sum (product -> product, sum -> sum);
+// a product that feeds a sum goes through the scalar __fmul_rn / __fadd_rn.
+NRC_DEV uint64_t f2_bits(float2 v) { return (uint64_t)__float_as_uint(v.x) | ((uint64_t)__float_as_uint(v.y) << 32); }
+NRC_DEV float2 bits_f2(uint64_t b) { return make_float2(__uint_as_float((uint32_t)b), __uint_as_float((uint32_t)(b >> 32))); }
+NRC_DEV float2 mul2_rn(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+NRC_DEV float2 add2_rn(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+NRC_DEV float2 sub2_rn(float2 a, float2 b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
 
 // UMMA shared-memory descriptor, K-major, no swizzle: 8x16-byte core matrices,
 // `lbo` = byte distance between the two 16-byte K halves, `sbo` = between
