@@ -347,6 +347,134 @@ __global__ void __launch_bounds__(ATT_THREADS, HD >= 128 ? 3 : 4) k_attention(co
   if (d < hd) a.out[(size_t)tok * att_dim + (size_t)h * hd + d] = acc;
 }
 
+// Multi-token attention (prefill chunks, batched sequences; never fused with
+// the KV append): one CTA per (KV head, token) serving the query heads of its
+// GQA group, so each K and V row is read once per group instead of once per
+// head. Per head the arithmetic is k_attention<false>'s exactly: the dot in
+// dimension order, the scale, the max, expf, the sum in position order, the
+// reciprocal, and each output dimension chained over positions in order.
+// Threads: gqa x HD (thread = (head, dim) in the V phase, = position in the
+// score phase).
+constexpr int ATT_GROUP_MAX = 8;  // query heads per KV head served by one CTA
+constexpr int ATT_VCH_GROUP = 64;
+
+template <int HD>
+__global__ void __launch_bounds__(1024) k_attention_group(const AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int g = blockIdx.x, tok = blockIdx.y;
+  const int gqa = a.n_heads / a.n_kv_heads;
+  const int nth = gqa * HD;
+  const int att_dim = a.n_heads * HD, kv_dim = a.n_kv_heads * HD;
+  const uint32_t pos = a.pos_tok ? a.pos_tok[tok] : a.pos_dev[0] + (uint32_t)tok;
+  const int npos = (int)pos + 1;
+  const size_t cache_off = a.pos_tok ? (size_t)a.seq_tok[tok] * a.seq_stride : 0;
+  const int sc_len = (a.ctx + 3) & ~3;
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                                                   // [gqa][HD]
+  float* sc = qs + gqa * HD;                                        // [gqa][sc_len] scores, then probabilities
+  uint16_t* vs = reinterpret_cast<uint16_t*>(sc + gqa * sc_len);   // [2][ATT_VCH_GROUP][HD]
+  __shared__ float red[32][ATT_GROUP_MAX];
+  __shared__ float hval[ATT_GROUP_MAX];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = nth >> 5;
+  const uint16_t* kbase = a.kcache + cache_off + (size_t)g * HD;
+  const uint16_t* vbase = a.vcache + cache_off + (size_t)g * HD;
+  constexpr int CPR = HD / 8;  // 16-byte chunks per K/V row
+  auto stage_v = [&](int t0, int buf) {
+    const int tn = min(ATT_VCH_GROUP, npos - t0);
+    uint16_t* dst = vs + (size_t)buf * ATT_VCH_GROUP * HD;
+    for (int i = tid; i < tn * CPR; i += nth) {
+      const int r = i / CPR, c = i - r * CPR;
+      cp_async16(dst + r * HD + c * 8, vbase + (size_t)(t0 + r) * kv_dim + c * 8);
+    }
+    cp_async_commit();
+  };
+  stage_v(0, 0);
+  for (int i = tid; i < gqa * HD; i += nth) qs[i] = a.q[(size_t)tok * att_dim + (size_t)g * gqa * HD + i];
+  __syncthreads();
+
+  // Scores: one position per thread, its K row loaded once for every head.
+  float mloc[ATT_GROUP_MAX];
+#pragma unroll
+  for (int hh = 0; hh < ATT_GROUP_MAX; hh++) mloc[hh] = -INFINITY;
+  for (int t = tid; t < npos; t += nth) {
+    const uint4* kr = reinterpret_cast<const uint4*>(kbase + (size_t)t * kv_dim);
+    uint4 kk[CPR];
+#pragma unroll
+    for (int c = 0; c < CPR; c++) kk[c] = kr[c];
+    float s[ATT_GROUP_MAX];
+#pragma unroll
+    for (int hh = 0; hh < ATT_GROUP_MAX; hh++) s[hh] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CPR; c++) {
+      const uint32_t w[4] = {kk[c].x, kk[c].y, kk[c].z, kk[c].w};
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const float kv = h2f((w[e >> 1] >> (16 * (e & 1))) & 0xffffu);
+#pragma unroll
+        for (int hh = 0; hh < ATT_GROUP_MAX; hh++)
+          if (hh < gqa) s[hh] = __fadd_rn(s[hh], __fmul_rn(kv, qs[hh * HD + c * 8 + e]));
+      }
+    }
+#pragma unroll
+    for (int hh = 0; hh < ATT_GROUP_MAX; hh++)
+      if (hh < gqa) {
+        const float v = __fmul_rn(s[hh], a.scale);
+        sc[hh * sc_len + t] = v;
+        mloc[hh] = fmaxf(mloc[hh], v);
+      }
+  }
+#pragma unroll
+  for (int hh = 0; hh < ATT_GROUP_MAX; hh++)
+    if (hh < gqa) {
+      const float m = warp_max(mloc[hh]);
+      if (lane == 0) red[warp][hh] = m;
+    }
+  __syncthreads();
+  if (tid < gqa) {
+    float mx = red[0][tid];
+    for (int w = 1; w < nwarp; w++) mx = fmaxf(mx, red[w][tid]);
+    hval[tid] = mx;
+  }
+  __syncthreads();
+  for (int i = tid; i < gqa * npos; i += nth) {
+    const int hh = i / npos, t = i - hh * npos;
+    sc[hh * sc_len + t] = expf_cr(__fsub_rn(sc[hh * sc_len + t], hval[hh]));
+  }
+  __syncthreads();
+  // Each head's sum in position order (vec.rs:35-36), one chain per head,
+  // the heads' chains on different warps.
+  if (lane == 0 && warp < gqa) {
+    const float* p = sc + warp * sc_len;
+    hval[warp] = __fdiv_rn(1.0f, seq_sum_serial(npos, [&](int t) { return p[t]; }));
+  }
+  __syncthreads();
+  for (int i = tid; i < gqa * npos; i += nth) {
+    const int hh = i / npos, t = i - hh * npos;
+    sc[hh * sc_len + t] = __fmul_rn(sc[hh * sc_len + t], hval[hh]);
+  }
+
+  const int hh = tid / HD, d = tid - hh * HD;
+  const float* ph = sc + hh * sc_len;
+  float acc = 0.0f;
+  int buf = 0;
+  for (int t0 = 0; t0 < npos; t0 += ATT_VCH_GROUP, buf ^= 1) {
+    const int tn = min(ATT_VCH_GROUP, npos - t0);
+    if (t0 + ATT_VCH_GROUP < npos) {
+      stage_v(t0 + ATT_VCH_GROUP, buf ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // the chunk (and, the first time, the probabilities) visible to all
+    const uint16_t* vr = vs + (size_t)buf * ATT_VCH_GROUP * HD + d;
+    const float* p = ph + t0;
+    acc = seq_sum_serial(tn, [&](int t) { return __fmul_rn(p[t], h2f(vr[(size_t)t * HD])); }, acc);
+    __syncthreads();  // the buffer is restaged two chunks later
+  }
+  a.out[(size_t)tok * att_dim + (size_t)(g * gqa + hh) * HD + d] = acc;
+}
+
 __global__ void k_embed(const EmbedArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -491,10 +619,28 @@ size_t attention_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx, 
   return (size_t)head_dim * 4 * 4 + (size_t)head_dim * 2 * 2 + (size_t)sc * 4 + (size_t)2 * vch * head_dim * 2;
 }
 
+size_t attention_group_smem_bytes(int n_heads, int n_kv_heads, int head_dim, int ctx) {
+  const int gqa = n_heads / n_kv_heads;
+  return (size_t)gqa * head_dim * 4 + (size_t)gqa * ((ctx + 3) & ~3) * 4 + (size_t)2 * ATT_VCH_GROUP * head_dim * 2;
+}
+
 cudaError_t attention_run(const AttnArgs& a, cudaStream_t s, bool pdl, bool fast) {
   if (a.n_kv_heads < 1 || a.n_heads % a.n_kv_heads || a.head_dim % 32 || a.head_dim > ATT_THREADS ||
       (a.fused && (a.nt != 1 || a.pos_tok)))
     return cudaErrorInvalidValue;
+  const int gqa = a.n_heads / a.n_kv_heads;
+  if (!a.fused && !fast && a.nt > 1 && gqa <= ATT_GROUP_MAX && gqa * a.head_dim <= 1024) {
+    const size_t gsmem = attention_group_smem_bytes(a.n_heads, a.n_kv_heads, a.head_dim, a.ctx);
+    if (gsmem <= ATTN_MAX_SMEM) {
+      const void* gfn = a.head_dim == 32 ? (const void*)k_attention_group<32>
+                        : a.head_dim == 64 ? (const void*)k_attention_group<64>
+                                           : (const void*)k_attention_group<128>;
+      if (cudaError_t e = ensure_smem_attr(gfn, ATTN_MAX_SMEM)) return e;
+      AttnArgs aa = a;
+      void* args[] = {&aa};
+      return launch(gfn, dim3(a.n_kv_heads, a.nt), dim3(gqa * a.head_dim), gsmem, s, pdl, args);
+    }
+  }
   const size_t smem = attention_smem_bytes(a.n_heads, a.n_kv_heads, a.head_dim, a.ctx, a.nt);
   if (smem > ATTN_MAX_SMEM) return cudaErrorInvalidValue;
   const void* fn = nullptr;
