@@ -256,19 +256,39 @@ def other_configs(torch, hbm):
         out[key] = {"model": name, "decode_tokens_per_s": ex, "decode_tokens_per_s_fast": fa, "ms_per_token": ms,
                     "step_gbs": gbs, "step_frac_of_hbm": gbs / hbm}
         m.close()
+    out["config4"] = config4_batch(torch, hbm, CONFIG4_SEQS, 0, None)
+    sweep = {}
+    gs = torch.cuda.Stream()
+    for rows, cols in ((2048, 2048), (8192, 2048), (2048, 8192), (128256, 2048), (9728, 2560)):
+        nb, ms = gemv_roofline(torch, rows, cols, 20, gs)
+        sweep[f"{rows}x{cols}"] = {"us": ms * 1000.0, "gbs": nb / ms / 1e6, "frac": nb / ms / 1e6 / hbm}
+    out["config1_q8_0_n1"] = sweep
+    return out
+
+
+CONFIG4_SEQS = 256
+
+
+def config4_batch(torch, hbm, nseq, seq0, reduce_ms, device=0):
+    """Config 4: `nseq` sequences (global indices seq0 .. seq0 + nseq - 1, each
+    a seeded 128-token prompt) prefilled and decoded as one batch on this GPU.
+    With `reduce_ms` (data parallel over ranks) every timed region is replaced
+    by the slowest rank's, and the throughputs count all ranks' sequences."""
+    from nightrun_b200 import Model
     cfg = CONFIGS["granite3b_q4km"]
-    m = Model.synth(cfg, MODEL_SEED)
-    S = 256
-    b = m.batch(128 + 24, S)
-    prompts = [prompt_ids(128, cfg["vocab"], seed=MODEL_SEED + 11 + i) for i in range(S)]
+    m = Model.synth(cfg, MODEL_SEED, device=device)
+    b = m.batch(128 + 24, nseq)
+    prompts = [prompt_ids(128, cfg["vocab"], seed=MODEL_SEED + 11 + seq0 + i) for i in range(nseq)]
     stream = torch.cuda.ExternalStream(b.stream_handle())
+    red = reduce_ms or (lambda v: v)
+    total = CONFIG4_SEQS if reduce_ms else nseq
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     e0.record(stream)
     b.prefill(prompts)
     e1.record(stream)
     torch.cuda.synchronize()
-    pre_ms = e0.elapsed_time(e1)
+    pre_ms = red(e0.elapsed_time(e1))
     b.decode_async(3)
     b.sync()
     torch.cuda.synchronize()
@@ -277,21 +297,15 @@ def other_configs(torch, hbm):
     e1.record(stream)
     b.sync()
     torch.cuda.synchronize()
-    step_ms = e0.elapsed_time(e1) / 16
+    step_ms = red(e0.elapsed_time(e1)) / 16
     wb, kvb = model_bytes(cfg)
-    step_bytes = wb + kvb * S * (128 + 11)
-    out["config4"] = {"model": "granite3b_q4km", "sequences": S, "decode_tokens_per_s": S * 1000.0 / step_ms,
-                      "ms_per_step": step_ms, "prefill_tokens_per_s": S * 128 * 1000.0 / pre_ms,
-                      "step_gbs": step_bytes / step_ms / 1e6, "step_frac_of_hbm": step_bytes / step_ms / 1e6 / hbm}
+    step_bytes = wb + kvb * nseq * (128 + 11)  # one GPU's bytes per step
+    res = {"model": "granite3b_q4km", "sequences": total, "decode_tokens_per_s": total * 1000.0 / step_ms,
+           "ms_per_step": step_ms, "prefill_tokens_per_s": total * 128 * 1000.0 / pre_ms,
+           "step_gbs_per_gpu": step_bytes / step_ms / 1e6, "step_frac_of_hbm": step_bytes / step_ms / 1e6 / hbm}
     b.close()
     m.close()
-    sweep = {}
-    gs = torch.cuda.Stream()
-    for rows, cols in ((2048, 2048), (8192, 2048), (2048, 8192), (128256, 2048), (9728, 2560)):
-        nb, ms = gemv_roofline(torch, rows, cols, 20, gs)
-        sweep[f"{rows}x{cols}"] = {"us": ms * 1000.0, "gbs": nb / ms / 1e6, "frac": nb / ms / 1e6 / hbm}
-    out["config1_q8_0_n1"] = sweep
-    return out
+    return res
 
 
 def max_over_ranks_of(v, world, device):
@@ -433,6 +447,14 @@ def run_ours(args, rank, world, local_rank):
                                        "step_share": cls.get("step_share"), "algorithmic_bytes_per_launch": cb}
         if not args.no_other_configs:
             line["other_configs"] = other_configs(torch, hbm)
+    if world > 1 and not args.no_other_configs:
+        # Config 4 data parallel: the 256 sequences split evenly over the ranks,
+        # each rank a batch context on its own GPU, no collective on the data path.
+        per = CONFIG4_SEQS // world
+        res = config4_batch(torch, hbm, per, rank * per, lambda v: max_over_ranks(v), device=local_rank)
+        res["parallelism"] = f"dp{world} ({per} sequences per GPU)"
+        res["scaling"] = "strong"
+        line["config4_dp"] = res
     line["clocks"] = sampler.stop()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         blob = model.export()
