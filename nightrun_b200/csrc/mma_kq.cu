@@ -17,15 +17,18 @@
 // with the reference's roundings in the reference's order, so outputs are
 // bit-identical to the scalar path.
 //
-// CTA = 128 weight rows x NS tokens (Q4_K NS = 64, Q6_K NS = 32: one
-// super-block's slots fill the 512 TMEM columns), one super-block per stage,
-// 14 warps:
+// CTA = 128 weight rows x 32 tokens, one super-block per stage (Q4_K three
+// shared-memory stages, Q6_K two), 14 warps:
 //   warps 0-7   epilogue: TMEM lane quarter warp % 4 (rows), token half warp / 4;
-//   warps 8-11  repack: raw rows (bulk-copied) -> canonical int8 A tiles + row scales;
-//   warp 12     producer: 1-D bulk copies of the raw rows (16-byte aligned
-//               supersets; a matrix's ragged last bytes by plain loads), the
-//               activation tiles and their scales / bsums (no multicast);
+//   warps 8-11  repack: raw rows -> canonical int8 A tiles + row scales;
+//   warp 12     producer: eight 2-D tensor copies per super-block (the
+//               matrix as rows of 8-row groups; box = one super-block window
+//               of 16 groups), the last rows % 8 by cp.async, the activation
+//               tiles and their scales / chunk sums by bulk copies (no multicast);
 //   warp 13     TMEM allocator and single-thread MMA issuer.
+// TMEM: two units of 8 slots x 32 columns; a Q4_K super-block fills one unit
+// (two super-blocks in flight), a Q6_K one fills both in turn (the MMA fills
+// one unit while the epilogue drains the other).
 // Every mbarrier wait is bounded (error word + clean exit, never a trap).
 #include <algorithm>
 
@@ -80,7 +83,7 @@ template <int FMT> struct KqShape {
   static constexpr int NA = FMT == FMT_Q4K ? 8 : 16;   // MMAs = TMEM slots per super-block
   static constexpr int NAT = 8;                        // A tiles: the 8 chunks of 32 values
   static constexpr int NBT = FMT == FMT_Q4K ? 8 : 16;  // B tiles (Q6_K: each chunk's two masked halves)
-  static constexpr int NB = 512 / (NA * KNS);          // TMEM buffers (super-blocks in flight)
+  static constexpr int UPS = NA / 8;                   // TMEM units (8 slots, 256 columns) per super-block
   static constexpr int NST = FMT == FMT_Q4K ? 3 : 2;   // smem stages
   static constexpr int BW = FMT == FMT_Q4K ? Q4K_BYTES : 240;
   static constexpr int RAW = FMT == FMT_Q4K ? Q4K_BYTES : 240;
@@ -92,15 +95,19 @@ NRC_DEV uint32_t q6_minus32(uint32_t q) { return ((q | 0x80808080u) - 0x20202020
 template <int FMT>
 __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqParams p) {
   using SH = KqShape<FMT>;
-  constexpr int NA = SH::NA, NB = SH::NB, NST = SH::NST, RAW = SH::RAW, BW = SH::BW;
+  constexpr int UPS = SH::UPS, NST = SH::NST, RAW = SH::RAW, BW = SH::BW;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.off_bar);
   uint64_t* full = bars;                  // producer -> repack (32 lane arrivals + tx bytes)
   uint64_t* aready = full + NST;          // repack -> MMA (A tiles, scales written)
   uint64_t* empty = aready + NST;         // MMA commit -> producer (stage consumed)
-  uint64_t* mdone = empty + NST;          // MMA commit -> epilogue (the super-block's slots written)
-  uint64_t* tfree = mdone + NST;          // epilogue warps -> MMA (TMEM buffer drained)
-  uint64_t* mfree = tfree + NB;           // epilogue warps -> repack (scale slot read)
+  // TMEM holds two units of 8 slots (32 columns each); fill f (f = st * UPS + h,
+  // unit f % 2) is the h-th unit of super-block st: Q4_K a super-block per
+  // unit (double-buffered), Q6_K two units per super-block (the MMA fills one
+  // unit while the epilogue drains the other).
+  uint64_t* mdone = empty + NST;          // MMA commit -> epilogue (a unit's slots written), per unit
+  uint64_t* tfree = mdone + 2;            // epilogue warps -> MMA (unit drained and preset), per unit
+  uint64_t* mfree = tfree + 2;            // epilogue warps -> repack (scale slot read)
   uint64_t* mready = mfree + NMR;         // repack warps -> epilogue (scale slot written)
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -126,9 +133,11 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
       mbar_init(&full[s], 32 + 1);
       mbar_init(&aready[s], REP_WARPS);
       mbar_init(&empty[s], 1);
-      mbar_init(&mdone[s], 1);
     }
-    for (int b = 0; b < NB; b++) mbar_init(&tfree[b], EPI_WARPS);
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&mdone[b], 1);
+      mbar_init(&tfree[b], EPI_WARPS);
+    }
     for (int m = 0; m < NMR; m++) {
       mbar_init(&mfree[m], EPI_WARPS);
       mbar_init(&mready[m], REP_WARPS);
@@ -248,22 +257,20 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
           b = st_base(s) + p.off_tail + (r - tma_rows) * RAW + (ga & 15);
         }
         if (FMT == FMT_Q4K) {
-          // d, dmin (f16), 12 scale bytes (q4k_scale_min, kquant.rs:83-92), 128 bytes of nibbles.
+          // d, dmin (f16), 12 scale bytes s[0..11] (q4k_scale_min, kquant.rs:83-92),
+          // 128 bytes of nibbles. One 16-byte load; the 6-bit (sc, m) pairs are
+          // unpacked four bytes at a time: sc[j] = s[j] & 63 and m[j] = s[j+4] & 63
+          // for j < 4; sc[j] = (s[j+4] & 15) | (s[j-4] >> 6) << 4 and
+          // m[j] = (s[j+4] >> 4) | (s[j] >> 6) << 4 for j >= 4.
+          const uint4 hd = *reinterpret_cast<const uint4*>(b);
           float* fm = reinterpret_cast<float*>(rm);
-          fm[0] = f16_to_f32((uint32_t)b[0] | ((uint32_t)b[1] << 8));
-          fm[1] = f16_to_f32((uint32_t)b[2] | ((uint32_t)b[3] << 8));
-          uint8_t* scm = rm + 8;  // sc[8], m[8]
-          const uint8_t* sb = b + 4;
-#pragma unroll
-          for (int j = 0; j < 8; j++) {
-            if (j < 4) {
-              scm[j] = sb[j] & 63;
-              scm[8 + j] = sb[j + 4] & 63;
-            } else {
-              scm[j] = (sb[j + 4] & 0x0F) | ((sb[j - 4] >> 6) << 4);
-              scm[8 + j] = (sb[j + 4] >> 4) | ((sb[j] >> 6) << 4);
-            }
-          }
+          fm[0] = f16_to_f32(hd.x & 0xffffu);
+          fm[1] = f16_to_f32(hd.x >> 16);
+          const uint32_t s0 = hd.y, s4 = hd.z, s8 = hd.w;
+          *reinterpret_cast<uint2*>(rm + 8) =
+              make_uint2(s0 & 0x3F3F3F3Fu, (s8 & 0x0F0F0F0Fu) | (((s0 >> 6) & 0x03030303u) << 4));
+          *reinterpret_cast<uint2*>(rm + 16) =
+              make_uint2(s4 & 0x3F3F3F3Fu, ((s8 >> 4) & 0x0F0F0F0Fu) | (((s4 >> 6) & 0x03030303u) << 4));
           // 16-byte loads: the rows sit 144 bytes (9 x 16) apart, so eight threads'
           // loads never share a bank group.
           const uint4* qs = reinterpret_cast<const uint4*>(b + 16);
@@ -357,35 +364,42 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = idesc_i8(KNS);
-      int issued = -1;  // last super-block whose MMAs were issued
-      for (int st = 0; st < nsb && !abort_flag; st++) {
-        const int s = st % NST, u = st / NST, bf = st % NB;
+      int last = -1;  // last unit fill whose MMAs were issued
+      bool bad = false;
+      for (int st = 0; st < nsb && !abort_flag && !bad; st++) {
+        const int s = st % NST, u = st / NST;
         if (!mbar_wait(&aready[s], u & 1)) {
           fail(ERR_WAIT_FULL);
           break;
         }
-        // The TMEM buffer drained and preset by the epilogue (first use: preset only).
-        if (!mbar_wait(&tfree[bf], (st / NB) & 1)) {
-          fail(ERR_WAIT_EMPTY);
-          break;
-        }
-        tc_fence_after();
         const uint8_t* a = st_base(s) + p.off_a;
         const uint8_t* bt = st_base(s) + p.off_b;
-        const uint32_t dbase = tbase + (uint32_t)(bf * NA * KNS);
 #pragma unroll 1
-        for (int k = 0; k < NA; k++) {
-          const int at = FMT == FMT_Q4K ? k : k / 2;  // Q6_K: group k = half (k % 2) of chunk k / 2
-          const uint64_t ad = smem_desc(a + at * (TC_M * 32), 128, 256);
-          const uint64_t bd = smem_desc(bt + k * (KNS * 32), 128, 256);
-          tc_mma_i8(dbase + (uint32_t)(k * KNS), ad, bd, idesc, 1u);  // onto the preset cell
+        for (int h = 0; h < UPS; h++) {
+          const int f = st * UPS + h, unit = f & 1;
+          // The unit drained and preset by the epilogue (first use: preset only).
+          if (!mbar_wait(&tfree[unit], (f >> 1) & 1)) {
+            fail(ERR_WAIT_EMPTY);
+            bad = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t dbase = tbase + (uint32_t)(unit * 8 * KNS);
+#pragma unroll 1
+          for (int kk = 0; kk < 8; kk++) {
+            const int k = 8 * h + kk;
+            const int at = FMT == FMT_Q4K ? k : k / 2;  // Q6_K: group k = half (k % 2) of chunk k / 2
+            const uint64_t ad = smem_desc(a + at * (TC_M * 32), 128, 256);
+            const uint64_t bd = smem_desc(bt + k * (KNS * 32), 128, 256);
+            tc_mma_i8(dbase + (uint32_t)(kk * KNS), ad, bd, idesc, 1u);  // onto the preset cell
+          }
+          tc_commit(&mdone[unit]);
+          last = f;
         }
-        tc_commit(&mdone[s]);
-        tc_commit(&empty[s]);
-        issued = st;
+        if (!bad) tc_commit(&empty[s]);
       }
       // Never release TMEM with an MMA in flight: wait (bounded) for the last commit.
-      if (issued >= 0 && !mbar_wait(&mdone[issued % NST], (issued / NST) & 1)) atomicOr(p.err, ERR_DRAIN);
+      if (last >= 0 && !mbar_wait(&mdone[last & 1], (last >> 1) & 1)) atomicOr(p.err, ERR_DRAIN);
     }
     __syncwarp();
   } else {
@@ -403,31 +417,27 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
     const int n0 = half * 16;     // this warp's 16 tokens
     const uint32_t lane_base = tbase + ((uint32_t)(q * 32) << 16);
     const float2 mneg = make_float2(-TC_MAGIC_F, -TC_MAGIC_F);
-    auto preset_buffer = [&](int bf) {
+    auto preset_unit = [&](int unit) {
 #pragma unroll
-      for (int k = 0; k < NA; k++) tc_st16_fill(lane_base + (uint32_t)(bf * NA * KNS + k * KNS + n0), TC_MAGIC_BITS);
+      for (int k = 0; k < 8; k++) tc_st16_fill(lane_base + (uint32_t)(unit * 8 * KNS + k * KNS + n0), TC_MAGIC_BITS);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tfree[bf]);
+      if (lane == 0) mbar_arrive(&tfree[unit]);
     };
-    for (int b = 0; b < NB; b++) preset_buffer(b);
+    preset_unit(0);
+    preset_unit(1);
     float2 acc[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
     for (int st = 0; st < nsb && !abort_flag; st++) {
-      const int s = st % NST, u = st / NST, bf = st % NB, m = st % NMR;
-      // mdone and mready complete at most one phase ahead of this warp: their
-      // next phases need this super-block's tfree / mfree.
-      if (!mbar_wait(&mdone[s], u & 1) || !mbar_wait(&mready[m], (st / NMR) & 1)) {
+      const int m = st % NMR;
+      // mready and each unit's mdone complete at most one phase ahead of this
+      // warp: their next phases need this super-block's mfree / the unit's tfree.
+      if (!mbar_wait(&mready[m], (st / NMR) & 1)) {
         fail(ERR_WAIT_FULL);
         break;
       }
-      tc_fence_after();
-      const uint32_t slot0 = lane_base + (uint32_t)(bf * NA * KNS + n0);
-      uint32_t va[32], vb[32];
-      tc_ld16(slot0, va);
-      tc_ld16(slot0 + (uint32_t)KNS, va + 16);
       const uint8_t* rm = meta(m) + r * RMETA;
       const float* dxs = reinterpret_cast<const float*>(meta(m) + TC_M * RMETA);
       const uint4* lohi = reinterpret_cast<const uint4*>(dxs + KNS);
@@ -454,35 +464,52 @@ __global__ void __launch_bounds__(KTHR, 1) k_mma_kq(const __grid_constant__ KqPa
         const uint32_t b = (sws[k >> 2] >> (8 * (k & 3))) & 0xffu;
         return FMT == FMT_Q4K ? (float)b : (float)(int)(int8_t)b;
       };
-      tc_wait_ld_regs<32>(va);
       float2 sq[8];
 #pragma unroll
       for (int i = 0; i < 8; i++) sq[i] = make_float2(0.0f, 0.0f);
-      // Two slots per TMEM round trip, the next pair's loads in flight while
-      // this pair is scaled; each slot's dots in slot order.
+      bool bad = false;
 #pragma unroll
-      for (int k = 0; k < NA; k += 2) {
-        uint32_t* cur = ((k >> 1) & 1) ? vb : va;
-        uint32_t* nxt = ((k >> 1) & 1) ? va : vb;
-        if (k + 2 < NA) {
-          tc_ld16(slot0 + (uint32_t)((k + 2) * KNS), nxt);
-          tc_ld16(slot0 + (uint32_t)((k + 3) * KNS), nxt + 16);
+      for (int h = 0; h < UPS; h++) {
+        const int f = st * UPS + h, unit = f & 1;
+        if (!mbar_wait(&mdone[unit], (f >> 1) & 1)) {
+          fail(ERR_WAIT_FULL);
+          bad = true;
+          break;
         }
-        const float sc0 = scale_of(k), sc1 = scale_of(k + 1);
-        const float2 s0 = make_float2(sc0, sc0), s1 = make_float2(sc1, sc1);
+        tc_fence_after();
+        const uint32_t slot0 = lane_base + (uint32_t)(unit * 8 * KNS + n0);
+        uint32_t va[32], vb[32];
+        tc_ld16(slot0, va);
+        tc_ld16(slot0 + (uint32_t)KNS, va + 16);
+        tc_wait_ld_regs<32>(va);
+        // Two slots per TMEM round trip, the next pair's loads in flight while
+        // this pair is scaled; each slot's dots in slot order.
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-          sq[i] = __ffma2_rn(add2_rn(make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), mneg),
-                             s0, sq[i]);
+        for (int kk = 0; kk < 8; kk += 2) {
+          const int k = 8 * h + kk;
+          uint32_t* cur = ((kk >> 1) & 1) ? vb : va;
+          uint32_t* nxt = ((kk >> 1) & 1) ? va : vb;
+          if (kk + 2 < 8) {
+            tc_ld16(slot0 + (uint32_t)((kk + 2) * KNS), nxt);
+            tc_ld16(slot0 + (uint32_t)((kk + 3) * KNS), nxt + 16);
+          }
+          const float sc0 = scale_of(k), sc1 = scale_of(k + 1);
+          const float2 s0 = make_float2(sc0, sc0), s1 = make_float2(sc1, sc1);
 #pragma unroll
-        for (int i = 0; i < 8; i++)
-          sq[i] = __ffma2_rn(
-              add2_rn(make_float2(__uint_as_float(cur[16 + 2 * i]), __uint_as_float(cur[16 + 2 * i + 1])), mneg), s1,
-              sq[i]);
-        if (k + 2 < NA) tc_wait_ld_regs<32>(nxt);
+          for (int i = 0; i < 8; i++)
+            sq[i] = __ffma2_rn(add2_rn(make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), mneg),
+                               s0, sq[i]);
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+            sq[i] = __ffma2_rn(
+                add2_rn(make_float2(__uint_as_float(cur[16 + 2 * i]), __uint_as_float(cur[16 + 2 * i + 1])), mneg), s1,
+                sq[i]);
+          if (kk + 2 < 8) tc_wait_ld_regs<32>(nxt);
+        }
+        // Unit drained: preset its cells again and hand it back.
+        preset_unit(unit);
       }
-      // Buffer drained: preset its cells again and hand it back before the tail.
-      preset_buffer(bf);
+      if (bad) break;
 #pragma unroll
       for (int i = 0; i < 8; i++) {
         const int n = n0 + 2 * i;
@@ -757,7 +784,6 @@ cudaError_t mma_kq_run(const MmaKqArgs& a, cudaStream_t s, bool pdl) {
   }
   const int nst = q4 ? KqShape<FMT_Q4K>::NST : KqShape<FMT_Q6K>::NST;
   const int nbt = q4 ? KqShape<FMT_Q4K>::NBT : KqShape<FMT_Q6K>::NBT;
-  const int nb = q4 ? KqShape<FMT_Q4K>::NB : KqShape<FMT_Q6K>::NB;
   // Stage: A tiles (1024-aligned) | raw rows | B tiles | token scales | chunk
   // sums. Then the scale ring and the barriers.
   const int raw_slot = q4 ? KqShape<FMT_Q4K>::RAW : KqShape<FMT_Q6K>::RAW;
@@ -781,7 +807,7 @@ cudaError_t mma_kq_run(const MmaKqArgs& a, cudaStream_t s, bool pdl) {
   p.off_meta = (int)(o * nst);
   const size_t meta_bytes = (size_t)NMR * (TC_M * RMETA + KNS * 36);
   p.off_bar = (int)((p.off_meta + meta_bytes + 15) & ~(size_t)15);
-  const size_t smem = p.off_bar + (size_t)(4 * nst + nb + 2 * NMR) * 8;
+  const size_t smem = p.off_bar + (size_t)(3 * nst + 4 + 2 * NMR) * 8;
   const void* fn = q4 ? (const void*)k_mma_kq<FMT_Q4K> : (const void*)k_mma_kq<FMT_Q6K>;
   if (smem > 225 * 1024) return cudaErrorInvalidValue;
   if (cudaError_t e = ensure_smem_attr(fn, 225 * 1024)) return e;
