@@ -37,6 +37,7 @@ extern "C" {
 #define NRC_ERR_BAD_TABLE (-14)   /* ParseError::BadTable   (format.rs:223) */
 #define NRC_ERR_MISSING (-15)     /* ParseError::MissingTensor (format.rs:224) */
 #define NRC_ERR_DATA_CRC (-16)    /* Model::verify_data returned false (format.rs:410-422) */
+#define NRC_ERR_UNSUPPORTED (-17) /* GGUF the converter rejects: architecture, SSM/MoE, tensor type (tools/nrconvert/src/main.rs:63-110, 246-252) */
 #define NRC_ERR_CTX_FULL (-20)    /* "context window exhausted" (crates/nr-model/src/infer.rs:513, 605) */
 #define NRC_ERR_BAD_BATCH (-21)   /* prefill batch outside 1..=MAX_BATCH (infer.rs:604, 754) */
 #define NRC_ERR_BAD_TOKEN (-22)   /* token id >= vocab (the reference would panic on the slice) */
@@ -173,6 +174,14 @@ typedef struct nrc_synth_cfg {
  * `device`. verify_crc != 0 also checks data_crc (Model::verify_data, format.rs:410-422). The blob
  * may be freed after the call. */
 int nrc_model_load(const uint8_t* blob, size_t len, int device, int verify_crc, nrc_model** out);
+/* GGUF ingestion (tools/nrconvert/src/gguf.rs; main.rs:180-453): a GGUF v2/v3 file of a dense
+ * llama / qwen3 / granite model with F32 / Q8_0 / Q4_K / Q6_K tensors as a .nrm v3 blob: the
+ * converter's tensor order, 64-byte alignment, header fields and CRCs, with the tokenizer section
+ * left empty. out == NULL: only *out_len is set. Conditions the converter panics or exits on
+ * return NRC_ERR_TOO_SHORT / BAD_MAGIC / BAD_VERSION / MISSING / UNSUPPORTED. */
+int nrc_gguf_to_nrm(const uint8_t* gguf, size_t len, uint8_t* out, size_t out_cap, size_t* out_len);
+/* nrc_gguf_to_nrm, then nrc_model_load (data CRC verified) of the result. */
+int nrc_model_load_gguf(const uint8_t* gguf, size_t len, int device, nrc_model** out);
 /* Build a seeded synthetic model directly in device memory (no host copy of the weights). */
 int nrc_model_synth(const nrc_synth_cfg* cfg, uint64_t seed, int device, nrc_model** out);
 int nrc_model_meta(const nrc_model* m, nrc_meta* out);

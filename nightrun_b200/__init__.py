@@ -8,6 +8,6 @@ transformer forward path behind a C ABI (include/nrcuda.h).
 """
 from . import configs
 from ._lib import NrcError, lib
-from .infer import BatchCtx, InferCtx, Model, tp_unique_id
+from .infer import BatchCtx, InferCtx, Model, gguf_to_nrm, tp_unique_id
 
-__all__ = ["configs", "lib", "Model", "InferCtx", "BatchCtx", "NrcError", "tp_unique_id"]
+__all__ = ["configs", "lib", "Model", "InferCtx", "BatchCtx", "NrcError", "gguf_to_nrm", "tp_unique_id"]

@@ -11,9 +11,12 @@ LIB_PATH = os.path.join(HERE, "libnrcuda.so")
 
 ERRORS = {
     0: "OK", -1: "INVALID", -2: "CUDA", -3: "ALLOC", -4: "DEVICE", -10: "TOO_SHORT", -11: "BAD_MAGIC",
-    -12: "BAD_VERSION", -13: "META_CRC", -14: "BAD_TABLE", -15: "MISSING", -16: "DATA_CRC",
+    -12: "BAD_VERSION", -13: "META_CRC", -14: "BAD_TABLE", -15: "MISSING", -16: "DATA_CRC", -17: "UNSUPPORTED",
     -20: "CTX_FULL", -21: "BAD_BATCH", -22: "BAD_TOKEN",
 }
+for _code, _name in ERRORS.items():
+    if _code:
+        globals()["NRC_ERR_" + _name] = _code
 MAX_BATCH = 64
 NOALLOC_MAX_COLS = 16384
 
@@ -89,6 +92,8 @@ SIGNATURES = [
     ("nrc_rope_freqs", I, [P, S, F, F, F, F, F]),
     ("nrc_rope_apply", I, [P, S, S, P, S, I, P]),
     ("nrc_model_load", I, [P, S, I, I, C.POINTER(P)]),
+    ("nrc_gguf_to_nrm", I, [P, S, P, S, C.POINTER(S)]),
+    ("nrc_model_load_gguf", I, [P, S, I, C.POINTER(P)]),
     ("nrc_model_synth", I, [C.POINTER(SynthCfg), U64, I, C.POINTER(P)]),
     ("nrc_model_meta", I, [P, C.POINTER(Meta)]),
     ("nrc_model_nrm_size", S, [P]),

@@ -9,7 +9,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "libnrcuda.so")
-SOURCES = ["gemv.cu", "mma.cu", "ops.cu", "attn.cu", "synth.cu", "engine.cu", "api.cu", "noalloc.cu", "sample.cu", "tp.cu", "mma_kq.cu"]
+SOURCES = ["gemv.cu", "mma.cu", "ops.cu", "attn.cu", "synth.cu", "engine.cu", "api.cu", "noalloc.cu", "sample.cu", "tp.cu", "mma_kq.cu", "gguf.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 

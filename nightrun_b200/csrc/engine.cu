@@ -124,6 +124,10 @@ void wr(uint8_t* p, T v) {
 
 int dtype_fmt(int dt) { return dt == DT_Q8_0 ? FMT_Q8_0 : (dt == DT_Q4K ? FMT_Q4K : FMT_Q6K); }
 }  // namespace
+namespace nrc {
+uint32_t crc32_bytes(const uint8_t* d, size_t n) { return crc32_host(d, n); }
+uint32_t crc32_update(uint32_t state, const uint8_t* d, size_t n) { return crc_tables().update(state, d, n); }
+}  // namespace nrc
 
 struct nrc_model {
   int device = 0;

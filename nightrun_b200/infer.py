@@ -10,6 +10,20 @@ from . import _lib
 from ._lib import check, lib
 
 
+def gguf_to_nrm(gguf):
+    """GGUF bytes -> .nrm v3 blob (numpy uint8), the conversion of
+    tools/nrconvert (tensor order, alignment, header and CRCs; empty tokenizer
+    section). Raises NrcError for what the converter rejects."""
+    buf = np.ascontiguousarray(np.frombuffer(bytes(gguf), np.uint8) if not isinstance(gguf, np.ndarray) else gguf,
+                               dtype=np.uint8)
+    n = C.c_size_t()
+    check(lib().nrc_gguf_to_nrm(buf.ctypes.data_as(C.c_void_p), buf.size, None, 0, C.byref(n)))
+    out = np.empty(n.value, np.uint8)
+    check(lib().nrc_gguf_to_nrm(buf.ctypes.data_as(C.c_void_p), buf.size, out.ctypes.data_as(C.c_void_p), out.size,
+                                C.byref(n)))
+    return out
+
+
 class Model:
     """A `.nrm` model resident in device memory (Model::parse + upload, format.rs:260-406)."""
 
@@ -25,6 +39,16 @@ class Model:
                                    dtype=np.uint8)
         h = C.c_void_p()
         check(lib().nrc_model_load(buf.ctypes.data_as(C.c_void_p), buf.size, device, int(verify_crc), C.byref(h)))
+        return cls(h, device)
+
+    @classmethod
+    def load_gguf(cls, gguf, device=0):
+        """A GGUF file's bytes (dense llama / qwen3 / granite; F32, Q8_0, Q4_K,
+        Q6_K tensors) converted as tools/nrconvert does and uploaded."""
+        buf = np.ascontiguousarray(np.frombuffer(bytes(gguf), np.uint8) if not isinstance(gguf, np.ndarray) else gguf,
+                                   dtype=np.uint8)
+        h = C.c_void_p()
+        check(lib().nrc_model_load_gguf(buf.ctypes.data_as(C.c_void_p), buf.size, device, C.byref(h)))
         return cls(h, device)
 
     @classmethod
