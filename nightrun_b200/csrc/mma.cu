@@ -9,15 +9,17 @@
 // warps apply the per-block scales with the reference's two roundings and add
 // the terms in block order, so outputs are bit-identical to the scalar path.
 //
-// CTA = 128 weight rows x NS tokens, 10 warps:
-//   warps 0-3  epilogue: TMEM lane = weight row; per block tcgen05.ld of the
-//              slot, exact scaling, running f32 sums in registers;
-//   warps 4-7  repack: raw Q8_0 rows (TMA-staged) -> UMMA K-major canonical
+// CTA = 128 weight rows x NS tokens, 14 warps:
+//   warps 0-7  epilogue: TMEM lane quarter warp % 4 = weight rows, token half
+//              warp / 4; per block tcgen05.ld of its half of the slot, exact
+//              scaling, running f32 sums in registers; the slot's cells are
+//              preset to the bits of 1.5 * 2^23 before the MMA adds onto them;
+//   warps 8-11 repack: raw Q8_0 rows (TMA-staged) -> UMMA K-major canonical
 //              int8 tiles + f32 row scales;
-//   warp 8     producer: per stage one 2-D tensor copy of the tile's raw
+//   warp 12    producer: per stage one 2-D tensor copy of the tile's raw
 //              weight rows (128 rows x 8 blocks) and bulk copies of the
 //              activation tiles and scales, into a 2-stage ring (no multicast);
-//   warp 9     TMEM allocator and single-thread MMA issuer.
+//   warp 13    TMEM allocator and single-thread MMA issuer.
 // Every mbarrier wait is bounded (error word + clean exit, never a trap).
 #include <algorithm>
 
@@ -35,9 +37,9 @@ constexpr int TM = 128;      // weight rows per tile (MMA M)
 constexpr int KB = 8;        // Q8_0 blocks per stage (K = 256; 272-byte row chunks are 16-byte aligned)
 constexpr int NST = 2;       // pipeline stages
 constexpr int NSLOT = 4;     // TMEM accumulator slots
-constexpr int NTHR = 320;
-constexpr int WP = 8, WM = 9;
-constexpr int EPI_WARPS = 4, REP_WARPS = 4;
+constexpr int NTHR = 448;
+constexpr int WP = 12, WM = 13;
+constexpr int EPI_WARPS = 8, REP_WARPS = 4;
 constexpr uint32_t MAGIC_BITS = 0x4B400000u;  // 12582912.0f = 1.5 * 2^23
 constexpr float MAGIC_F = 12582912.0f;
 
@@ -214,14 +216,15 @@ __global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Para
         for (int blk = 0; blk < KB; blk++) {
           const int b = st * KB + blk;
           const int slot = b % NSLOT;
-          if (b >= NSLOT && !mbar_wait(&tfree[slot], ((b / NSLOT) - 1) & 1)) {
+          // The slot drained and preset by the epilogue (first use: preset only).
+          if (!mbar_wait(&tfree[slot], (b / NSLOT) & 1)) {
             fail(ERR_WAIT_EMPTY);
             break;
           }
           tc_fence_after();
           const uint64_t ad = smem_desc(st_a(s) + blk * (TM * 32), 128, 256);
           const uint64_t bd = smem_desc(st_b(s) + blk * (NS * 32), 128, 256);
-          tc_mma_i8(tbase + (uint32_t)(slot * NS), ad, bd, idesc, 0u);
+          tc_mma_i8(tbase + (uint32_t)(slot * NS), ad, bd, idesc, 1u);  // onto the preset cells
           tc_commit(&mdone[slot]);
           issued = b + 1;
         }
@@ -236,11 +239,23 @@ __global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Para
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int r = tid;  // warps 0-3: TMEM lanes 0-127 = weight rows
-    float acc[NS];
+    constexpr int NH = NS / 2;  // tokens of this warp
+    const int q = warp & 3, half = warp >> 2;
+    const int r = q * 32 + lane;  // TMEM lane = weight row
+    const int n0 = half * NH;
+    float acc[NH];
 #pragma unroll
-    for (int i = 0; i < NS; i++) acc[i] = 0.0f;
-    const uint32_t lane_base = tbase + ((uint32_t)(warp * 32) << 16);
+    for (int i = 0; i < NH; i++) acc[i] = 0.0f;
+    const uint32_t lane_base = tbase + ((uint32_t)(q * 32) << 16);
+    auto preset_slot = [&](int slot) {
+#pragma unroll
+      for (int c = 0; c < NH; c += 8) tc_st8_fill(lane_base + (uint32_t)(slot * NS + n0 + c), MAGIC_BITS);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tfree[slot]);
+    };
+    for (int k = 0; k < NSLOT; k++) preset_slot(k);
     for (int st = 0; st < nstages && !abort_flag; st++) {
       const int s = st % NST, u = st / NST;
       if (!mbar_wait(&full[s], u & 1) || !mbar_wait(&aready[s], u & 1)) {
@@ -259,40 +274,33 @@ __global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Para
           break;
         }
         tc_fence_after();
+        // Each cell holds the bits of 1.5 * 2^23 + acc (|acc| < 2^22).
+        uint32_t v[NH];
+#pragma unroll
+        for (int c = 0; c < NH; c += 8) tc_ld8(lane_base + (uint32_t)(slot * NS + n0 + c), v + c);
+        tc_wait_ld_regs<NH>(v);
+        preset_slot(slot);  // values in registers: the slot goes back to the MMA issuer
         const float d = dw[blk * TM + r];
         const float negmd = -MAGIC_F * d;  // exact: d has <= 11 significant bits
         const bool fin = isfinite(d);
-        const float* dxb = dx + blk * NS;
+        const float* dxb = dx + blk * NS + n0;
 #pragma unroll
-        for (int c0 = 0; c0 < NS; c0 += 16) {
-          uint32_t v[16];
-          tc_ld16(lane_base + (uint32_t)(slot * NS + c0), v);
-          tc_wait_ld();
-          if (c0 + 16 >= NS) {
-            // Slot drained: hand it back to the MMA issuer.
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tfree[slot]);
+        for (int j = 0; j < NH; j += 2) {
+          // (acc as f32 * d_w) * d_x, then sum += term (kernels.rs:79).
+          // M + acc is exact, and fma(M + acc, d, -M*d) rounds acc*d once,
+          // exactly like the reference's multiply.
+          float2 t1;
+          if (fin) {
+            t1 = __ffma2_rn(make_float2(__uint_as_float(v[j]), __uint_as_float(v[j + 1])), make_float2(d, d),
+                            make_float2(negmd, negmd));
+          } else {
+            t1 = make_float2(__fmul_rn(i2f((int)(v[j] - MAGIC_BITS)), d), __fmul_rn(i2f((int)(v[j + 1] - MAGIC_BITS)), d));
           }
-#pragma unroll
-          for (int j = 0; j < 16; j += 2) {
-            // (acc as f32 * d_w) * d_x, then sum += term (kernels.rs:79).
-            // M + acc is exact (|acc| < 2^22), and fma(M + acc, d, -M*d)
-            // rounds acc*d once, exactly like the reference's multiply.
-            float2 t1;
-            const float fa = __uint_as_float(v[j] + MAGIC_BITS), fb = __uint_as_float(v[j + 1] + MAGIC_BITS);
-            if (fin) {
-              t1 = __ffma2_rn(make_float2(fa, fb), make_float2(d, d), make_float2(negmd, negmd));
-            } else {
-              t1 = make_float2(__fmul_rn(i2f((int)v[j]), d), __fmul_rn(i2f((int)v[j + 1]), d));
-            }
-            // The product and the sum stay two roundings: the packed
-            // __fmul2_rn/__fadd2_rn pair is contracted into one FFMA2 by the
-            // compiler, the scalar _rn intrinsics never are.
-            const float2 x2 = *reinterpret_cast<const float2*>(dxb + c0 + j);
-            acc[c0 + j] = __fadd_rn(acc[c0 + j], __fmul_rn(t1.x, x2.x));
-            acc[c0 + j + 1] = __fadd_rn(acc[c0 + j + 1], __fmul_rn(t1.y, x2.y));
-          }
+          // The product and the sum stay two roundings (scalar _rn operations,
+          // never contracted; a packed multiply feeding a packed add would be).
+          const float2 x2 = *reinterpret_cast<const float2*>(dxb + j);
+          acc[j] = __fadd_rn(acc[j], __fmul_rn(t1.x, x2.x));
+          acc[j + 1] = __fadd_rn(acc[j + 1], __fmul_rn(t1.y, x2.y));
         }
       }
       if (bad) break;
@@ -302,8 +310,8 @@ __global__ void __launch_bounds__(NTHR, 1) k_mma_q8(const __grid_constant__ Para
     if (!abort_flag && r < nrows) {
       const int row = row0 + r;
 #pragma unroll
-      for (int n = 0; n < NS; n++) {
-        const int tok = tg * NS + n;
+      for (int n = 0; n < NH; n++) {
+        const int tok = tg * NS + n0 + n;
         if (tok >= p.nt) break;
         float sv = acc[n];
         if (p.epi == EPI_RESID) {
