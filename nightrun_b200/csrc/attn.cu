@@ -157,8 +157,15 @@ NRC_DEV void cp_async_wait() {
 // four CTAs resident per SM when many (token, head) CTAs run.
 template <bool FAST, int HD>
 __global__ void __launch_bounds__(ATT_THREADS, HD >= 128 ? 3 : 4) k_attention(const AttnArgs a) {
-  pdl_wait();
-  pdl_trigger();
+  const bool fused = a.fused != 0;
+  // Single-token decode with the KV append fused: the position and the cached
+  // rows [0, pos) were final before the previous attention (or embedding)
+  // kernel returned from its own dependency wait, and every kernel between
+  // them lets its dependents start only once it is running, so they are read
+  // before this kernel's wait, overlapping the QKV launch's tail. Everything
+  // the previous kernel writes (q, k, v; rows appended by a separate kernel)
+  // is read after it.
+  if (!fused) pdl_wait();
   const int h = blockIdx.x, tok = blockIdx.y;
   const int hd = a.head_dim, half = hd / 2;
   const int gqa = a.n_heads / a.n_kv_heads;
@@ -166,7 +173,6 @@ __global__ void __launch_bounds__(ATT_THREADS, HD >= 128 ? 3 : 4) k_attention(co
   const int att_dim = a.n_heads * hd, kv_dim = a.n_kv_heads * hd;
   const uint32_t pos = a.pos_tok ? a.pos_tok[tok] : a.pos_dev[0] + (uint32_t)tok;
   const int npos = (int)pos + 1;
-  const bool fused = a.fused != 0;
   const size_t cache_off = a.pos_tok ? (size_t)a.seq_tok[tok] * a.seq_stride : 0;
   extern __shared__ __align__(16) float sm[];
   float* qs = sm;                                               // [hd]
@@ -204,6 +210,8 @@ __global__ void __launch_bounds__(ATT_THREADS, HD >= 128 ? 3 : 4) k_attention(co
 #pragma unroll
     for (int c = 0; c < HD / 8; c++) k0[c] = kr[c];
   }
+  if (fused) pdl_wait();
+  pdl_trigger();
   if (fused) {
     const float* ct = a.cos_tab + (size_t)pos * half;
     const float* st = a.sin_tab + (size_t)pos * half;
