@@ -195,7 +195,8 @@ def synth_q8_weights(torch, rows, cols, seed):
 
 def gemv_roofline(torch, rows, cols, reps, stream):
     """Standalone Q8_0 GEMV (one token) on an in-step shape: algorithmic bytes
-    per launch and the average launch time (CUDA events on the launching stream)."""
+    per launch and the average launch time (CUDA events on the launching
+    stream around a graph of `reps` launches)."""
     from nightrun_b200 import kernels
     w = synth_q8_weights(torch, rows, cols, rows + cols)
     x = torch.randn(cols, device="cuda")
@@ -204,13 +205,30 @@ def gemv_roofline(torch, rows, cols, reps, stream):
     kernels.quantize(x, xq, stream=stream)
     # Rotate over copies larger than L2 (126 MB) so every launch streams from HBM.
     copies = [w] + [w.clone() for _ in range(max(0, (160 << 20) // w.numel()))]
+    def launches():
+        for i in range(reps):
+            kernels.matvec_q8(y, copies[i % len(copies)], xq, rows, cols, stream=stream)
+
     for i in range(3):
         kernels.matvec_q8(y, copies[i % len(copies)], xq, rows, cols, stream=stream)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    # Replayed as one CUDA graph, so the events time the launches on the GPU,
+    # not the host's per-call work (tensor-map encoding, launch).
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
+            launches()
+
+        def replay():
+            with torch.cuda.stream(stream):
+                g.replay()
+    except Exception:  # capture unavailable: time the eager launches
+        replay = launches
+    replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
-    for i in range(reps):
-        kernels.matvec_q8(y, copies[i % len(copies)], xq, rows, cols, stream=stream)
+    replay()
     ev1.record(stream)
     ev1.synchronize()
     kernels.sync_check(stream)

@@ -5,7 +5,9 @@ matvec/matmul entry points on device-resident random weights.
     python -m nightrun_b200.bench_gemv --fmt q8_0 --rows 128256 --cols 2048 --n 1 --reps 3
 
 Algorithmic bytes per launch = packed weight bytes + activation blocks + f32 outputs.
-Consecutive launches use different weight copies (more than L2 together).
+Consecutive launches use different weight copies (more than L2 together); the
+timed launches are replayed as one CUDA graph, so CUDA events measure the GPU
+rather than the host's per-call work.
 """
 import argparse
 import json
@@ -45,20 +47,40 @@ def run(fmt, rows, cols, n, reps, stream):
     # Rotate over weight copies larger than L2 (126 MB) together, so every
     # launch streams its weights from HBM.
     copies = [w] + [w.clone() for _ in range(max(0, (160 << 20) // w.numel()))]
+    def launches():
+        for i in range(reps):
+            fn(y, copies[i % len(copies)], xq, rows, cols, n, stream=stream)
+
     for i in range(3):
         fn(y, copies[i % len(copies)], xq, rows, cols, n, stream=stream)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    # The timed launches as one CUDA graph: the events then measure the GPU,
+    # not the host's per-call work (scratch allocation, tensor-map encoding,
+    # two launches), which for the small shapes takes longer than the kernels.
+    timing = "graph"
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream, capture_error_mode="relaxed"):
+            launches()
+
+        def replay():
+            with torch.cuda.stream(stream):
+                g.replay()
+    except Exception:  # capture unavailable: time the eager launches
+        timing = "eager"
+        replay = launches
+    replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for i in range(reps):
-        fn(y, copies[i % len(copies)], xq, rows, cols, n, stream=stream)
+    replay()
     e1.record(stream)
     e1.synchronize()
     kernels.sync_check(stream)
     us = e0.elapsed_time(e1) * 1000.0 / reps
     nbytes = w.numel() + xq.numel() + y.numel() * 4
     return {"fmt": fmt, "rows": rows, "cols": cols, "n": n, "us": us, "bytes": nbytes,
-            "gbs": nbytes / us / 1e3, "int8_tops": 2.0 * rows * cols * n / us / 1e6}
+            "gbs": nbytes / us / 1e3, "int8_tops": 2.0 * rows * cols * n / us / 1e6, "timing": timing}
 
 
 def main():
