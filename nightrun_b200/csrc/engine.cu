@@ -550,8 +550,9 @@ Layout layout_for(const nrc_meta& mt, size_t ctx, size_t n_seqs = 1, bool batch 
   L.mxd = take(BM * (maxk / 32) * 4);  // and their block scales
   L.mxb = take(BM * (maxk / 256) * 8 * 4);  // and the chunk sums of the K-quant tiles
   // Quantized attention-norm activations shared by the QKV launches of one layer
-  // (8 tokens of Q8_0 or Q8_K blocks).
-  L.xsh = take(8 * std::max(dim / 32 * 34, dim / 256 * 292 + 292));
+  // (8 tokens of Q8_0 or Q8_K blocks); in a decode step, after QKV, the
+  // attention output as Q8_0 blocks for the output projection.
+  L.xsh = take(8 * std::max(std::max(dim, att) / 32 * 34, dim / 256 * 292 + 292));
   L.status = take(sizeof(Status));
   L.hist = take((ctx + 1) * 4);
   L.samp = take(sample_scratch_bytes((int)mt.vocab));  // sampler candidates
@@ -1165,6 +1166,8 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
       aa.cos_tab = c->cos_t;
       aa.sin_tab = c->sin_t;
       aa.style = c->style;
+      // A Q8_0 output projection takes the attention output already quantized.
+      if (w.fo == FMT_Q8_0 && !tp) aa.xq_out = c->xsh;
     } else {
       RopeArgs ra{c->q, c->k, c->v, w.q_norm, w.k_norm, c->eps, c->cos_t, c->sin_t, c->style, kc_l, vc_l,
                   nt, sh.nh, sh.nkv, hd, (int)c->ctx, &c->st->pos};
@@ -1182,6 +1185,7 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
       L.fmt = w.fo;
       L.K = c->att_dim;
       L.x = c->att;
+      L.xq = aa.xq_out;  // quantized by the attention kernel (fused decode, Q8_0), else null
       L.w[0] = wo;
       L.y[0] = c->tp_send;
       L.rows[0] = sh.dn;

@@ -44,6 +44,9 @@ struct RopeArgs {
   const uint32_t* pos_tok;
   const uint32_t* seq_tok;
   size_t seq_stride;
+  // Fused decode only: the output also as Q8_0 blocks (q8::quantize, q8.rs:
+  // 27-44), the next projection's input, or null.
+  uint8_t* xq_out;
 };
 cudaError_t rope_append_run(const RopeArgs& a, cudaStream_t s, bool pdl);
 
@@ -71,6 +74,9 @@ struct AttnArgs {
   const uint32_t* pos_tok;
   const uint32_t* seq_tok;
   size_t seq_stride;
+  // Fused decode only: the output also as Q8_0 blocks (q8::quantize, q8.rs:
+  // 27-44), the next projection's input, or null.
+  uint8_t* xq_out;
 };
 // Shared memory of one attention CTA (its score rows hold `ctx` positions);
 // contexts needing more than ATTN_MAX_SMEM are rejected at context creation.
