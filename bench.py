@@ -238,23 +238,30 @@ def gemv_roofline(torch, rows, cols, reps, stream):
     return nbytes, ms
 
 
-def decode_rate(torch, model, steps, mode, ctx_len=256, prompt=PROMPT):
-    """Device-resident greedy decode tokens/s of one context (graph replays)."""
+def decode_rate(torch, model, steps, mode, ctx_len=256, prompt=PROMPT, tp=None, reduce_ms=None, barrier=None):
+    """Device-resident greedy decode tokens/s of one context (graph replays);
+    with `tp` a tensor-parallel context on every rank, timed as the slowest
+    rank (`reduce_ms`) after a barrier."""
     cfg_vocab = model.meta.vocab
-    c = model.ctx(ctx_len)
+    c = model.ctx(ctx_len, tp=tp)
     c.set_mode(mode)
     stream = torch.cuda.ExternalStream(c.stream_handle())
     c.prefill(np.array(prompt_ids(prompt, cfg_vocab), np.uint32))
     c.decode_async(3)
     c.sync()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if barrier:
+        barrier()
     torch.cuda.synchronize()
     e0.record(stream)
     c.decode_async(steps)
     e1.record(stream)
     c.sync()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    ms = e0.elapsed_time(e1)
+    if reduce_ms:
+        ms = reduce_ms(ms)
+    ms /= steps
     c.close()
     return 1000.0 / ms, ms
 
@@ -473,6 +480,16 @@ def run_ours(args, rank, world, local_rank):
         res["parallelism"] = f"dp{world} ({per} sequences per GPU)"
         res["scaling"] = "strong"
         line["config4_dp"] = res
+        # Config 2 tensor parallel (one sequence over NCCL all-gathers), exact mode.
+        cfg2 = CONFIGS["llama3b_q4km"]
+        m2 = Model.synth(cfg2, MODEL_SEED, device=local_rank)
+        uid2 = [NB.tp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid2, src=0)
+        tps2, ms2 = decode_rate(torch, m2, 24, 0, tp=(world, rank, uid2[0]), reduce_ms=max_over_ranks,
+                                barrier=barrier)
+        line["config2_tp"] = {"model": "llama3b_q4km", "decode_tokens_per_s": tps2, "ms_per_token": ms2,
+                              "parallelism": f"tp{world}", "scaling": "strong"}
+        m2.close()
     line["clocks"] = sampler.stop()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         blob = model.export()
