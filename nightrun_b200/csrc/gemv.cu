@@ -44,10 +44,10 @@
 namespace nrc {
 namespace {
 
-constexpr int NCW = 8;             // consumer warps
+constexpr int NCW = 12;            // consumer warps (a stage's units are latency-bound: more warps, more stages in flight)
 constexpr int NC = NCW * 32;       // consumer threads
 constexpr int NTHREADS = NC + 32;  // + producer warp
-constexpr int MAX_STAGES = 16;
+constexpr int MAX_STAGES = 24;
 constexpr int SMEM_RESERVE = 1024;  // static shared memory of the kernel, rounded up
 
 struct Params {
