@@ -4,7 +4,7 @@
 // Reference: crates/nr-tensor/src/kernels.rs:36-143 (Q8_0) and
 // crates/nr-tensor/src/kquant.rs:192-250, 536-639 (Q4_K / Q6_K).
 //
-// Structure (persistent, one CTA per SM, 8 consumer warps + 1 producer warp):
+// Structure (persistent, one CTA per SM, 12 consumer warps + 1 producer warp):
 //  * a tile is R consecutive weight rows (whole rows; gate and up are two
 //    spans of one tile in the SwiGLU pair), i.e. one or two contiguous byte
 //    ranges. The producer warp copies each tile HBM -> shared memory with one
