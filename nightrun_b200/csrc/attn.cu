@@ -155,27 +155,6 @@ NRC_DEV void cp_async_wait() {
 // HD: head_dim as a constant (32, 64 or 128), so a thread's K row lives in
 // HD / 8 registers of 16 bytes; the register bound keeps three (HD 128) or
 // four CTAs resident per SM when many (token, head) CTAs run.
-// q8::quantize (q8.rs:27-44) of one 32-value block held one value per lane
-// of a full warp: d = f16(amax / 127) (amax folded from 0, NaN ignored like
-// f32::max), q = v / d rounded half away from zero, saturated to +-127.
-NRC_DEV void warp_quant_q8_block(float v, int lane, uint8_t* blk) {
-  float amax = fmaxf(0.0f, fabsf(v));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const uint16_t dbits = f32_to_f16(__fdiv_rn(amax, 127.0f));
-  const float d = f16_to_f32(dbits);
-  const float inv = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
-  const float xsv = __fmul_rn(v, inv);
-  const float r = xsv >= 0.0f ? __fadd_rn(xsv, 0.5f) : __fsub_rn(xsv, 0.5f);
-  int q = rust_f2i(r);
-  q = q < -127 ? -127 : (q > 127 ? 127 : q);
-  blk[2 + lane] = (uint8_t)(int8_t)q;
-  if (lane == 0) {
-    blk[0] = (uint8_t)(dbits & 0xffu);
-    blk[1] = (uint8_t)(dbits >> 8);
-  }
-}
-
 template <bool FAST, int HD>
 __global__ void __launch_bounds__(ATT_THREADS, HD >= 128 ? 3 : 4) k_attention(const AttnArgs a) {
   const bool fused = a.fused != 0;

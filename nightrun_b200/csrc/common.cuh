@@ -109,6 +109,27 @@ NRC_DEV int32_t rust_f2i(float f) { return __float2int_rz(f); }
 // Exact int -> float for |v| < 2^24 is cvt.rn; used where the reference casts.
 NRC_DEV float i2f(int32_t v) { return __int2float_rn(v); }
 
+// q8::quantize (q8.rs:27-44) of one 32-value block held one value per lane
+// of a full warp: d = f16(amax / 127) (amax folded from 0, NaN ignored like
+// f32::max), q = v / d rounded half away from zero, saturated to +-127.
+NRC_DEV void warp_quant_q8_block(float v, int lane, uint8_t* blk) {
+  float amax = fmaxf(0.0f, fabsf(v));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const uint16_t dbits = f32_to_f16(__fdiv_rn(amax, 127.0f));
+  const float d = f16_to_f32(dbits);
+  const float inv = d > 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+  const float xsv = __fmul_rn(v, inv);
+  const float r = xsv >= 0.0f ? __fadd_rn(xsv, 0.5f) : __fsub_rn(xsv, 0.5f);
+  int q = rust_f2i(r);
+  q = q < -127 ? -127 : (q > 127 ? 127 : q);
+  blk[2 + lane] = (uint8_t)(int8_t)q;
+  if (lane == 0) {
+    blk[0] = (uint8_t)(dbits & 0xffu);
+    blk[1] = (uint8_t)(dbits >> 8);
+  }
+}
+
 // ------------------------------------------------------------ misc device
 NRC_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

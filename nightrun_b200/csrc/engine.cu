@@ -549,10 +549,12 @@ Layout layout_for(const nrc_meta& mt, size_t ctx, size_t n_seqs = 1, bool batch 
   L.mxq = take(BM * maxk * 2);        // tensor-core activation tiles (x 2: the Q6_K masked halves)
   L.mxd = take(BM * (maxk / 32) * 4);  // and their block scales
   L.mxb = take(BM * (maxk / 256) * 8 * 4);  // and the chunk sums of the K-quant tiles
-  // Quantized attention-norm activations shared by the QKV launches of one layer
-  // (8 tokens of Q8_0 or Q8_K blocks); in a decode step, after QKV, the
-  // attention output as Q8_0 blocks for the output projection.
-  L.xsh = take(8 * std::max(std::max(dim, att) / 32 * 34, dim / 256 * 292 + 292));
+  // Quantized activations of up to 8 tokens handed from one kernel to the
+  // next: the attention-norm input shared by the QKV launches of one layer
+  // (Q8_0 or Q8_K blocks), the attention output for the output projection and
+  // the SwiGLU output for the down projection (Q8_0 blocks).
+  const size_t q8_max = std::max(std::max(dim, att), (size_t)mt.ffn_dim) / 32 * 34;
+  L.xsh = take(8 * std::max(q8_max, dim / 256 * 292 + 292));
   L.status = take(sizeof(Status));
   L.hist = take((ctx + 1) * 4);
   L.samp = take(sample_scratch_bytes((int)mt.vocab));  // sampler candidates
@@ -873,6 +875,7 @@ cudaError_t gemv_tokens(GemvArgs a, int nt, int x_ld_f, cudaStream_t s, bool pdl
       b.xq = static_cast<const uint8_t*>(a.xq) + (size_t)t0 * blk;
     }
     if (t0 > 0) b.xq_out = nullptr;  // the sharing serves one group of at most 8 tokens
+    if (nt > 8) b.yq_out = nullptr;  // and so does the SwiGLU output export
     for (int i = 0; i < b.nseg; i++)
       if (b.seg[i].y) b.seg[i].y = a.seg[i].y + (size_t)t0 * a.seg[i].ld;
     if (b.resid) b.resid = a.resid + (size_t)t0 * a.resid_ld;
@@ -913,6 +916,10 @@ struct Lin {
   // already quantized (xq, then x / norm_w are not read).
   uint8_t* xq_out = nullptr;
   const uint8_t* xq = nullptr;
+  // EPI_SWIGLU on the streaming GEMV: also store the output as Q8_0 blocks in
+  // yq_out when the launch can; *yq_done (set to 0 or 1) says whether it did.
+  uint8_t* yq_out = nullptr;
+  int* yq_done = nullptr;
   // Weights of the next linear layer, prefetched into L2 while this one runs.
   const uint8_t* pf;
   size_t pf_bytes;
@@ -1008,6 +1015,8 @@ cudaError_t linear(nrc_ctx* c, const Lin& L, int nt) {
   if (L.epi == EPI_SWIGLU) {
     a.pair = 1;
     a.seg[1].y = nullptr;
+    a.yq_out = L.yq_out;
+    a.yq_done = L.yq_done;
   }
   if (L.epi == EPI_RESID) {
     a.resid = c->x;
@@ -1196,6 +1205,7 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
       if ((e = linear(c, L, nt))) return e;
       if (tp && (e = tp_gather(c, c->x, c->dim, sh.dn, nt, 1))) return e;
     }
+    int h_quantized = 0;  // the SwiGLU output also left in xsh as Q8_0 blocks
     {  // SwiGLU MLP gate/up (infer.rs:577-581)
       float* g = tp ? c->tp_send : c->g;
       Lin L{};
@@ -1216,6 +1226,10 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
         L.rows[1] = sh.fn;
         L.nseg = 2;
         L.epi = EPI_SWIGLU;
+        if (w.fd == FMT_Q8_0 && !tp) {  // a Q8_0 down projection takes it quantized
+          L.yq_out = c->xsh;
+          L.yq_done = &h_quantized;
+        }
         if ((e = linear(c, L, nt))) return e;
       } else {
         if ((e = linear(c, L, nt))) return e;
@@ -1232,6 +1246,7 @@ cudaError_t enqueue_step(nrc_ctx* c, int nt, bool draw, const Pass* bp = nullptr
       L.fmt = w.fd;
       L.K = c->ffn;
       L.x = c->g;
+      L.xq = h_quantized ? c->xsh : nullptr;
       L.w[0] = wd;
       L.y[0] = c->tp_send;
       L.rows[0] = sh.dn;

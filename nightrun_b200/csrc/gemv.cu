@@ -69,6 +69,7 @@ struct Params {
   int ncw;          // consumer warps that own tiles (the others only help with the prologue)
   const uint8_t* xq;
   uint8_t* xq_out;
+  uint8_t* yq_out;  // EPI_SWIGLU output as Q8_0 blocks (lane-per-row kernel, 32-row groups), or null
   const float* xf;
   int xf_ld;
   const float* norm_w;
@@ -790,6 +791,7 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
       int seg, row0;
       lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
       const int row = row0 + lane;
+      float hv[NT] = {};
       if (lane < lp.rg && row < p.rows[seg]) {
 #pragma unroll
         for (int t = 0; t < NT; t++) {
@@ -797,7 +799,8 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
           if (p.epi == EPI_SWIGLU) {
             // vec::swiglu: silu = x / (1 + expf(-x)); gate = silu * up
             const float silu = __fdiv_rn(acc[t], __fadd_rn(1.0f, expf_cr(-acc[t])));
-            p.y[0][(size_t)t * p.ld[0] + row] = __fmul_rn(silu, accu[t]);
+            hv[t] = __fmul_rn(silu, accu[t]);
+            p.y[0][(size_t)t * p.ld[0] + row] = hv[t];
           } else if (p.epi == EPI_RESID) {
             float* dst = p.resid + (size_t)t * p.resid_ld + row;
             *dst = __fadd_rn(*dst, __fmul_rn(p.rs, acc[t]));
@@ -810,6 +813,15 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
               best = key > best ? key : best;
             }
           }
+        }
+      }
+      if (p.yq_out) {
+        // The host sets yq_out only for 32-row groups of a row count that is a
+        // multiple of 32: every lane holds one row, row0 starts a block.
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+          if (NT > 1 && t >= p.nt) break;
+          warp_quant_q8_block(hv[t], lane, p.yq_out + ((size_t)t * (p.rows[0] / 32) + row0 / 32) * Q8_0_BYTES);
         }
       }
     }
@@ -1037,6 +1049,10 @@ bool gemv_lr_try(const GemvArgs& a, const Params& base, int NTc, int xmode, cuda
       return true;
     }
   lp.ngroups = ng;
+  if (a.yq_out && a.pair && a.epi == EPI_SWIGLU && lp.rg == 32 && a.seg[0].rows % 32 == 0) {
+    p.yq_out = a.yq_out;
+    if (a.yq_done) *a.yq_done = 1;
+  }
   lp.off_tr = (int)off_tr;
   lp.off_bar = (int)off_bar;
   p.nstage = LR_CW;
@@ -1070,6 +1086,7 @@ cudaError_t gemv_run(const GemvArgs& a, cudaStream_t stream, bool pdl) {
   const int bbytes = a.fmt == FMT_Q8_0 ? Q8_0_BYTES : (a.fmt == FMT_Q4K ? Q4K_BYTES : Q6K_BYTES);
   if (a.K <= 0 || a.K % blk || a.nt < 1 || a.nt > 8 || a.nseg < 1 || a.nseg > 3) return cudaErrorInvalidValue;
   if (a.pair && (a.nseg != 2 || a.seg[0].rows != a.seg[1].rows)) return cudaErrorInvalidValue;
+  if (a.yq_done) *a.yq_done = 0;
   p.K = a.K;
   p.bpr = a.K / blk;
   p.row_bytes = p.bpr * bbytes;

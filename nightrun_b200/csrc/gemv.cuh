@@ -38,6 +38,11 @@ struct GemvArgs {
   // slot), so a following launch over other weights of the same input takes
   // them as xq instead of normalizing and quantizing again.
   void* xq_out;
+  // EPI_SWIGLU: also store silu(gate) * up as Q8_0 blocks [nt][rows / 32] (the
+  // down projection's activations, quantized once) when one warp of the launch
+  // forms each 32-row block; gemv_run sets *yq_done to 1 when it does, else 0.
+  uint8_t* yq_out;
+  int* yq_done;
   const float* norm_w;
   float eps;
   int fast_norm;  // tolerance mode: the RMSNorm sum of squares as a tree (not the reference's chain)
