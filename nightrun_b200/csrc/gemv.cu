@@ -731,9 +731,10 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
     // ------------------------------------------------------- chain warps
     // Chain warp c takes the CTA's row groups c, c + LR_NCH, ...: each group's
     // stages in order (so every row's terms are added in block order), CB
-    // stages per flag round. Hand-offs: acquire flags in, mbarriers out.
+    // stages (64 terms per lane) per flag round. Hand-offs: acquire flags in,
+    // mbarriers out.
     const int c = warp - LR_CW;
-    constexpr int CB = NT * OPS >= 4 ? 1 : 4 / (NT * OPS);
+    constexpr int CB = NT * OPS >= 8 ? 1 : 8 / (NT * OPS);
     // Sleep through the consumers' prologue (no polling beside its chain).
     named_sync(2, (LR_CW + LR_NCH) * 32);
     unsigned long long best = 0ull;
