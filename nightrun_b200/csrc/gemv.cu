@@ -737,12 +737,30 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
     constexpr int CB = NT * OPS >= 8 ? 1 : 8 / (NT * OPS);
     // Sleep through the consumers' prologue (no polling beside its chain).
     named_sync(2, (LR_CW + LR_NCH) * 32);
+    // The SwiGLU epilogue's expf table, brought into L1 while the sums run.
+    if (p.epi == EPI_SWIGLU && lane < (int)(sizeof(EXPCR_T_DEV) / 128))
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(__cvta_generic_to_global(EXPCR_T_DEV) + (size_t)lane * 128));
     unsigned long long best = 0ull;
     bool stop = false;
     for (int gl = c; gl < my_groups && !stop; gl += LR_NCH) {
       float acc[NT], accu[NT];
 #pragma unroll
       for (int t = 0; t < NT; t++) acc[t] = accu[t] = 0.0f;
+      int seg, row0;
+      lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
+      const int row = row0 + lane;
+      const bool own = lane < lp.rg && row < p.rows[seg];
+      // Residual epilogue: the lane's residual values are final (every earlier
+      // launch completed before the consumers' dependency wait, and only this
+      // lane writes them), so they are read now, off the end of the chain.
+      float rold[NT];
+#pragma unroll
+      for (int t = 0; t < NT; t++) rold[t] = 0.0f;
+      if (p.epi == EPI_RESID && own) {
+#pragma unroll
+        for (int t = 0; t < NT; t++)
+          if (NT == 1 || t < p.nt) rold[t] = p.resid[(size_t)t * p.resid_ld + row];
+      }
       for (int q0 = 0; q0 < spg; q0 += CB) {
         const int i0 = gl * spg + q0;
         const int nb = spg - q0 < CB ? spg - q0 : CB;
@@ -789,11 +807,8 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
         }
       }
       if (stop) break;
-      int seg, row0;
-      lr_group(lp, (int)blockIdx.x + gl * (int)gridDim.x, seg, row0);
-      const int row = row0 + lane;
       float hv[NT] = {};
-      if (lane < lp.rg && row < p.rows[seg]) {
+      if (own) {
 #pragma unroll
         for (int t = 0; t < NT; t++) {
           if (NT > 1 && t >= p.nt) break;
@@ -803,8 +818,7 @@ __global__ void __launch_bounds__(LR_THREADS, 1) gemv_lr_kernel(const __grid_con
             hv[t] = __fmul_rn(silu, accu[t]);
             p.y[0][(size_t)t * p.ld[0] + row] = hv[t];
           } else if (p.epi == EPI_RESID) {
-            float* dst = p.resid + (size_t)t * p.resid_ld + row;
-            *dst = __fadd_rn(*dst, __fmul_rn(p.rs, acc[t]));
+            p.resid[(size_t)t * p.resid_ld + row] = __fadd_rn(rold[t], __fmul_rn(p.rs, acc[t]));
           } else {
             float sv = acc[t];
             if (p.scale != 1.0f) sv = __fmul_rn(sv, p.scale);
